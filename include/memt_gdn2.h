@@ -1,0 +1,227 @@
+/*
+ * memt_gdn2.h — C ABI of the B200 (sm_100a) GDN-2 memory hot path.
+ *
+ * The functions below replace the operator layer of the MemT-1.0 SGLang plugin
+ * (package inference/memt_sglang of the reference). Paths in the comments are
+ * relative to that package:
+ *
+ *   token_memory_packed   models/qwen/ops/packed.py:34-81, models/deepseek/ops/packed.py:70-108
+ *                         = memt_gdn2_update (write path) + memt_gdn2_read (read of the incoming
+ *                           snapshot)
+ *   memt_gdn2_fwd_h and the intra-chunk WY kernels it consumes
+ *                         models/qwen/ops/_triton/state.py:127-174, _vendor/fla/ops/gdn2/
+ *                         chunk_intra.py:693-787, wy_fast.py:145-196, utils/cumsum.py:446-486
+ *                         = memt_gdn2_update
+ *   memt_gdn2_read_fwd    models/qwen/ops/read.py:10-39  = memt_gdn2_read
+ *   snapshot_read         models/deepseek/ops/read.py:6-31 = memt_gdn2_read
+ *   l2norm(q) + read + MemTRMSNormGated + residual injection
+ *                         models/qwen/layer.py:15-31,112-131, models/qwen/integration.py:61-64
+ *                         = memt_memory_readout
+ *   packed_plan / build_chunk_plan (write events + 64-token tiles)
+ *                         models/qwen/ops/packed.py:16-31, models/qwen/ops/layout.py:128-189
+ *                         = built on the device inside memt_gdn2_update;
+ *                           memt_gdn2_count_chunks gives the host the same count
+ *
+ * Conventions
+ *   - All tensor pointers are device pointers to contiguous row-major arrays.
+ *     Token-major activations are [L, H, D] (the reference's [1, L, H, D] without
+ *     the leading 1). States are fp32 [N, H, K, V], V fastest, the reference's pool
+ *     layout (runtime/state.py:47-51).
+ *   - Samples are given by cu_seqlens (int32 device array of N+1 offsets), the
+ *     reference's boundaries(lengths) (models/common/packed.py:8-9).
+ *   - Every entry point is asynchronous on the given stream, never synchronises the
+ *     host, allocates nothing (scratch comes from the caller's workspace) and returns a
+ *     status. Arguments are checked on the host before any launch; a bad argument
+ *     returns a negative status and launches nothing (the reference raises ValueError
+ *     before launch: models/common/packed.py:12-34).
+ *   - Device-side data that the host cannot see without a sync (cu_seqlens contents)
+ *     is clamped on the device so that every access stays in bounds; the plan kernel
+ *     records the problem in the workspace status word (memt_gdn2_workspace_status).
+ */
+#ifndef MEMT_GDN2_H
+#define MEMT_GDN2_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* cudaStream_t without including the CUDA headers. */
+typedef struct CUstream_st *memt_stream_t;
+
+/* ---- status codes ---------------------------------------------------- */
+#define MEMT_OK 0
+#define MEMT_ERR_INVALID_ARGUMENT (-1) /* null pointer, bad count, bad enum value      */
+#define MEMT_ERR_UNSUPPORTED (-2)      /* head dim / dtype combination not compiled   */
+#define MEMT_ERR_MISALIGNED (-3)       /* pointer not 16-byte aligned                 */
+#define MEMT_ERR_WORKSPACE (-4)        /* workspace null or smaller than required     */
+#define MEMT_ERR_CUDA (-5)             /* a CUDA launch failed; see memt_last_cuda_error */
+
+/* ---- element types ---------------------------------------------------- */
+#define MEMT_F32 0
+#define MEMT_BF16 1
+
+/* ---- gate layouts ------------------------------------------------------
+ * NONE:        gate absent (log-decay 0 / factor 1)
+ * PER_HEAD:    one value per (token, head): [L, H]          (BASELINE's g, beta)
+ * PER_CHANNEL: one value per (token, head, channel): [L, H, D] (the reference's layout)
+ */
+#define MEMT_GATE_NONE 0
+#define MEMT_GATE_PER_HEAD 1
+#define MEMT_GATE_PER_CHANNEL 2
+
+/* Library version (major*10000 + minor*100 + patch). */
+int memt_version(void);
+
+/* Human-readable name of a status code. */
+const char *memt_status_string(int status);
+
+/* The cudaError_t of the last MEMT_ERR_CUDA returned on this thread (0 if none). */
+int memt_last_cuda_error(void);
+
+/* Number of 64-token chunks the update scans for these samples: the reference's
+ * plan.num_chunk (models/qwen/ops/layout.py:142-149). Host array, N+1 entries.
+ * Returns -1 on invalid input (non-monotonic offsets, chunk_tokens < 1). */
+int64_t memt_gdn2_count_chunks(const int32_t *cu_seqlens_host, int32_t num_samples,
+                               int32_t chunk_tokens);
+
+/* ---- GDN-2 chunked update (the writer) ---------------------------------
+ *
+ * Replaces the write half of token_memory_packed: chunk_local_cumsum ->
+ * chunk_gdn2_fwd_intra (token-parallel diagonal, inter-solve, WY recompute) ->
+ * memt_gdn2_fwd_h (models/qwen/ops/packed.py:49-79).
+ *
+ * Per sample, starting from initial_state, for each token t and head h
+ * (a_t = exp(g_t), k'_t = sqrt(beta_t) * k_t, b = erase, w = write):
+ *     S  <- diag(a_t) S
+ *     d  <- w_t*v_t - S^T (b_t*k'_t)
+ *     S  <- S + k'_t d^T
+ * computed with the chunked WY algorithm (64-token chunks). final_state receives S.
+ *
+ * dtype BF16: k, v, beta, erase, write are bf16; the tensor-core path reproduces the
+ *   reference GPU rounding points (bf16 A^-1, u, w, kg; bf16 state and v_new operands;
+ *   tf32 solve). dtype F32: all inputs fp32, exact fp32 token recurrence on CUDA cores.
+ * g is always fp32 natural-log decay (<= 0).
+ * initial_state may alias final_state (in-place update).
+ */
+typedef struct memt_gdn2_update_args {
+  int32_t num_samples;     /* N >= 1                                            */
+  int32_t num_heads;       /* H >= 1                                            */
+  int32_t key_dim;         /* K: 64, 128 or 256                                 */
+  int32_t value_dim;       /* V: equal to K                                     */
+  int64_t total_tokens;    /* L = cu_seqlens[N]                                 */
+  int32_t chunk_tokens;    /* write-event length (reference chunk_tokens), >= 1 */
+  int32_t dtype;           /* MEMT_BF16 or MEMT_F32                             */
+  const int32_t *cu_seqlens; /* device [N+1]                                    */
+  const void *k;           /* [L,H,K] (already L2-normalised)                   */
+  const void *v;           /* [L,H,V]                                           */
+  const float *g;          /* log-decay, layout g_layout (PER_HEAD or PER_CHANNEL) */
+  int32_t g_layout;
+  const void *beta;        /* sqrt(beta) folded into k; NONE / PER_HEAD / PER_CHANNEL */
+  int32_t beta_layout;
+  const void *erase;       /* FLA channel-wise erase factor b; NONE or PER_CHANNEL  */
+  int32_t erase_layout;
+  const void *write;       /* write gate on V; NONE or PER_CHANNEL ([L,H,V])        */
+  int32_t write_layout;
+  const float *initial_state; /* [N,H,K,V] fp32                                  */
+  float *final_state;         /* [N,H,K,V] fp32                                  */
+} memt_gdn2_update_args;
+
+/* Workspace bytes memt_gdn2_update needs for these sizes (0 on invalid sizes). */
+size_t memt_gdn2_update_workspace_size(int32_t num_samples, int64_t total_tokens, int32_t num_heads,
+                                       int32_t key_dim, int32_t value_dim, int32_t chunk_tokens,
+                                       int32_t dtype);
+
+/* Run the update. workspace: device memory of at least the size above, 256-byte aligned. */
+int memt_gdn2_update(const memt_gdn2_update_args *args, void *workspace, size_t workspace_bytes,
+                     memt_stream_t stream);
+
+/* Device status word the last update left in this workspace (0 = clean; bit 0: a sample
+ * had negative length or offsets outside [0, L]; bit 1: chunk table overflow). Reading it
+ * synchronises the stream; intended for tests and debugging. */
+int memt_gdn2_workspace_status(const void *workspace, memt_stream_t stream, int32_t *status_out);
+
+/* ---- snapshot read -----------------------------------------------------
+ *
+ * Replaces memt_gdn2_read_fwd (models/qwen/ops/read.py:10-39, kernel
+ * models/qwen/ops/_triton/read.py:22-71) and snapshot_read
+ * (models/deepseek/ops/read.py:6-31): every token reads the snapshot of its block,
+ *     out[t,h,:] = cast_out( scale * q[t,h,:] . cast_q(states[block(t),h]) )
+ * q_dtype BF16: the state is rounded to bf16 before the product and accumulated in
+ * fp32 (the reference's rounding); F32: exact fp32.
+ */
+typedef struct memt_gdn2_read_args {
+  int32_t num_blocks;      /* number of snapshots / token blocks                */
+  int32_t num_heads;
+  int32_t key_dim;         /* 64, 128, 256                                      */
+  int32_t value_dim;       /* equal to key_dim                                  */
+  int64_t total_tokens;    /* L                                                 */
+  int32_t max_block_tokens;/* host bound on tokens per block (selects the kernel); 0 = L */
+  const int32_t *cu_seqlens; /* device [num_blocks+1]                           */
+  const void *q;           /* [L,H,K]                                           */
+  int32_t q_dtype;         /* MEMT_BF16 or MEMT_F32                             */
+  const float *states;     /* [num_blocks,H,K,V] fp32                           */
+  float scale;
+  void *out;               /* [L,H,V]                                           */
+  int32_t out_dtype;       /* MEMT_BF16 or MEMT_F32                             */
+} memt_gdn2_read_args;
+
+int memt_gdn2_read(const memt_gdn2_read_args *args, memt_stream_t stream);
+
+/* ---- fused memory readout (decode / query path) -----------------------
+ *
+ * One pass over the fp32 state for:
+ *   q_hat = l2norm(q) (optional, FLA l2norm eps)        models/qwen/layer.py:116
+ *   o     = bf16(scale * q_hat . bf16(S))               models/qwen/ops/_triton/read.py:51-71
+ *   y     = bf16(w * bf16(o * rsqrt(mean o^2 + eps))) * L tanh(SiLU(gate)/L)
+ *                                                       models/qwen/layer.py:22-31
+ *   out[t, (head_offset+h)*D + v] = bf16(residual[...] + y)   (or y when residual is NULL)
+ *                                                       models/qwen/integration.py:61-64
+ * All activations bf16. residual may alias out (in-place add into the attention output).
+ */
+typedef struct memt_memory_readout_args {
+  int32_t num_blocks;
+  int32_t num_heads;       /* heads read by this call                           */
+  int32_t head_dim;        /* 64, 128, 256                                      */
+  int64_t total_tokens;
+  int32_t max_block_tokens;/* host bound on tokens per block; 0 = L             */
+  const int32_t *cu_seqlens; /* device [num_blocks+1]                           */
+  const void *q;           /* bf16 [L,H,D]                                      */
+  int32_t normalize_q;     /* 1: apply l2norm to q first                        */
+  float q_eps;             /* l2norm epsilon (1e-6 in the reference)            */
+  const float *states;     /* [num_blocks,H,D,D] fp32                           */
+  float scale;
+  const void *gate;        /* bf16 [L,H,D] output-gate pre-activation           */
+  const void *norm_weight; /* bf16 [D]                                          */
+  float norm_eps;
+  float softcap;           /* L in L*tanh(SiLU(g)/L); <= 0 disables the softcap  */
+  const void *residual;    /* bf16 [L, row_stride] or NULL                      */
+  void *out;               /* bf16 [L, row_stride]                              */
+  int64_t row_stride;      /* elements per token row of residual/out (>= (head_offset+H)*D) */
+  int32_t head_offset;     /* first head column written                         */
+} memt_memory_readout_args;
+
+int memt_memory_readout(const memt_memory_readout_args *args, memt_stream_t stream);
+
+/* ---- kernel timing (benchmarks) ----------------------------------------
+ *
+ * No counterpart in the reference (its kernels are timed from Python). When enabled,
+ * every kernel this library launches is bracketed by CUDA events on its own stream and
+ * its device time is accumulated per kernel family; disabled (the default) it costs
+ * nothing. Families: 0 plan, 1 intra (WY operands), 2 scan, 3 read (GEMV),
+ * 4 read (tensor-core tiles), 5 fp32 recurrence.
+ */
+#define MEMT_PROF_FAMILIES 6
+int memt_profiler_enable(int on);
+int memt_profiler_reset(void);
+/* Synchronises the recorded events, then fills ms[i] (total device milliseconds) and
+ * launches[i] for i < min(n, MEMT_PROF_FAMILIES). */
+int memt_profiler_read(double *ms, int64_t *launches, int n);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MEMT_GDN2_H */

@@ -1,0 +1,211 @@
+// Shared device helpers for the GDN-2 memory kernels (sm_100a).
+//
+// Warp-level tensor-core fragments (mma.sync m16n8k16 bf16 and m16n8k8 tf32),
+// ldmatrix, cp.async, and the rounding helpers that reproduce the reference's
+// bf16 / tf32 cast points.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace memt {
+
+constexpr int kTile = 64;    // tokens per chunk (models/common/constants.py:3)
+constexpr int kSub = 16;     // sub-chunk of the blocked solve (gdn2/chunk_intra.py:710)
+constexpr float kRcpLn2 = 1.4426950216f;  // _vendor/fla/ops/utils/constant.py:10
+
+// ---------------------------------------------------------------------------
+// scalar conversions
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float bf16_round(float x) {
+  return __bfloat162float(__float2bfloat16_rn(x));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ float2 unpack_bf16x2(uint32_t u) {
+  __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162*>(&u);
+  return __bfloat1622float2(v);
+}
+
+// fp32 -> tf32, round to nearest, ties away from zero (what Triton emits for tf32 dots).
+__device__ __forceinline__ uint32_t to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
+__device__ __forceinline__ float fast_exp2(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+// ---------------------------------------------------------------------------
+// tensor-core fragments
+//   A (16 x k, row-major), B (k x 8, "col"), C/D (16 x 8) per the PTX ISA layouts:
+//   g = lane / 4, t = lane % 4;  C: c0 (g, 2t) c1 (g, 2t+1) c2 (g+8, 2t) c3 (g+8, 2t+1)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4],
+                                               const uint32_t (&b)[2]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+// A: a0 (g, t) a1 (g+8, t) a2 (g, t+4) a3 (g+8, t+4);  B: b0 (k=t, n=g) b1 (k=t+4, n=g)
+__device__ __forceinline__ void mma_tf32_1688(float (&d)[4], const uint32_t (&a)[4],
+                                              const uint32_t (&b)[2]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ldmatrix: lane i supplies the address of row (i % 8) of 8x8 matrix (i / 8).
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2_t(uint32_t (&r)[2], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];\n"
+               : "=r"(r[0]), "=r"(r[1])
+               : "r"(addr));
+}
+
+// ---------------------------------------------------------------------------
+// async copies (16 bytes per thread, L2-only)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(smem)), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async16_zfill(void* smem, const void* gmem, bool valid) {
+  int src = valid ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_u32(smem)),
+               "l"(gmem), "r"(src));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
+// ---------------------------------------------------------------------------
+// chunk table entry written by the plan kernel
+// ---------------------------------------------------------------------------
+struct ChunkDesc {
+  int32_t sample;  // owning sample
+  int32_t tok0;    // first packed token
+  int32_t len;     // 1..64 valid tokens
+  int32_t pad;
+};
+
+// Workspace header (first 256 bytes of every update workspace).
+struct WsHeader {
+  int32_t num_chunks;  // chunks written by the plan kernel
+  int32_t status;      // bit 0: clamped offsets, bit 1: chunk table overflow
+  int32_t reserved[62];
+};
+
+// chunks a sample of `len` tokens produces: full events of chunk_tokens plus the remainder
+__host__ __device__ inline int64_t chunks_for_length(int64_t len, int32_t chunk_tokens) {
+  if (len <= 0) return 0;
+  const int64_t per_event = (chunk_tokens + kTile - 1) / kTile;
+  const int64_t full = len / chunk_tokens;
+  const int64_t rem = len % chunk_tokens;
+  return full * per_event + (rem + kTile - 1) / kTile;
+}
+
+// Upper bound on the chunk count for any split of L tokens into N samples.
+__host__ __device__ inline int64_t max_chunks_bound(int64_t L, int32_t N, int32_t chunk_tokens) {
+  return (L + kTile - 1) / kTile + (L + chunk_tokens - 1) / chunk_tokens + N;
+}
+
+// ---------------------------------------------------------------------------
+// kernel parameter blocks
+// ---------------------------------------------------------------------------
+struct IntraParams {
+  const WsHeader* hdr;
+  const ChunkDesc* table;
+  int32_t H;
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* v;
+  const float* g;
+  int32_t g_layout;  // 1 per head, 2 per channel
+  const __nv_bfloat16* beta;
+  int32_t beta_layout;  // 0 none, 1 per head, 2 per channel
+  const __nv_bfloat16* erase;  // per channel or null
+  const __nv_bfloat16* write;  // per channel or null
+  __nv_bfloat16* W;
+  __nv_bfloat16* U;
+  __nv_bfloat16* KG;
+  float* Elast;
+};
+
+struct ScanParams {
+  const WsHeader* hdr;
+  const int32_t* sample_off;  // [N+1] chunk offsets per sample
+  int32_t N, H;
+  const __nv_bfloat16* W;
+  const __nv_bfloat16* U;
+  const __nv_bfloat16* KG;
+  const float* Elast;
+  const float* h0;
+  float* ht;
+};
+
+struct ReadParams {
+  int32_t num_blocks, H;
+  int64_t L;
+  const int32_t* cu;
+  const void* q;        // bf16 or fp32 [L,H,D]
+  const float* states;  // [num_blocks,H,D,D]
+  float scale;
+  void* out;            // plain read: [L,H,D] (bf16 or fp32)
+  int32_t out_bf16;
+  // fused readout
+  int32_t fused;
+  int32_t normalize_q;
+  float q_eps;
+  const __nv_bfloat16* gate;
+  const __nv_bfloat16* norm_w;
+  float norm_eps, softcap;
+  const __nv_bfloat16* residual;
+  int64_t row_stride;
+  int32_t head_offset;
+};
+
+struct RecurrentParams {
+  const int32_t* cu;
+  int32_t N, H;
+  int64_t L;
+  const float* k;
+  const float* v;
+  const float* g;
+  int32_t g_layout;
+  const float* beta;
+  int32_t beta_layout;
+  const float* erase;
+  const float* write;
+  const float* h0;
+  float* ht;
+};
+
+}  // namespace memt

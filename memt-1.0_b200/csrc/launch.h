@@ -1,0 +1,54 @@
+// Internal launchers, one translation unit per kernel family (built in parallel).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <mutex>
+#include <set>
+#include <utility>
+
+#include "common.cuh"
+#include "memt_gdn2.h"
+
+namespace memt {
+
+// Maps a CUDA error to MEMT_ERR_CUDA and records it for memt_last_cuda_error().
+int cuda_status(cudaError_t e);
+
+// Opt a kernel into large dynamic shared memory once per (kernel, device).
+template <typename Kernel>
+cudaError_t ensure_smem(Kernel kernel, size_t bytes) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  auto key = std::make_pair(reinterpret_cast<const void*>(kernel), dev);
+  if (done.count(key)) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+  if (e == cudaSuccess) done.insert(key);
+  return e;
+}
+
+// Optional per-launch CUDA-event timing (memt_profiler_*). Usage around a launch:
+//   ProfScope prof(kProfIntra, stream);  kernel<<<...>>>(...);
+enum ProfFamily { kProfPlan = 0, kProfIntra, kProfScan, kProfReadGemv, kProfReadTile, kProfRecurrent };
+void prof_begin(int family, cudaStream_t s, void** token);
+void prof_end(void* token, cudaStream_t s);
+struct ProfScope {
+  void* token = nullptr;
+  cudaStream_t s;
+  ProfScope(int family, cudaStream_t stream) : s(stream) { prof_begin(family, stream, &token); }
+  ~ProfScope() { prof_end(token, s); }
+};
+
+int launch_plan(const int32_t* cu, int32_t N, int64_t L, int32_t chunk_tokens, int32_t max_chunks,
+                WsHeader* hdr, ChunkDesc* table, int32_t* sample_off, cudaStream_t s);
+int launch_intra(int D, bool erase, const IntraParams& p, int64_t max_chunks, cudaStream_t s);
+int launch_scan(int D, const ScanParams& p, cudaStream_t s);
+int launch_recurrent(int D, const RecurrentParams& p, cudaStream_t s);
+// exact: fp32 query and state (no bf16 rounding); maxlen: bound on tokens per block
+int launch_read(const ReadParams& p, int D, bool exact, int64_t maxlen, cudaStream_t s);
+
+}  // namespace memt

@@ -1,0 +1,53 @@
+// Launchers for the snapshot readout kernels (read.cuh).
+#include "launch.h"
+#include "read.cuh"
+
+namespace memt {
+
+constexpr int kGemvTokens = 4;     // tokens per GEMV CTA
+constexpr int kGemvMaxBlock = 16;  // blocks up to this many tokens use the GEMV kernel
+
+template <int D, bool EXACT>
+static int launch_gemv(const ReadParams& p, int64_t maxlen, cudaStream_t s) {
+  int64_t groups = (maxlen + kGemvTokens - 1) / kGemvTokens;
+  if (groups < 1) groups = 1;
+  if (groups > 65535) return MEMT_ERR_UNSUPPORTED;
+  dim3 grid(static_cast<unsigned>(p.num_blocks) * p.H, static_cast<unsigned>(groups));
+  ProfScope prof(kProfReadGemv, s);
+  read_gemv_kernel<D, kGemvTokens, EXACT><<<grid, 256, 0, s>>>(p);
+  return cuda_status(cudaGetLastError());
+}
+
+template <int D>
+static int launch_tile(const ReadParams& p, int64_t maxlen, cudaStream_t s) {
+  using Cfg = ReadTileCfg<D>;
+  cudaError_t e = ensure_smem(read_tile_kernel<D>, Cfg::kSmem);
+  if (e != cudaSuccess) return cuda_status(e);
+  const int64_t per = int64_t(kReadTilesPerCta) * kTile;
+  int64_t groups = (maxlen + per - 1) / per;
+  if (groups < 1) groups = 1;
+  if (groups > 65535) return MEMT_ERR_UNSUPPORTED;
+  dim3 grid(static_cast<unsigned>(p.num_blocks) * p.H, static_cast<unsigned>(groups));
+  ProfScope prof(kProfReadTile, s);
+  read_tile_kernel<D><<<grid, Cfg::kNW * 32, Cfg::kSmem, s>>>(p);
+  return cuda_status(cudaGetLastError());
+}
+
+int launch_read(const ReadParams& p, int D, bool exact, int64_t maxlen, cudaStream_t s) {
+  if (exact || maxlen <= kGemvMaxBlock) {
+    switch (D) {
+      case 64: return exact ? launch_gemv<64, true>(p, maxlen, s) : launch_gemv<64, false>(p, maxlen, s);
+      case 128: return exact ? launch_gemv<128, true>(p, maxlen, s) : launch_gemv<128, false>(p, maxlen, s);
+      case 256: return exact ? launch_gemv<256, true>(p, maxlen, s) : launch_gemv<256, false>(p, maxlen, s);
+      default: return MEMT_ERR_UNSUPPORTED;
+    }
+  }
+  switch (D) {
+    case 64: return launch_tile<64>(p, maxlen, s);
+    case 128: return launch_tile<128>(p, maxlen, s);
+    case 256: return launch_tile<256>(p, maxlen, s);
+    default: return MEMT_ERR_UNSUPPORTED;
+  }
+}
+
+}  // namespace memt

@@ -1,0 +1,29 @@
+// Launcher for the inter-chunk state scan (scan.cuh).
+#include "launch.h"
+#include "scan.cuh"
+
+namespace memt {
+
+template <int D>
+static int launch_scan_t(const ScanParams& p, cudaStream_t s) {
+  constexpr int BV = 64;
+  constexpr int NW = D <= 128 ? 4 : 8;
+  using Cfg = ScanCfg<D, BV, NW>;
+  cudaError_t e = ensure_smem(scan_kernel<D, BV, NW>, Cfg::kSmem);
+  if (e != cudaSuccess) return cuda_status(e);
+  const unsigned grid = static_cast<unsigned>(p.N) * p.H * (D / BV);
+  ProfScope prof(kProfScan, s);
+  scan_kernel<D, BV, NW><<<grid, Cfg::kThreads, Cfg::kSmem, s>>>(p);
+  return cuda_status(cudaGetLastError());
+}
+
+int launch_scan(int D, const ScanParams& p, cudaStream_t s) {
+  switch (D) {
+    case 64: return launch_scan_t<64>(p, s);
+    case 128: return launch_scan_t<128>(p, s);
+    case 256: return launch_scan_t<256>(p, s);
+    default: return MEMT_ERR_UNSUPPORTED;
+  }
+}
+
+}  // namespace memt

@@ -1,0 +1,307 @@
+"""Drop-in operators for the MemT-1.0 memory hot path, backed by the sm_100a C ABI.
+
+Signatures, argument meaning and error behaviour follow the reference plugin
+(paths relative to ``inference/memt_sglang``):
+
+* ``token_memory_packed``  models/qwen/ops/packed.py:34-81 (Qwen, with ``erase``) and
+                           models/deepseek/ops/packed.py:70-108 (DeepSeek, no erase)
+* ``memt_gdn2_read_fwd``   models/qwen/ops/read.py:10-39
+* ``snapshot_read``        models/deepseek/ops/read.py:6-31
+* ``memory_readout``       l2norm(q) -> read -> MemTRMSNormGated -> residual add
+                           (models/qwen/layer.py:15-31,112-131; models/qwen/integration.py:61-64)
+* ``gdn2_chunked``         the BASELINE-style (q, k, v, g, beta, initial_state, cu_seqlens)
+                           -> (o, final_state) entry over the same kernels.
+
+Every operator runs on the current torch CUDA stream, never synchronises the host and
+raises ``ValueError`` for invalid arguments before any launch (the reference checks in
+models/common/packed.py:12-34 and runtime/executor.py:41-58).
+"""
+
+from __future__ import annotations
+
+import ctypes
+from collections import OrderedDict
+
+import torch
+
+from . import _lib
+from .layout import ChunkPlan
+
+__all__ = [
+    "token_memory_packed", "memt_gdn2_read_fwd", "snapshot_read", "memory_readout", "gdn2_chunked",
+    "gdn2_update", "Workspace",
+]
+
+_DTYPE = {torch.bfloat16: _lib.MEMT_BF16, torch.float32: _lib.MEMT_F32}
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
+
+
+def _stream(device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+class Workspace:
+    """Scratch for the update, one buffer per (device, stream), grown on demand and reused
+    by later calls on the same stream (stream order keeps reuse race-free)."""
+
+    _buffers: dict = {}
+
+    @classmethod
+    def get(cls, device: torch.device, nbytes: int) -> torch.Tensor:
+        key = (device.type, device.index, torch.cuda.current_stream(device).cuda_stream)
+        buf = cls._buffers.get(key)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
+            cls._buffers[key] = buf
+        return buf
+
+
+_cu_cache: OrderedDict = OrderedDict()
+
+
+def _cu_seqlens(lengths, device) -> torch.Tensor:
+    key = (tuple(lengths), device.type, device.index)
+    hit = _cu_cache.get(key)
+    if hit is not None:
+        _cu_cache.move_to_end(key)
+        return hit
+    cu = [0]
+    for n in lengths:
+        cu.append(cu[-1] + int(n))
+    t = torch.tensor(cu, dtype=torch.int32).to(device, non_blocking=True)
+    _cu_cache[key] = t
+    if len(_cu_cache) > 64:
+        _cu_cache.popitem(last=False)
+    return t
+
+
+def _check_lengths(lengths, total):
+    if not lengths or any(int(n) <= 0 for n in lengths) or sum(int(n) for n in lengths) != total:
+        raise ValueError("Packed sample lengths must cover the token rows")
+
+
+def _tokens(x, name):
+    """Accept [1, L, H, D] (reference layout) or [L, H, D]; return a contiguous [L, H, D] view."""
+    if x.dim() == 4:
+        if x.shape[0] != 1:
+            raise ValueError(f"{name}: packed inputs have batch size 1")
+        x = x[0]
+    if x.dim() != 3:
+        raise ValueError(f"{name}: expected [1, L, H, D] or [L, H, D]")
+    if not x.is_cuda:
+        raise ValueError(f"{name}: expected a CUDA tensor")
+    return x.contiguous()
+
+
+def _gate(x, L, H, D, name, dtype=None):
+    """Gate tensor in per-head [L,H] or per-channel [L,H,D] layout -> (tensor, layout)."""
+    if x is None:
+        return None, _lib.GATE_NONE
+    if x.dim() == 4 and x.shape[0] == 1:
+        x = x[0]
+    if dtype is not None and x.dtype != dtype:
+        raise ValueError(f"{name}: expected dtype {dtype}, got {x.dtype}")
+    if not x.is_cuda:
+        raise ValueError(f"{name}: expected a CUDA tensor")
+    if x.dim() == 2 and tuple(x.shape) == (L, H):
+        return x.contiguous(), _lib.GATE_PER_HEAD
+    if x.dim() == 3 and tuple(x.shape) == (L, H, 1):
+        return x.reshape(L, H).contiguous(), _lib.GATE_PER_HEAD
+    if x.dim() == 3 and tuple(x.shape) == (L, H, D):
+        return x.contiguous(), _lib.GATE_PER_CHANNEL
+    raise ValueError(f"{name}: expected [L, H] or [L, H, {D}], got {tuple(x.shape)}")
+
+
+def _states(x, N, H, K, V, device, name):
+    if tuple(x.shape) != (N, H, K, V) or x.dtype != torch.float32 or x.device != device:
+        raise ValueError(f"{name}: expected FP32 states {(N, H, K, V)} on {device}")
+    return x.contiguous()
+
+
+def gdn2_update(k, v, g, initial_state, cu_seqlens, *, num_samples, total_tokens, beta=None, erase=None,
+                write=None, chunk_tokens=2048, final_state=None):
+    """GDN-2 write path over packed samples. Returns the final state [N, H, K, V] fp32.
+
+    k, v: [L, H, D] bf16 (tensor-core path, reference GPU rounding) or fp32 (exact fp32
+    recurrence). g: fp32 natural-log decay [L, H] or [L, H, K]. beta: sqrt(beta) is folded
+    into k ([L, H] or [L, H, K]). erase: FLA channel-wise erase factor [L, H, K]. write:
+    write gate [L, H, V]. cu_seqlens: int32 device [N+1]. final_state may alias
+    initial_state (in-place update).
+    """
+    k = _tokens(k, "k")
+    v = _tokens(v, "v")
+    L, H, K = k.shape
+    V = v.shape[-1]
+    if v.shape[:2] != (L, H) or v.dtype != k.dtype:
+        raise ValueError("k and v must share [L, H] and dtype")
+    if k.dtype not in _DTYPE:
+        raise ValueError(f"unsupported dtype {k.dtype}")
+    if L != total_tokens:
+        raise ValueError("total_tokens must equal the packed token count")
+    dev = k.device
+    if g.dtype != torch.float32:
+        raise ValueError("log-decay must be float32")
+    g, g_layout = _gate(g, L, H, K, "g")
+    beta, beta_layout = _gate(beta, L, H, K, "beta", k.dtype)
+    erase, erase_layout = _gate(erase, L, H, K, "erase", k.dtype)
+    if erase_layout == _lib.GATE_PER_HEAD:
+        raise ValueError("erase must be per channel [L, H, K]")
+    if write is not None:
+        write = _tokens(write, "write")
+        if tuple(write.shape) != (L, H, V) or write.dtype != k.dtype:
+            raise ValueError("write gate must be [L, H, V] in the value dtype")
+    N = int(num_samples)
+    h0 = _states(initial_state, N, H, K, V, dev, "initial_state")
+    out = torch.empty_like(h0) if final_state is None else final_state
+    _states(out, N, H, K, V, dev, "final_state")
+    if not out.is_contiguous():
+        raise ValueError("final_state must be contiguous")
+    if cu_seqlens.dtype != torch.int32 or cu_seqlens.device != dev or cu_seqlens.numel() != N + 1:
+        raise ValueError("cu_seqlens must be int32 [N+1] on the input device")
+    lib = _lib.load()
+    dt = _DTYPE[k.dtype]
+    need = lib.memt_gdn2_update_workspace_size(N, L, H, K, V, int(chunk_tokens), dt)
+    if need == 0:
+        raise ValueError("unsupported update sizes")
+    ws = Workspace.get(dev, need)
+    args = _lib.UpdateArgs(
+        num_samples=N, num_heads=H, key_dim=K, value_dim=V, total_tokens=L, chunk_tokens=int(chunk_tokens),
+        dtype=dt, cu_seqlens=cu_seqlens.data_ptr(), k=k.data_ptr(), v=v.data_ptr(), g=g.data_ptr(),
+        g_layout=g_layout, beta=beta.data_ptr() if beta is not None else None, beta_layout=beta_layout,
+        erase=erase.data_ptr() if erase is not None else None, erase_layout=erase_layout,
+        write=write.data_ptr() if write is not None else None,
+        write_layout=_lib.GATE_PER_CHANNEL if write is not None else _lib.GATE_NONE,
+        initial_state=h0.data_ptr(), final_state=out.data_ptr())
+    _lib.check(lib.memt_gdn2_update(ctypes.byref(args), _ptr(ws), ws.numel(), _stream(dev)), "memt_gdn2_update")
+    return out
+
+
+def _read(q, states, cu, num_blocks, max_block_tokens, scale, out_dtype):
+    q = _tokens(q, "q")
+    L, H, K = q.shape
+    if q.dtype not in _DTYPE or out_dtype not in _DTYPE:
+        raise ValueError("q and output must be bfloat16 or float32")
+    states = _states(states, num_blocks, H, K, states.shape[-1], q.device, "states")
+    V = states.shape[-1]
+    out = torch.empty(L, H, V, device=q.device, dtype=out_dtype)
+    lib = _lib.load()
+    args = _lib.ReadArgs(
+        num_blocks=num_blocks, num_heads=H, key_dim=K, value_dim=V, total_tokens=L,
+        max_block_tokens=int(max_block_tokens), cu_seqlens=cu.data_ptr(), q=q.data_ptr(), q_dtype=_DTYPE[q.dtype],
+        states=states.data_ptr(), scale=float(scale), out=out.data_ptr(), out_dtype=_DTYPE[out_dtype])
+    _lib.check(lib.memt_gdn2_read(ctypes.byref(args), _stream(q.device)), "memt_gdn2_read")
+    return out
+
+
+def token_memory_packed(q, k, v, log_decay, write, read_states, write_states, *, erase=None, lengths, scale,
+                        chunk_tokens):
+    """Write packed GDN-2 events and read each sample's fixed incoming snapshot.
+
+    Returns (read [1, L, H, V] in v.dtype, final_state [N, H, K, V] fp32), like the
+    reference. ``erase`` is the Qwen flavour's channel-wise erase factor; the DeepSeek
+    flavour passes none.
+    """
+    L = _tokens(q, "q").shape[0]
+    _check_lengths(lengths, L)
+    cu = _cu_seqlens(lengths, q.device)
+    final = gdn2_update(k, v, log_decay, write_states, cu, num_samples=len(lengths), total_tokens=L,
+                        erase=erase, write=write, chunk_tokens=chunk_tokens)
+    read = _read(q, read_states, cu, len(lengths), max(lengths), scale, v.dtype)
+    return read.unsqueeze(0), final
+
+
+def memt_gdn2_read_fwd(q, snaps, plan: ChunkPlan, scale, out_dtype):
+    """Read each token from its read-block snapshot (models/qwen/ops/read.py:10-39)."""
+    read_slice = getattr(plan, "read_slice", None)
+    if read_slice is None:
+        raise ValueError("plan must come from memt_b200.layout.build_chunk_plan")
+    out = _read(q, snaps, read_slice, plan.num_block, plan.max_block_tokens, scale, out_dtype)
+    return out.unsqueeze(0)
+
+
+def snapshot_read(query, states, lengths, scale, *, bf16_accumulator_output=False):
+    """DeepSeek snapshot read (models/deepseek/ops/read.py:6-31): output in the query dtype.
+
+    Both accumulator modes accumulate in fp32 and round once to the query dtype; the
+    reference's bf16 baddbmm path does the same up to accumulation order.
+    """
+    L = _tokens(query, "query").shape[0]
+    _check_lengths(lengths, L)
+    cu = _cu_seqlens(lengths, query.device)
+    return _read(query, states, cu, len(lengths), max(lengths), scale, query.dtype).unsqueeze(0)
+
+
+def memory_readout(q, states, lengths, scale, gate, norm_weight, *, eps=1e-6, softcap, residual=None,
+                   out=None, head_offset=0, normalize_q=True, q_eps=1e-6):
+    """Fused decode/query readout over bf16 activations.
+
+    y = MemTRMSNormGated(read(l2norm(q), states), gate) and out = residual + y, written into
+    out[:, (head_offset + h) * D + v] (``residual`` may be ``out`` for an in-place add into
+    the attention output). Returns out [L, row_stride].
+    """
+    q = _tokens(q, "q")
+    L, H, D = q.shape
+    _check_lengths(lengths, L)
+    if q.dtype != torch.bfloat16:
+        raise ValueError("memory_readout expects bf16 activations")
+    gate = _tokens(gate, "gate")
+    if tuple(gate.shape) != (L, H, D) or gate.dtype != torch.bfloat16:
+        raise ValueError("gate must be bf16 [L, H, D]")
+    states = _states(states, len(lengths), H, D, D, q.device, "states")
+    if tuple(norm_weight.shape) != (D,) or norm_weight.dtype != torch.bfloat16:
+        raise ValueError("norm_weight must be bf16 [D]")
+    norm_weight = norm_weight.contiguous()
+    if out is None:
+        out = torch.empty(L, (head_offset + H) * D, device=q.device, dtype=torch.bfloat16)
+    if out.dim() != 2 or out.shape[0] != L or out.dtype != torch.bfloat16 or not out.is_contiguous():
+        raise ValueError("out must be a contiguous bf16 [L, row] tensor")
+    if residual is not None and (residual.shape != out.shape or residual.dtype != torch.bfloat16
+                                 or not residual.is_contiguous()):
+        raise ValueError("residual must match out")
+    cu = _cu_seqlens(lengths, q.device)
+    lib = _lib.load()
+    args = _lib.ReadoutArgs(
+        num_blocks=len(lengths), num_heads=H, head_dim=D, total_tokens=L, max_block_tokens=max(lengths),
+        cu_seqlens=cu.data_ptr(), q=q.data_ptr(), normalize_q=1 if normalize_q else 0, q_eps=float(q_eps),
+        states=states.data_ptr(), scale=float(scale), gate=gate.data_ptr(), norm_weight=norm_weight.data_ptr(),
+        norm_eps=float(eps), softcap=float(softcap),
+        residual=residual.data_ptr() if residual is not None else None, out=out.data_ptr(),
+        row_stride=out.shape[1], head_offset=int(head_offset))
+    _lib.check(lib.memt_memory_readout(ctypes.byref(args), _stream(q.device)), "memt_memory_readout")
+    return out
+
+
+def gdn2_chunked(q, k, v, g, beta, initial_state, cu_seqlens, *, w=None, scale=None, read_states=None,
+                 chunk_tokens=2048, erase=None, max_seqlen=None):
+    """(q, k, v, g, beta, initial_state, cu_seqlens) -> (o, final_state).
+
+    q, k: L2-normalised [L, H, K]; beta enters as sqrt(beta) folded into k (stable GDN-2);
+    w: optional write gate [L, H, V]; o reads the incoming snapshot (read_states, default
+    initial_state) and is returned in v's dtype; final_state is fp32 [N, H, K, V].
+    cu_seqlens may live on the host (validated there) or on the device; with device offsets
+    pass ``max_seqlen`` (the longest sample) to avoid a device-to-host copy.
+    """
+    k3 = _tokens(k, "k")
+    L, H, K = k3.shape
+    if cu_seqlens.is_cuda and max_seqlen is not None:
+        N = cu_seqlens.numel() - 1
+        max_len = int(max_seqlen)
+        if N < 1 or max_len < 1:
+            raise ValueError("cu_seqlens must hold at least two offsets and max_seqlen >= 1")
+        cu = cu_seqlens if cu_seqlens.dtype == torch.int32 else cu_seqlens.to(torch.int32)
+    else:
+        cu_host = cu_seqlens.detach().to("cpu", torch.int64)
+        N = cu_host.numel() - 1
+        if N < 1 or int(cu_host[0]) != 0 or int(cu_host[-1]) != L or bool((cu_host[1:] < cu_host[:-1]).any()):
+            raise ValueError("cu_seqlens must be nondecreasing offsets from 0 to L")
+        max_len = int((cu_host[1:] - cu_host[:-1]).max())
+        cu = cu_seqlens.to(device=k3.device, dtype=torch.int32).contiguous()
+    scale = K ** -0.5 if scale is None else scale
+    final = gdn2_update(k3, v, g, initial_state, cu, num_samples=N, total_tokens=L, beta=beta,
+                        erase=erase, write=w, chunk_tokens=chunk_tokens)
+    rs = initial_state if read_states is None else read_states
+    o = _read(q, rs, cu, N, max(max_len, 1), scale, _tokens(v, "v").dtype)
+    return o, final

@@ -1,0 +1,370 @@
+"""GPU parity of the sm_100a kernels against the CPU oracle and the reference's goldens.
+
+Tolerances (relative Frobenius):
+  * bf16 inputs / fp32 state: <= 1e-3 against the oracle's emulation of the reference's
+    GPU rounding points (BASELINE tolerance);
+  * fp32 mode: <= 1e-5 against float64 exact math and the reference's fp32 outputs.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import memt_b200 as M
+from memt_b200 import ops
+from oracle import gdn2 as O
+
+pytestmark = pytest.mark.gpu
+
+TOL_BF16 = 1e-3
+TOL_F32 = 1e-5
+
+
+def _t(x, dev, dtype=torch.float32):
+    return torch.from_numpy(np.ascontiguousarray(np.asarray(x, np.float32))).to(dev).to(dtype)
+
+
+def make_inputs(seed, lengths, H, D, *, gate="channel", beta="head", erase=False, write=True, state=True,
+                decay_mean=2.0):
+    """BASELINE distributions: q,k ~N(0,1) then L2-normalised, v ~N(0,1), g = logsigmoid(N(2,.5)),
+    beta = sigmoid(N(0,1)), write = sigmoid(N(0,1)), states ~N(0, 0.02)."""
+    rng = np.random.default_rng(seed)
+    L, N = int(sum(lengths)), len(lengths)
+
+    def nrm(x):
+        return x / np.sqrt((x.astype(np.float64) ** 2).sum(-1, keepdims=True) + 1e-6)
+
+    x = dict(lengths=list(lengths), cu=np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32))
+    x["q"] = nrm(rng.standard_normal((L, H, D))).astype(np.float32)
+    x["k"] = nrm(rng.standard_normal((L, H, D))).astype(np.float32)
+    x["v"] = rng.standard_normal((L, H, D)).astype(np.float32)
+    gshape = (L, H, D) if gate == "channel" else (L, H)
+    x["g"] = (-np.logaddexp(0.0, -rng.normal(decay_mean, 0.5, gshape))).astype(np.float32)
+    bshape = {"head": (L, H), "channel": (L, H, D), None: None}[beta]
+    x["beta"] = None if bshape is None else (1 / (1 + np.exp(-rng.standard_normal(bshape)))).astype(np.float32)
+    x["erase"] = (1 / (1 + np.exp(-rng.standard_normal((L, H, D))))).astype(np.float32) if erase else None
+    x["w"] = (1 / (1 + np.exp(-rng.standard_normal((L, H, D))))).astype(np.float32) if write else None
+    sd = 0.02 if state else 0.0
+    x["h0"] = (sd * rng.standard_normal((N, H, D, D))).astype(np.float32)
+    x["r0"] = (sd * rng.standard_normal((N, H, D, D))).astype(np.float32)
+    return x
+
+
+def to_bf16(x):
+    out = dict(x)
+    for key in ("q", "k", "v", "beta", "erase", "w"):
+        if out[key] is not None:
+            out[key] = O.bf16(out[key]).astype(np.float32)
+    return out
+
+
+def oracle_key(x, mode):
+    """k' = sqrt(beta) * k, with the reference's bf16 rounding of sqrt(beta) and of the product."""
+    k = x["k"].astype(np.float64)
+    if x["beta"] is None:
+        return k
+    b = x["beta"].astype(np.float64)
+    if b.ndim == 2:
+        b = b[:, :, None]
+    s = np.sqrt(b)
+    return O.bf16(O.bf16(s) * k) if mode == "bf16" else s * k
+
+
+def oracle_update(x, chunk_tokens, mode):
+    kk = oracle_key(x, mode)
+    g = x["g"] if x["g"].ndim == 3 else np.broadcast_to(x["g"][:, :, None], x["k"].shape)
+    if mode == "bf16":
+        ops_ = O.intra(kk, g, x["v"], O.plan_chunks(x["cu"], chunk_tokens), b=x["erase"], w=x["w"], mode="bf16")
+        return O.scan(ops_, O.plan_chunks(x["cu"], chunk_tokens), x["h0"], mode="bf16")
+    return O.recurrence(kk, x["v"], g, x["h0"], x["cu"], b=x["erase"], w=x["w"])
+
+
+def gpu_update(x, dev, dtype, chunk_tokens, final_state=None, h0=None):
+    cu = torch.from_numpy(x["cu"]).to(dev)
+    h0 = _t(x["h0"], dev) if h0 is None else h0
+    return ops.gdn2_update(
+        _t(x["k"], dev, dtype), _t(x["v"], dev, dtype), _t(x["g"], dev), h0, cu,
+        num_samples=len(x["lengths"]), total_tokens=int(x["cu"][-1]),
+        beta=None if x["beta"] is None else _t(x["beta"], dev, dtype),
+        erase=None if x["erase"] is None else _t(x["erase"], dev, dtype),
+        write=None if x["w"] is None else _t(x["w"], dev, dtype), chunk_tokens=chunk_tokens,
+        final_state=final_state)
+
+
+# ---------------------------------------------------------------------------
+# reference goldens
+# ---------------------------------------------------------------------------
+
+PACKED = ["cfg0_qwen", "varlen_qwen", "d128_qwen", "varlen_flash"]
+
+
+@pytest.mark.parametrize("name", PACKED)
+def test_golden_fp32(golden, cuda, name):
+    """fp32 mode against the reference's own fp32 outputs."""
+    z = golden(name)
+    erase = _t(z["b"], cuda)[None] if str(z["flavour"]) == "qwen" else None
+    read, final = M.token_memory_packed(
+        _t(z["q"], cuda)[None], _t(z["k"], cuda)[None], _t(z["v"], cuda)[None], _t(z["g"], cuda)[None],
+        _t(z["w"], cuda)[None], _t(z["r0"], cuda), _t(z["h0"], cuda), erase=erase,
+        lengths=[int(n) for n in z["lengths"]], scale=float(z["scale"]), chunk_tokens=int(z["chunk_tokens"]))
+    torch.cuda.synchronize()
+    assert read.shape == (1, *z["read"].shape) and read.dtype == torch.float32
+    assert O.rel_fro(final.cpu().numpy(), z["final_state"]) <= TOL_F32
+    if np.abs(z["read"]).sum() > 0:
+        assert O.rel_fro(read[0].cpu().numpy(), z["read"]) <= TOL_F32
+
+
+@pytest.mark.parametrize("name", PACKED)
+def test_golden_bf16(golden, cuda, name):
+    """bf16 inputs through token_memory_packed against the oracle's GPU-rounding emulation."""
+    z = golden(name)
+    qwen = str(z["flavour"]) == "qwen"
+    rb = {key: O.bf16(z[key]).astype(np.float32) for key in ("q", "k", "v", "w", "b")}
+    bf = torch.bfloat16
+    read, final = M.token_memory_packed(
+        _t(rb["q"], cuda, bf)[None], _t(rb["k"], cuda, bf)[None], _t(rb["v"], cuda, bf)[None],
+        _t(z["g"], cuda)[None], _t(rb["w"], cuda, bf)[None], _t(z["r0"], cuda), _t(z["h0"], cuda),
+        erase=_t(rb["b"], cuda, bf)[None] if qwen else None, lengths=[int(n) for n in z["lengths"]],
+        scale=float(z["scale"]), chunk_tokens=int(z["chunk_tokens"]))
+    torch.cuda.synchronize()
+    assert read.dtype == torch.bfloat16
+    o_ref, s_ref = O.chunked(rb["q"], rb["k"], rb["v"], z["g"], z["h0"], z["r0"], z["cu_seqlens"],
+                             float(z["scale"]), b=rb["b"] if qwen else None, w=rb["w"],
+                             chunk_tokens=int(z["chunk_tokens"]), mode="bf16")
+    err_s = O.rel_fro(final.cpu().numpy(), s_ref)
+    assert err_s <= TOL_BF16, err_s
+    if np.abs(o_ref).sum() > 0:
+        assert O.rel_fro(read[0].float().cpu().numpy(), o_ref) <= TOL_BF16
+
+
+# ---------------------------------------------------------------------------
+# update parity sweep
+# ---------------------------------------------------------------------------
+
+CASES = [
+    # lengths, H, D, gate, beta, erase, write, chunk_tokens
+    ([512], 4, 64, "head", "head", False, True, 2048),           # BASELINE config 0 shape
+    ([1], 2, 128, "channel", None, False, True, 2048),
+    ([63, 64, 65], 2, 128, "channel", "head", True, True, 2048),
+    ([130, 1, 200], 3, 128, "head", "channel", False, False, 128),
+    ([300, 7], 2, 128, "channel", "head", False, True, 100),     # events not a multiple of 64
+    ([150, 64], 2, 256, "channel", "head", True, True, 2048),
+    ([257], 1, 256, "head", None, False, True, 2048),
+    ([33, 97, 64, 1], 4, 64, "channel", "channel", True, False, 64),
+]
+
+
+@pytest.mark.parametrize("case", CASES, ids=[f"c{i}" for i in range(len(CASES))])
+def test_update_bf16_parity(cuda, case):
+    lengths, H, D, gate, beta, erase, write, ct = case
+    x = to_bf16(make_inputs(hash(str(case)) % 2**31, lengths, H, D, gate=gate, beta=beta, erase=erase,
+                            write=write))
+    out = gpu_update(x, cuda, torch.bfloat16, ct)
+    torch.cuda.synchronize()
+    ref = oracle_update(x, ct, "bf16")
+    err = O.rel_fro(out.cpu().numpy(), ref)
+    assert err <= TOL_BF16, err
+
+
+@pytest.mark.parametrize("case", CASES[:5], ids=[f"c{i}" for i in range(5)])
+def test_update_fp32_exact(cuda, case):
+    lengths, H, D, gate, beta, erase, write, ct = case
+    x = make_inputs(1 + hash(str(case)) % 2**31, lengths, H, D, gate=gate, beta=beta, erase=erase, write=write)
+    out = gpu_update(x, cuda, torch.float32, ct)
+    torch.cuda.synchronize()
+    ref = oracle_update(x, ct, "exact")
+    assert O.rel_fro(out.cpu().numpy(), ref) <= TOL_F32
+
+
+def test_update_extreme_decay_slow_path(cuda):
+    """Channels that decay by ~2^-40 per token overflow any factorised exponent; the kernel
+    must switch to exact per-pair exponents (as the reference's diagonal kernel does)."""
+    x = make_inputs(7, [200, 64], 2, 128, gate="channel", beta="head", erase=False, write=True)
+    x["g"][:, :, ::5] = -28.0
+    x = to_bf16(x)
+    out = gpu_update(x, cuda, torch.bfloat16, 2048)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    assert np.isfinite(got).all()
+    assert O.rel_fro(got, oracle_update(x, 2048, "bf16")) <= TOL_BF16
+
+
+def test_update_in_place(cuda):
+    x = to_bf16(make_inputs(11, [100, 37], 2, 128))
+    state = _t(x["h0"], cuda)
+    out = gpu_update(x, cuda, torch.bfloat16, 2048, final_state=state, h0=state)
+    torch.cuda.synchronize()
+    assert out.data_ptr() == state.data_ptr()
+    assert O.rel_fro(state.cpu().numpy(), oracle_update(x, 2048, "bf16")) <= TOL_BF16
+
+
+def test_update_zero_state_and_single_token_samples(cuda):
+    x = to_bf16(make_inputs(12, [1, 1, 1, 2], 2, 64, state=False))
+    out = gpu_update(x, cuda, torch.bfloat16, 2048)
+    torch.cuda.synchronize()
+    assert O.rel_fro(out.cpu().numpy(), oracle_update(x, 2048, "bf16")) <= TOL_BF16
+
+
+def test_update_workspace_status_clean(cuda):
+    x = to_bf16(make_inputs(13, [70, 3], 2, 128))
+    gpu_update(x, cuda, torch.bfloat16, 2048)
+    from memt_b200 import _lib
+    import ctypes
+    lib = _lib.load()
+    ws = ops.Workspace.get(cuda, 0)
+    st = ctypes.c_int32(-1)
+    _lib.check(lib.memt_gdn2_workspace_status(ctypes.c_void_p(ws.data_ptr()),
+                                              ctypes.c_void_p(torch.cuda.current_stream().cuda_stream),
+                                              ctypes.byref(st)), "status")
+    assert st.value == 0
+
+
+# ---------------------------------------------------------------------------
+# reads
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("lengths", [[1, 1, 1], [3, 16, 2], [70, 1, 130], [600]])
+@pytest.mark.parametrize("D", [64, 128, 256])
+def test_read_bf16(cuda, lengths, D):
+    rng = np.random.default_rng(D + len(lengths))
+    L, N, H = sum(lengths), len(lengths), 2
+    q = O.bf16(rng.standard_normal((L, H, D)) / np.sqrt(D)).astype(np.float32)
+    S = (0.05 * rng.standard_normal((N, H, D, D))).astype(np.float32)
+    out = M.snapshot_read(_t(q, cuda, torch.bfloat16)[None], _t(S, cuda), lengths, D ** -0.5)
+    torch.cuda.synchronize()
+    cu = np.concatenate([[0], np.cumsum(lengths)])
+    ref = O.read(q, S, cu, D ** -0.5, mode="bf16")
+    got = out[0].float().cpu().numpy()
+    assert O.rel_fro(got, ref) <= TOL_BF16
+    assert np.mean(got != ref.astype(np.float32)) < 0.02
+
+
+@pytest.mark.parametrize("lengths", [[1, 2], [5, 40, 3]])
+def test_read_fp32_exact(cuda, lengths):
+    rng = np.random.default_rng(3)
+    L, N, H, D = sum(lengths), len(lengths), 2, 128
+    q = rng.standard_normal((L, H, D)).astype(np.float32)
+    S = rng.standard_normal((N, H, D, D)).astype(np.float32)
+    out = M.snapshot_read(_t(q, cuda)[None], _t(S, cuda), lengths, 0.1)
+    torch.cuda.synchronize()
+    ref = O.read(q, S, np.concatenate([[0], np.cumsum(lengths)]), 0.1)
+    assert O.rel_fro(out[0].cpu().numpy(), ref) <= TOL_F32
+
+
+def test_read_golden(golden, cuda):
+    z = golden("read_qwen")
+    plan = M.build_chunk_plan(torch.from_numpy(z["cu_seqlens"]).to(cuda), torch.from_numpy(z["cu_seqlens"]).to(cuda),
+                              event_slice=torch.from_numpy(z["cu_seqlens"]).to(cuda))
+    out = M.memt_gdn2_read_fwd(_t(z["q"], cuda)[None], _t(z["states"], cuda), plan, float(z["scale"]),
+                               torch.float32)
+    torch.cuda.synchronize()
+    assert O.rel_fro(out[0].cpu().numpy(), z["read"]) <= TOL_F32
+
+
+# ---------------------------------------------------------------------------
+# fused readout
+# ---------------------------------------------------------------------------
+
+def test_readout_against_reference_bf16_golden(golden, cuda):
+    z = golden("readout_bf16")
+    lengths = [int(n) for n in z["lengths"]]
+    bf = torch.bfloat16
+    out = _t(z["attn"], cuda, bf).clone()
+    M.memory_readout(_t(z["q_raw"], cuda, bf), _t(z["states"], cuda), lengths, float(z["scale"]),
+                     _t(z["gate"], cuda, bf), _t(z["weight"], cuda, bf), eps=float(z["eps"]),
+                     softcap=float(z["softcap"]), residual=out, out=out, normalize_q=True)
+    torch.cuda.synchronize()
+    got = out.float().cpu().numpy()
+    assert O.rel_fro(got, z["residual"]) <= 4e-3  # the reference's own bf16 pipeline (bmm order differs)
+    ref = O.readout_fused(z["q_raw"], z["states"], z["cu_seqlens"], float(z["scale"]), z["gate"], z["weight"],
+                          float(z["eps"]), float(z["softcap"]), z["attn"], normalize_q=True, mode="bf16")
+    assert O.rel_fro(got, ref) <= TOL_BF16
+
+
+@pytest.mark.parametrize("lengths", [[1] * 9, [2, 1, 30], [100, 1]])
+@pytest.mark.parametrize("D", [64, 128, 256])
+def test_readout_fused_parity(cuda, lengths, D):
+    rng = np.random.default_rng(D * 7 + sum(lengths))
+    L, N, H = sum(lengths), len(lengths), 3
+    cu = np.concatenate([[0], np.cumsum(lengths)])
+    q = O.bf16(rng.standard_normal((L, H, D))).astype(np.float32)
+    S = (0.05 * rng.standard_normal((N, H, D, D))).astype(np.float32)
+    gate = O.bf16(rng.normal(0.5, 2.0, (L, H, D))).astype(np.float32)
+    w = O.bf16(rng.normal(1.0, 0.1, (D,))).astype(np.float32)
+    head_offset = 1
+    attn = O.bf16(rng.standard_normal((L, (H + head_offset) * D))).astype(np.float32)
+    bf = torch.bfloat16
+    out = _t(attn, cuda, bf)
+    M.memory_readout(_t(q, cuda, bf), _t(S, cuda), lengths, D ** -0.5, _t(gate, cuda, bf), _t(w, cuda, bf),
+                     eps=1e-6, softcap=10.0, residual=out, out=out, head_offset=head_offset, normalize_q=True)
+    torch.cuda.synchronize()
+    got = out.float().cpu().numpy()
+    y = O.readout_fused(q, S, cu, D ** -0.5, gate, w, 1e-6, 10.0, None, normalize_q=True, mode="bf16")
+    ref = attn.astype(np.float64).copy()
+    ref[:, head_offset * D:] = O.bf16(ref[:, head_offset * D:] + y)
+    assert np.array_equal(got[:, :head_offset * D], attn[:, :head_offset * D])  # other heads untouched
+    assert O.rel_fro(got, ref) <= TOL_BF16
+
+
+# ---------------------------------------------------------------------------
+# full-size properties (BASELINE config 1 geometry)
+# ---------------------------------------------------------------------------
+
+def test_config1_pack_independence_and_sampled_oracle(cuda):
+    """B=8 x T=8192, H=16, d=128. Each sample's result must not depend on the others
+    (bitwise) and one (sample, head) slice is checked against the oracle."""
+    lengths, H, D = [8192] * 8, 16, 128
+    rng = np.random.default_rng(0)
+    L = sum(lengths)
+    gen = torch.Generator(device=cuda).manual_seed(0)
+    bf = torch.bfloat16
+
+    def nrm(x):
+        return (x / torch.sqrt((x.float() ** 2).sum(-1, keepdim=True) + 1e-6)).to(bf)
+
+    k = nrm(torch.randn(L, H, D, device=cuda, generator=gen))
+    v = torch.randn(L, H, D, device=cuda, generator=gen).to(bf)
+    g = torch.nn.functional.logsigmoid(2.0 + 0.5 * torch.randn(L, H, device=cuda, generator=gen))
+    beta = torch.sigmoid(torch.randn(L, H, device=cuda, generator=gen)).to(bf)
+    w = torch.sigmoid(torch.randn(L, H, D, device=cuda, generator=gen)).to(bf)
+    h0 = 0.02 * torch.randn(8, H, D, D, device=cuda, generator=gen)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lengths)]), dtype=torch.int32, device=cuda)
+    full = ops.gdn2_update(k, v, g, h0, cu, num_samples=8, total_tokens=L, beta=beta, write=w)
+    n = 5
+    sl = slice(n * 8192, (n + 1) * 8192)
+    one = ops.gdn2_update(k[sl], v[sl], g[sl], h0[n:n + 1].contiguous(),
+                          torch.tensor([0, 8192], dtype=torch.int32, device=cuda), num_samples=1,
+                          total_tokens=8192, beta=beta[sl], write=w[sl])
+    torch.cuda.synchronize()
+    assert torch.isfinite(full).all()
+    assert torch.equal(full[n], one[0])
+    h = 9
+    x = dict(lengths=[8192], cu=np.array([0, 8192], np.int32),
+             k=k[sl, h:h + 1].float().cpu().numpy(), v=v[sl, h:h + 1].float().cpu().numpy(),
+             g=g[sl, h:h + 1].cpu().numpy(), beta=beta[sl, h:h + 1].float().cpu().numpy(), erase=None,
+             w=w[sl, h:h + 1].float().cpu().numpy(), h0=h0[n:n + 1, h:h + 1].cpu().numpy())
+    ref = oracle_update(x, 2048, "bf16")
+    assert O.rel_fro(full[n, h:h + 1].cpu().numpy()[None], ref) <= TOL_BF16
+
+
+# ---------------------------------------------------------------------------
+# host-side validation (reference raises ValueError before launch)
+# ---------------------------------------------------------------------------
+
+def test_invalid_arguments_raise(cuda):
+    x = to_bf16(make_inputs(5, [10, 6], 2, 64))
+    bf = torch.bfloat16
+    args = (_t(x["q"], cuda, bf)[None], _t(x["k"], cuda, bf)[None], _t(x["v"], cuda, bf)[None],
+            _t(x["g"], cuda)[None], _t(x["w"], cuda, bf)[None], _t(x["r0"], cuda), _t(x["h0"], cuda))
+    with pytest.raises(ValueError):
+        M.token_memory_packed(*args, lengths=[10, 5], scale=0.1, chunk_tokens=2048)  # lengths do not cover L
+    with pytest.raises(ValueError):
+        M.token_memory_packed(*args, lengths=[16, 0], scale=0.1, chunk_tokens=2048)  # empty sample
+    bad = list(args)
+    bad[5] = bad[5].double()
+    with pytest.raises(ValueError):
+        M.token_memory_packed(*bad, lengths=[10, 6], scale=0.1, chunk_tokens=2048)  # fp64 states
+    bad = list(args)
+    bad[3] = bad[3].to(bf)
+    with pytest.raises(ValueError):
+        M.token_memory_packed(*bad, lengths=[10, 6], scale=0.1, chunk_tokens=2048)  # bf16 log-decay

@@ -1,0 +1,107 @@
+"""Pin the CPU oracle against the reference's own outputs (fixtures in tests/golden).
+
+The fixtures were produced by tests/golden/make_golden.py, which runs the reference
+plugin's operators on CPU: its Triton kernels under the Triton interpreter (fp32) and
+its PyTorch readout / gated RMSNorm in bf16.
+"""
+
+import numpy as np
+import pytest
+
+from oracle import gdn2 as O
+
+PACKED = ["cfg0_qwen", "varlen_qwen", "d128_qwen", "varlen_flash"]
+
+
+def _chunked(z, mode):
+    b = z["b"] if str(z["flavour"]) == "qwen" else None
+    return O.chunked(z["q"], z["k"], z["v"], z["g"], z["h0"], z["r0"], z["cu_seqlens"], float(z["scale"]),
+                     b=b, w=z["w"], chunk_tokens=int(z["chunk_tokens"]), mode=mode)
+
+
+@pytest.mark.parametrize("name", PACKED)
+def test_chunked_exact_matches_reference(golden, name):
+    z = golden(name)
+    o, s = _chunked(z, "exact")
+    # the reference ran in fp32 on the interpreter; the oracle is float64
+    assert O.rel_fro(s, z["final_state"]) < 2e-6
+    if np.abs(z["read"]).sum() > 0:
+        assert O.rel_fro(o, z["read"]) < 2e-6
+
+
+@pytest.mark.parametrize("name", PACKED)
+def test_recurrence_matches_reference(golden, name):
+    z = golden(name)
+    b = z["b"] if str(z["flavour"]) == "qwen" else None
+    s = O.recurrence(z["k"], z["v"], z["g"], z["h0"], z["cu_seqlens"], b=b, w=z["w"])
+    assert O.rel_fro(s, z["final_state"]) < 2e-6
+
+
+@pytest.mark.parametrize("name", PACKED)
+def test_bf16_emulation_is_close_to_exact(golden, name):
+    """The reference's GPU rounding points keep it within a few 1e-3 of exact math."""
+    z = golden(name)
+    _, s_exact = _chunked(z, "exact")
+    _, s_bf16 = _chunked(z, "bf16")
+    err = O.rel_fro(s_bf16, s_exact)
+    assert 1e-5 < err < 1e-2
+
+
+def test_read_matches_reference(golden):
+    z = golden("read_qwen")
+    o = O.read(z["q"], z["states"], z["cu_seqlens"], float(z["scale"]))
+    assert O.rel_fro(o, z["read"]) < 1e-6
+
+
+def test_l2norm_matches_reference(golden):
+    z = golden("l2norm")
+    y = O.l2norm(z["x"], float(z["eps"]))
+    assert O.rel_fro(y, z["y"]) < 1e-6
+
+
+def test_bf16_readout_pipeline_matches_reference(golden):
+    """l2norm -> bf16 snapshot read -> gated RMSNorm -> residual, all in bf16 on the reference."""
+    z = golden("readout_bf16")
+    qh = O.l2norm(z["q_raw"], mode="bf16")
+    assert np.array_equal(qh.astype(np.float32), z["q_hat"])
+    o = O.read(z["q_hat"], z["states"], z["cu_seqlens"], float(z["scale"]), mode="bf16")
+    # reference bf16 bmm vs oracle: identical rounding points, accumulation order differs
+    assert O.rel_fro(o, z["read"]) < 4e-3
+    D = z["read"].shape[-1]
+    y = O.gated_rms_norm(z["read"].reshape(-1, D), z["gate"].reshape(-1, D), z["weight"], float(z["eps"]),
+                         float(z["softcap"]), mode="bf16")
+    assert O.rel_fro(y, z["y_qwen"]) < 4e-3
+    assert O.rel_fro(y, z["y_deepseek"]) < 4e-3
+    mism = np.mean(y.astype(np.float32) != z["y_qwen"].reshape(y.shape))
+    assert mism < 0.02  # nearly bit-identical bf16 outputs
+    full = O.readout_fused(z["q_raw"], z["states"], z["cu_seqlens"], float(z["scale"]), z["gate"], z["weight"],
+                           float(z["eps"]), float(z["softcap"]), z["attn"], normalize_q=True, mode="bf16")
+    assert O.rel_fro(full, z["residual"]) < 4e-3
+
+
+@pytest.mark.parametrize("lengths,ct", [([1], 2048), ([63, 64, 65], 2048), ([300], 128), ([130, 7], 100),
+                                        ([5000], 2048), ([1, 1, 1], 64)])
+def test_plan_chunks(lengths, ct):
+    cu = np.concatenate([[0], np.cumsum(lengths)])
+    chunks = O.plan_chunks(cu, ct)
+    # every token is covered exactly once, in order, by chunks of <= 64 tokens
+    covered = []
+    for n, t0, ln in chunks:
+        assert 1 <= ln <= 64
+        assert cu[n] <= t0 and t0 + ln <= cu[n + 1]
+        covered.extend(range(t0, t0 + ln))
+    assert covered == list(range(int(cu[-1])))
+    # chunks never straddle a write event
+    for n, t0, ln in chunks:
+        assert (t0 - cu[n]) // ct == (t0 + ln - 1 - cu[n]) // ct
+
+
+def test_rounding_helpers():
+    x = np.array([1.0, 1.00390625, 1.005859375, -3.14159, 1e-30, 65504.0], np.float64)
+    b = O.bf16(x)
+    # bf16 keeps 8 significant bits
+    for v, r in zip(x, b):
+        assert abs(v - r) <= abs(v) * 2 ** -8 + 1e-45
+    assert O.bf16(np.array([1.00390625]))[0] == 1.0  # tie to even
+    t = O.tf32(np.array([1.0 + 2 ** -11]))[0]
+    assert t == 1.0 + 2 ** -10  # tie away from zero
