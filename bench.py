@@ -189,10 +189,12 @@ def run_ours(args, rank, world, local_rank):
 
     # CPU-baseline pool is created before any GPU work (spawn).
     pool, cores = (None, 0)
-    if rank == 0 and world == 1 and not args.skip_cpu_baseline:
+    if rank == 0 and world == 1 and not args.skip_cpu_baseline and args.only == "all":
         pool, cores = cpu_pool()
 
     hbm, tflops, peak_kind = peaks()
+    SESSIONS = args.sessions
+    only_update = args.only == "update"
     gen = torch.Generator(device=dev).manual_seed(1234 + rank)
     bf = torch.bfloat16
     L = SESSIONS * T
@@ -245,62 +247,65 @@ def run_ours(args, rank, world, local_rank):
     _lib.profiler_reset()
     launches = sum(n for _, n in prof.values())
 
-    # ---- end to end through the public API: pinned host inputs -> device -> result -> host ----
-    host_in = {name: t.cpu().pin_memory() for name, t in
-               dict(q=q, k=k, v=v, g=g, beta=beta, w=w, h0=h0).items()}
-    dev_in = {name: torch.empty_like(t) for name, t in dict(q=q, k=k, v=v, g=g, beta=beta, w=w, h0=h0).items()}
-    host_out_o = torch.empty(L, H, D, dtype=bf, pin_memory=True)
-    host_out_s = torch.empty(SESSIONS, H, D, D, dtype=torch.float32, pin_memory=True)
-    bytes_in = sum(t.numel() * t.element_size() for t in host_in.values())
-    bytes_out = host_out_o.numel() * 2 + host_out_s.numel() * 4
+    e2e_ms = ro_us = ro_gbs = float("nan")
+    bytes_in = bytes_out = 0
+    if not only_update:
+        # ---- end to end through the public API: pinned host inputs -> device -> result -> host ----
+        host_in = {name: t.cpu().pin_memory() for name, t in
+                   dict(q=q, k=k, v=v, g=g, beta=beta, w=w, h0=h0).items()}
+        dev_in = {name: torch.empty_like(t) for name, t in dict(q=q, k=k, v=v, g=g, beta=beta, w=w, h0=h0).items()}
+        host_out_o = torch.empty(L, H, D, dtype=bf, pin_memory=True)
+        host_out_s = torch.empty(SESSIONS, H, D, D, dtype=torch.float32, pin_memory=True)
+        bytes_in = sum(t.numel() * t.element_size() for t in host_in.values())
+        bytes_out = host_out_o.numel() * 2 + host_out_s.numel() * 4
 
-    def e2e_step():
-        for name, t in host_in.items():
-            dev_in[name].copy_(t, non_blocking=True)
-        o, s = M.gdn2_chunked(dev_in["q"], dev_in["k"], dev_in["v"], dev_in["g"], dev_in["beta"], dev_in["h0"],
-                              cu, w=dev_in["w"], max_seqlen=T, chunk_tokens=CHUNK_TOKENS)
-        host_out_o.copy_(o, non_blocking=True)
-        host_out_s.copy_(s, non_blocking=True)
+        def e2e_step():
+            for name, t in host_in.items():
+                dev_in[name].copy_(t, non_blocking=True)
+            o, s = M.gdn2_chunked(dev_in["q"], dev_in["k"], dev_in["v"], dev_in["g"], dev_in["beta"], dev_in["h0"],
+                                  cu, w=dev_in["w"], max_seqlen=T, chunk_tokens=CHUNK_TOKENS)
+            host_out_o.copy_(o, non_blocking=True)
+            host_out_s.copy_(s, non_blocking=True)
 
-    for _ in range(2):
-        e2e_step()
-    torch.cuda.synchronize()
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / args.steps
-    barrier()
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = e0.elapsed_time(e1) / args.steps
+        barrier()
 
-    # ---- decode readout, one layer per call, state >> L2 ----
-    ro_states = torch.randn(RO_LAYERS_RESIDENT, RO_SESSIONS, H, D, D, device=dev, generator=gen) * 0.05
-    ro_q = torch.randn(RO_SESSIONS, H, D, device=dev, generator=gen).to(bf)
-    ro_gate = torch.randn(RO_SESSIONS, H, D, device=dev, generator=gen).to(bf)
-    ro_w = (1.0 + 0.1 * torch.randn(D, device=dev, generator=gen)).to(bf)
-    ro_attn = torch.randn(RO_SESSIONS, H * D, device=dev, generator=gen).to(bf)
-    ro_out = torch.empty_like(ro_attn)
-    lengths = [1] * RO_SESSIONS
+        # ---- decode readout, one layer per call, state >> L2 ----
+        ro_states = torch.randn(RO_LAYERS_RESIDENT, RO_SESSIONS, H, D, D, device=dev, generator=gen) * 0.05
+        ro_q = torch.randn(RO_SESSIONS, H, D, device=dev, generator=gen).to(bf)
+        ro_gate = torch.randn(RO_SESSIONS, H, D, device=dev, generator=gen).to(bf)
+        ro_w = (1.0 + 0.1 * torch.randn(D, device=dev, generator=gen)).to(bf)
+        ro_attn = torch.randn(RO_SESSIONS, H * D, device=dev, generator=gen).to(bf)
+        ro_out = torch.empty_like(ro_attn)
+        lengths = [1] * RO_SESSIONS
 
-    def ro_step(i):
-        M.memory_readout(ro_q, ro_states[i % RO_LAYERS_RESIDENT], lengths, D ** -0.5, ro_gate, ro_w,
-                         softcap=10.0, residual=ro_attn, out=ro_out)
+        def ro_step(i):
+            M.memory_readout(ro_q, ro_states[i % RO_LAYERS_RESIDENT], lengths, D ** -0.5, ro_gate, ro_w,
+                             softcap=10.0, residual=ro_attn, out=ro_out)
 
-    for i in range(8):
-        ro_step(i)
-    torch.cuda.synchronize()
-    r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ro_iters = 40
-    r0.record(stream)
-    for i in range(ro_iters):
-        ro_step(i)
-    r1.record(stream)
-    torch.cuda.synchronize()
-    ro_us = r0.elapsed_time(r1) * 1e3 / ro_iters
-    ro_bytes = RO_SESSIONS * H * (4 * D * D + 4 * 2 * D) + 2 * D  # state + q, gate, attn in, out
-    ro_gbs = ro_bytes / (ro_us * 1e-6) / 1e9
+        for i in range(8):
+            ro_step(i)
+        torch.cuda.synchronize()
+        r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ro_iters = 40
+        r0.record(stream)
+        for i in range(ro_iters):
+            ro_step(i)
+        r1.record(stream)
+        torch.cuda.synchronize()
+        ro_us = r0.elapsed_time(r1) * 1e3 / ro_iters
+        ro_bytes = RO_SESSIONS * H * (4 * D * D + 4 * 2 * D) + 2 * D  # state + q, gate, attn in, out
+        ro_gbs = ro_bytes / (ro_us * 1e-6) / 1e9
 
     # ---- max over ranks ----
     vals = torch.tensor([ms, e2e_ms, ro_us], dtype=torch.float64, device=dev)
@@ -337,9 +342,10 @@ def run_ours(args, rank, world, local_rank):
             "step_roofline": {"bytes": step_alg, "gbs": step_alg / (ms * 1e-3) / 1e9,
                               "frac": step_alg / (ms * 1e-3) / 1e9 / hbm},
             "kernels": {f: {"ms_per_step": v[0] / args.steps, "launches": v[1]} for f, v in prof.items() if v[1]},
-            "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": bytes_in,
+            "e2e": None if only_update else {
+                    "value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": bytes_in,
                     "d2h_bytes_per_step": bytes_out, "ms_per_step": e2e_ms},
-            "readout": {"workload": "config2: 256 sessions x 16 heads, fp32 128x128 state, 1 bf16 query each, "
+            "readout": None if only_update else {"workload": "config2: 256 sessions x 16 heads, fp32 128x128 state, 1 bf16 query each, "
                                     "fused l2norm/read/gated RMSNorm/residual, one layer per call",
                         "us_per_layer": ro_us, "gbs": ro_gbs * world, "frac": ro_gbs / hbm},
             "gpu_launches": launches,
@@ -385,6 +391,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-cpu-baseline", action="store_true")
     ap.add_argument("--reference-tokens", type=int, default=1024)
+    ap.add_argument("--sessions", type=int, default=SESSIONS, help="sessions per GPU (profiling cases)")
+    ap.add_argument("--only", choices=["all", "update"], default="all",
+                    help="update: time only the commit step (no e2e, readout, CPU baseline)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

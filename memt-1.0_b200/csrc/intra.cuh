@@ -1,53 +1,74 @@
-// GDN-2 intra-chunk kernel: one CTA per (64-token chunk, head).
+// GDN-2 intra-chunk kernel: one CTA (8 warps) per (64-token chunk, head).
 //
 // Fuses what the reference runs as four launches with HBM round trips between them
 // (paths relative to inference/memt_sglang):
-//   chunk_local_cumsum                _vendor/fla/ops/utils/cumsum.py:76-133
-//   diagonal key-key blocks           _vendor/fla/ops/gdn2/chunk_intra_token_parallel.py:25-132
-//   off-diagonal blocks + blocked solve _vendor/fla/ops/gdn2/chunk_intra.py:153-417
-//   WY operands u, w, kg              _vendor/fla/ops/gdn2/wy_fast.py:36-142
+//   chunk_local_cumsum                   _vendor/fla/ops/utils/cumsum.py:76-133
+//   diagonal key-key blocks              _vendor/fla/ops/gdn2/chunk_intra_token_parallel.py:25-132
+//   off-diagonal blocks + blocked solve  _vendor/fla/ops/gdn2/chunk_intra.py:153-417
+//   WY operands u, w, kg                 _vendor/fla/ops/gdn2/wy_fast.py:36-142
 // and writes only what the state scan consumes: w, u, kg (bf16, [chunk][head][64][D])
 // and the chunk's total decay 2^G_last (fp32, [chunk][head][D]).
 //
 // Numerics follow the reference's GPU rounding points: fp32 cumulative log2 decay;
-// exact-fp32 diagonal 16x16 blocks (here: 3xTF32 tensor-core products of the
-// factorised operands); tf32 off-diagonal blocks with the per-sub-chunk reference
-// point; fp32 forward substitution on the diagonal blocks; tf32 products for the
-// off-diagonal inverse blocks; A^-1 stored as bf16; u = A^-1 bf16(v*w),
-// w = A^-1 bf16(bf16(k*b) 2^G), kg = bf16(k 2^(G_last-G)), all with fp32 accumulation.
+// exact-fp32 diagonal 16x16 key-key blocks; tf32 off-diagonal blocks built from operands
+// scaled to the first token of the row sub-chunk; fp32 forward substitution on the
+// diagonal blocks and tf32 products for the off-diagonal inverse blocks; A^-1 stored as
+// bf16; u = A^-1 bf16(v*w), w = A^-1 bf16(bf16(k*b) 2^G), kg = bf16(k 2^(G_last-G)), all
+// with fp32 accumulation.
 //
-// Decay factors: when every cumulative exponent of the panel lies in [-60, 60] the
-// kernel tabulates E = 2^G and 1/E once and forms every factor 2^(G_i - G_n) as a
-// product (no per-pair exponentials). Otherwise (extreme decays) it evaluates
-// exp2(G_i - G_n) directly and computes the diagonal blocks pair by pair, exactly as
-// the reference does, so no factor can overflow.
+// Operand staging: k, erase, v, write (bf16) and the decay arrive by cp.async into
+// XOR-swizzled shared tiles. The tf32 score products take their fragments straight from
+// ldmatrix: the k dimension is permuted so that the bf16 pair (2t, 2t+1) a lane receives
+// feeds k-slots t and t+4 of an m16n8k8 fragment (a permutation of the summation index
+// leaves the product unchanged).
+//
+// Gate layouts:
+//   per head (one decay per token): every factor is a row or column scalar. The diagonal
+//     blocks are exact bf16 products (fp32 accumulation) times the per-pair 2^(G_i-G_j),
+//     which is the reference's fp32 sum; no factor can overflow.
+//   per channel: 2^G and 2^-G are tabulated once when every exponent of the panel lies in
+//     [-60, 60] and factors are products of table entries (diagonal blocks in 3xTF32);
+//     otherwise factors are exp2 of differences and the diagonal blocks are evaluated pair
+//     by pair, exactly as the reference's token-parallel kernel does.
 #pragma once
 
 #include "common.cuh"
 
 namespace memt {
 
-template <int D>
+template <int RL>
+__device__ __forceinline__ int xswz(int row, int col) {
+  return row * RL + ((((col >> 3) ^ row) & 7) | ((col >> 3) & ~7)) * 8 + (col & 7);
+}
+
+template <int D, bool HEAD, bool ERASE>
 struct IntraCfg {
   static constexpr int kPanel = D < 128 ? D : 128;
   static constexpr int kPanels = D / kPanel;
   static constexpr int kThreads = 256;
-  static constexpr int kLdE = kPanel + 4;   // fp32 row stride (conflict-free fragment reads)
-  static constexpr int kLdK = kPanel + 8;   // bf16 row stride
-  static constexpr int kLdA = kTile + 4;    // fp32 64x64
-  static constexpr int kLdAi = kTile + 8;   // bf16 64x64
-  static constexpr size_t kBytesE = size_t(kTile) * kLdE * 4;
-  static constexpr size_t kBytesK = size_t(kTile) * kLdK * 2;
+  static constexpr int kLdE = kPanel + 4;   // fp32 decay tables
+  static constexpr int kLdA = kTile + 4;    // fp32 64x64 scores / inverse blocks
+  static constexpr int kLdAi = kTile + 8;   // bf16 64x64 inverse
+  static constexpr size_t kTileB = size_t(kTile) * kPanel * 2;  // one bf16 [64][panel] tile
+  static constexpr size_t kBytesE = HEAD ? 0 : size_t(kTile) * kLdE * 4;
   static constexpr size_t kBytesA = size_t(kTile) * kLdA * 4;
   static constexpr size_t kBytesAi = size_t(kTile) * kLdAi * 2;
-  static_assert(size_t(kTile) * kLdK * 2 <= kBytesA, "staging tile must fit in the score buffer");
-  static constexpr size_t smem(bool erase) {
-    return 2 * kBytesE + kBytesK * (erase ? 2 : 1) + kBytesA + kBytesAi + 16;
-  }
+  // sK | sB? | sV | sW | sO | sE? | sEi? | sA (aliased by sX) | sAi
+  static constexpr size_t offK = 0;
+  static constexpr size_t offB = offK + kTileB;
+  static constexpr size_t offV = offB + (ERASE ? kTileB : 0);
+  static constexpr size_t offW = offV + kTileB;
+  static constexpr size_t offO = offW + kTileB;
+  static constexpr size_t offE = offO + kTileB;
+  static constexpr size_t offEi = offE + kBytesE;
+  static constexpr size_t offA = offEi + kBytesE;
+  static constexpr size_t offAi = offA + kBytesA;
+  static constexpr size_t kSmem = offAi + kBytesAi;
+  static_assert(kTileB <= kBytesA, "staging tile aliases the score buffer");
 };
 
-// 16x16x16 tf32 product on one warp: acc[nt] += A (16x16, row-major, lda) . B (16x16,
-// row-major [k][n], ldb); acc[nt] is the C fragment of columns 8*nt..8*nt+7.
+// 16x16x16 tf32 product on one warp: acc[nt] += A (16x16 fp32, row-major, lda) . B (16x16,
+// [k][n], ldb); acc[nt] is the C fragment of columns 8*nt..8*nt+7.
 __device__ __forceinline__ void warp_tf32_16x16x16(float (&acc)[2][4], const float* A, int lda,
                                                    const float* B, int ldb, int lane) {
   const int g = lane >> 2, t = lane & 3;
@@ -68,18 +89,6 @@ __device__ __forceinline__ void warp_tf32_16x16x16(float (&acc)[2][4], const flo
   }
 }
 
-__device__ __forceinline__ void warp_store_16x16(float* C, int ldc, const float (&acc)[2][4],
-                                                 int lane, float sign) {
-  const int g = lane >> 2, t = lane & 3;
-#pragma unroll
-  for (int nt = 0; nt < 2; ++nt) {
-    C[g * ldc + nt * 8 + 2 * t] = sign * acc[nt][0];
-    C[g * ldc + nt * 8 + 2 * t + 1] = sign * acc[nt][1];
-    C[(g + 8) * ldc + nt * 8 + 2 * t] = sign * acc[nt][2];
-    C[(g + 8) * ldc + nt * 8 + 2 * t + 1] = sign * acc[nt][3];
-  }
-}
-
 __device__ __forceinline__ void zero_acc(float (&acc)[2][4]) {
 #pragma unroll
   for (int i = 0; i < 2; ++i)
@@ -87,213 +96,345 @@ __device__ __forceinline__ void zero_acc(float (&acc)[2][4]) {
     for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
 }
 
-template <int D, bool ERASE>
-struct IntraKernel {
-  using Cfg = IntraCfg<D>;
-  static constexpr int P = Cfg::kPanel;
+// Store a 16x16 C fragment pair as fp32 (sign applied) into A and, rows masked by `len`,
+// as bf16 into Ai.
+__device__ __forceinline__ void warp_store_block(float* A, int lda, __nv_bfloat16* Ai, int ldai,
+                                                 const float (&acc)[2][4], int lane, float sign,
+                                                 int row0, int len) {
+  const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+    const float x0 = sign * acc[nt][0], x1 = sign * acc[nt][1];
+    const float x2 = sign * acc[nt][2], x3 = sign * acc[nt][3];
+    const int c = nt * 8 + 2 * t;
+    if (A != nullptr) {
+      *reinterpret_cast<float2*>(A + g * lda + c) = make_float2(x0, x1);
+      *reinterpret_cast<float2*>(A + (g + 8) * lda + c) = make_float2(x2, x3);
+    }
+    const bool ok0 = row0 + g < len, ok1 = row0 + g + 8 < len;
+    *reinterpret_cast<uint32_t*>(Ai + g * ldai + c) = ok0 ? pack_bf16x2(x0, x1) : 0u;
+    *reinterpret_cast<uint32_t*>(Ai + (g + 8) * ldai + c) = ok1 ? pack_bf16x2(x2, x3) : 0u;
+  }
+}
 
-  float* sE;   // E = 2^G (fast) or G (slow)   [64][kLdE]
-  float* sEi;  // 1/E (fast)                   [64][kLdE]
-  __nv_bfloat16* sK;  // k' (beta folded)      [64][kLdK]
-  __nv_bfloat16* sB;  // erase b               [64][kLdK]
-  float* sA;          // key-key scores / inverse blocks (fp32) [64][kLdA]
-  __nv_bfloat16* sX;  // bf16 staging operand (aliases sA)   [64][kLdK]
-  __nv_bfloat16* sAi; // A^-1 bf16              [64][kLdAi]
-  int* sFlag;
+__device__ __forceinline__ float bf_lo(uint32_t u) { return __uint_as_float(u << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
+
+template <int D, bool HEAD, bool ERASE>
+struct IntraKernel {
+  using Cfg = IntraCfg<D, HEAD, ERASE>;
+  static constexpr int P = Cfg::kPanel;
+  static constexpr int NT = Cfg::kThreads;
+
+  __nv_bfloat16 *sK, *sB, *sV, *sW, *sO, *sX, *sAi;
+  float *sE, *sEi, *sA;
+  // per-head factors: G, left (row) factor, right factors per row block, 2^G, 2^(G_last-G)
+  float *sG, *sLf, *sRf, *sEh, *sKgf;
+  float* sSeg;
 
   int tid, lane, warp, len, tok0, h;
-  int64_t row_stride;  // H*D
+  int64_t row_stride;
   bool fast;
 
-  __device__ __forceinline__ float kval(int i, int c) const {
-    return __bfloat162float(sK[i * Cfg::kLdK + c]);
-  }
-  __device__ __forceinline__ float kbval(int i, int c) const {
-    float x = kval(i, c);
-    if constexpr (ERASE) x *= __bfloat162float(sB[i * Cfg::kLdK + c]);
-    return x;
-  }
-  // 2^(G_i - G_n) for channel c of the panel
-  __device__ __forceinline__ float p2d(int i, int n, int c) const {
-    if (fast) return sE[i * Cfg::kLdE + c] * sEi[n * Cfg::kLdE + c];
-    return fast_exp2(sE[i * Cfg::kLdE + c] - sE[n * Cfg::kLdE + c]);
-  }
-  // 2^G_i
-  __device__ __forceinline__ float p2(int i, int c) const {
-    if (fast) return sE[i * Cfg::kLdE + c];
-    return fast_exp2(sE[i * Cfg::kLdE + c]);
+  // async copy of one [64][P] bf16 panel (rows >= len zero-filled) into a swizzled tile
+  __device__ __forceinline__ void load_tile(__nv_bfloat16* dst, const __nv_bfloat16* src, int c0) {
+    const __nv_bfloat16* base = src + (int64_t)tok0 * row_stride + (int64_t)h * D + c0;
+    constexpr int kChunks = kTile * P / 8;
+#pragma unroll
+    for (int i = tid; i < kChunks; i += NT) {
+      const int row = i / (P / 8), col = (i % (P / 8)) * 8;
+      const bool valid = row < len;
+      cp_async16_zfill(dst + xswz<P>(row, col), valid ? base + (int64_t)row * row_stride + col : src, valid);
+    }
   }
 
-  // Load k (beta folded), erase and the log-decay of one channel panel; build the
-  // cumulative log2 decay and the factor tables. Ends with a barrier.
-  __device__ void load_panel(const IntraParams& p, int c0) {
-    const int64_t base = (int64_t)tok0 * row_stride + (int64_t)h * D + c0;
-    // k, erase: 8 bf16 (16 B) per thread-iteration
-    constexpr int kVecPerRow = P / 8;
-    for (int idx = tid; idx < kTile * kVecPerRow; idx += Cfg::kThreads) {
-      const int i = idx / kVecPerRow, cv = (idx % kVecPerRow) * 8;
-      uint4 kv = make_uint4(0, 0, 0, 0), bv = make_uint4(0, 0, 0, 0);
-      if (i < len) {
-        const int64_t off = base + (int64_t)i * row_stride + cv;
-        kv = *reinterpret_cast<const uint4*>(p.k + off);
-        if constexpr (ERASE) bv = *reinterpret_cast<const uint4*>(p.erase + off);
-        if (p.beta_layout != 0) {
-          // k' = bf16( bf16(sqrt(beta)) * k ): stable GDN-2 key scaling
-          // (models/qwen/layer.py:81-85, 96)
-          float sb[8];
-          if (p.beta_layout == 1) {
-            float b = __bfloat162float(p.beta[(int64_t)(tok0 + i) * p.H + h]);
-            float s = bf16_round(sqrtf(b));
+  // Fold sqrt(beta) into k in place: k' = bf16( bf16(sqrt(beta)) * k ) (models/qwen/layer.py:81-96)
+  __device__ void fold_beta(const IntraParams& p, int c0) {
+    constexpr int kChunks = kTile * P / 8;
+    for (int i = tid; i < kChunks; i += NT) {
+      const int row = i / (P / 8), col = (i % (P / 8)) * 8;
+      if (row >= len) continue;
+      uint4* ptr = reinterpret_cast<uint4*>(sK + xswz<P>(row, col));
+      uint4 kv = *ptr;
+      float sb[8];
+      if (p.beta_layout == 1) {
+        const float s = bf16_round(sqrtf(__bfloat162float(p.beta[(int64_t)(tok0 + row) * p.H + h])));
 #pragma unroll
-            for (int e = 0; e < 8; ++e) sb[e] = s;
-          } else {
-            uint4 be = *reinterpret_cast<const uint4*>(p.beta + off);
-            const uint32_t* bw = reinterpret_cast<const uint32_t*>(&be);
+        for (int e = 0; e < 8; ++e) sb[e] = s;
+      } else {
+        const uint4 be = *reinterpret_cast<const uint4*>(p.beta + (int64_t)(tok0 + row) * row_stride +
+                                                         (int64_t)h * D + c0 + col);
+        const uint32_t* bw = reinterpret_cast<const uint32_t*>(&be);
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              float2 f = unpack_bf16x2(bw[e]);
-              sb[2 * e] = bf16_round(sqrtf(f.x));
-              sb[2 * e + 1] = bf16_round(sqrtf(f.y));
-            }
-          }
-          uint32_t* kw = reinterpret_cast<uint32_t*>(&kv);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            float2 f = unpack_bf16x2(kw[e]);
-            kw[e] = pack_bf16x2(f.x * sb[2 * e], f.y * sb[2 * e + 1]);
-          }
+        for (int e = 0; e < 4; ++e) {
+          sb[2 * e] = bf16_round(sqrtf(bf_lo(bw[e])));
+          sb[2 * e + 1] = bf16_round(sqrtf(bf_hi(bw[e])));
         }
       }
-      *reinterpret_cast<uint4*>(sK + i * Cfg::kLdK + cv) = kv;
-      if constexpr (ERASE) *reinterpret_cast<uint4*>(sB + i * Cfg::kLdK + cv) = bv;
+      uint32_t* kw = reinterpret_cast<uint32_t*>(&kv);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) kw[e] = pack_bf16x2(bf_lo(kw[e]) * sb[2 * e], bf_hi(kw[e]) * sb[2 * e + 1]);
+      *ptr = kv;
     }
-    // cumulative decay: one thread per channel, sequential over the 64 tokens
-    // G_t = (sum_{s<=t} g_s) * (1/ln2)  (cumsum.py:126-133; padded tokens add 0)
-    bool ok = true;
-    if (tid < P) {
-      const int c = tid;
+  }
+
+  // ---- decay, per-head layout: one warp computes every factor the chunk needs ----
+  __device__ void head_factors(const IntraParams& p) {
+    if (warp != 0) return;
+    // G_t = (sum_{s<=t} g_s) / ln2 over the 64 tokens; lane owns tokens 2*lane, 2*lane+1
+    const int t0 = 2 * lane, t1 = 2 * lane + 1;
+    float g0 = t0 < len ? p.g[(int64_t)(tok0 + t0) * p.H + h] : 0.f;
+    float g1 = t1 < len ? p.g[(int64_t)(tok0 + t1) * p.H + h] : 0.f;
+    float s = g0 + g1;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, s, o);
+      if (lane >= o) s += y;
+    }
+    const float excl = s - (g0 + g1);
+    sG[t0] = (excl + g0) * kRcpLn2;
+    sG[t1] = (excl + g0 + g1) * kRcpLn2;
+    __syncwarp();
+    const int last = len - 1;
+    const float Gl = sG[last];
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int i = 2 * lane + q;
+      const float Gi = sG[i];
+      const float Gn = sG[i & ~15];
+      sLf[i] = fast_exp2(Gi - Gn);                 // left factor 2^(G_i - G_n(i))
+      sEh[i] = fast_exp2(Gi);                      // 2^G_i
+      sKgf[i] = i < len ? fast_exp2(Gl - Gi) : 0.f;  // 2^(G_last - G_i)
+#pragma unroll
+      for (int r = 1; r < 4; ++r)                  // right factors 2^(G_n(r) - G_j), j < 16r
+        sRf[r * kTile + i] = i < 16 * r ? fast_exp2(sG[16 * r] - Gi) : 0.f;
+    }
+    if (lane == 0) sSeg[0] = fast_exp2(Gl);        // 2^G_last
+  }
+
+  // ---- decay, per-channel layout: cumulative sum and factor tables of one panel ----
+  __device__ void channel_tables() {
+    // sE holds the raw decay (cp.async); segmented scan over the 64 tokens per channel
+    constexpr int kSeg = NT / P, kSegLen = kTile / kSeg;
+    const int c = tid % P, sg = tid / P;
+    {
       float acc = 0.f;
-      for (int i = 0; i < kTile; ++i) {
-        float gi = 0.f;
-        if (i < len) {
-          if (p.g_layout == 2)
-            gi = p.g[base + (int64_t)i * row_stride + c];
-          else
-            gi = p.g[(int64_t)(tok0 + i) * p.H + h];
-        }
-        acc += gi;
-        const float G = acc * kRcpLn2;
+#pragma unroll 8
+      for (int i = sg * kSegLen; i < (sg + 1) * kSegLen; ++i) {
+        acc += sE[i * Cfg::kLdE + c];
+        sE[i * Cfg::kLdE + c] = acc;
+      }
+      sSeg[sg * P + c] = acc;
+    }
+    __syncthreads();
+    bool ok = true;
+    {
+      float off = 0.f;
+      for (int s2 = 0; s2 < sg; ++s2) off += sSeg[s2 * P + c];
+#pragma unroll 8
+      for (int i = sg * kSegLen; i < (sg + 1) * kSegLen; ++i) {
+        const float G = (sE[i * Cfg::kLdE + c] + off) * kRcpLn2;
         ok = ok && (G >= -60.f) && (G <= 60.f);
         sE[i * Cfg::kLdE + c] = G;
       }
     }
     fast = __syncthreads_and(ok) != 0;
     if (fast) {
-      for (int idx = tid; idx < kTile * P; idx += Cfg::kThreads) {
-        const int i = idx / P, c = idx % P;
-        const float G = sE[i * Cfg::kLdE + c];
-        sEi[i * Cfg::kLdE + c] = fast_exp2(-G);
-        sE[i * Cfg::kLdE + c] = fast_exp2(G);
+      for (int idx = tid; idx < kTile * P; idx += NT) {
+        const int i = idx / P, cc = idx % P;
+        const float G = sE[i * Cfg::kLdE + cc];
+        sEi[i * Cfg::kLdE + cc] = fast_exp2(-G);
+        sE[i * Cfg::kLdE + cc] = fast_exp2(G);
       }
     }
     __syncthreads();
   }
+  __device__ __forceinline__ float2 ld2(const float* a, int row, int col) const {
+    return *reinterpret_cast<const float2*>(a + row * Cfg::kLdE + col);
+  }
+  // 2^(G_i - G_n) for the channel pair (c, c+1)
+  __device__ __forceinline__ float2 p2d2(int i, int n, int c) const {
+    if (fast) {
+      const float2 e = ld2(sE, i, c), ei = ld2(sEi, n, c);
+      return make_float2(e.x * ei.x, e.y * ei.y);
+    }
+    const float2 gi = ld2(sE, i, c), gn = ld2(sE, n, c);
+    return make_float2(fast_exp2(gi.x - gn.x), fast_exp2(gi.y - gn.y));
+  }
+  __device__ __forceinline__ float2 p22(int i, int c) const {
+    const float2 e = ld2(sE, i, c);
+    if (fast) return e;
+    return make_float2(fast_exp2(e.x), fast_exp2(e.y));
+  }
 
-  // Accumulate this panel's contribution to the key-key scores of the warp's row block.
-  // Warp w: row block r = w/2, n-tiles nt = (w&1), (w&1)+2, ... <= 2r+1.
+  // ---- key-key scores of this panel, accumulated into acc (warp: row block r = w/2,
+  //      n-tiles half, half+2, ..., the diagonal n-tile last) ----
   __device__ void scores_panel(float (&acc)[4][4]) {
     const int r = warp >> 1, half = warp & 1;
     if (16 * r >= len) return;  // whole row block beyond the chunk (chunk_intra.py:242-278)
     const int g = lane >> 2, t = lane & 3;
     const int n_ref = 16 * r;
     const int i0 = n_ref + g, i1 = n_ref + g + 8;
-    const bool v0 = i0 < len, v1 = i1 < len;
-#pragma unroll 2
-    for (int c0 = 0; c0 < P; c0 += 8) {
-      const int ca = c0 + t, cb = c0 + t + 4;
-      // left operand: kb_i 2^(G_i - G_n)   (chunk_intra.py:252-256)
-      float la[4];
-      la[0] = v0 ? kbval(i0, ca) * p2d(i0, n_ref, ca) : 0.f;
-      la[1] = v1 ? kbval(i1, ca) * p2d(i1, n_ref, ca) : 0.f;
-      la[2] = v0 ? kbval(i0, cb) * p2d(i0, n_ref, cb) : 0.f;
-      la[3] = v1 ? kbval(i1, cb) * p2d(i1, n_ref, cb) : 0.f;
-      uint32_t ahi[4], alo[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        ahi[q] = to_tf32(la[q]);
-        alo[q] = to_tf32(la[q] - __uint_as_float(ahi[q]));
-      }
+    float lf0 = 0.f, lf1 = 0.f, rf[4] = {0.f, 0.f, 0.f, 0.f};
+    if constexpr (HEAD) {
+      lf0 = i0 < len ? sLf[i0] : 0.f;
+      lf1 = i1 < len ? sLf[i1] : 0.f;
 #pragma unroll
       for (int s = 0; s < 4; ++s) {
         const int nt = half + 2 * s;
-        if (nt > 2 * r + 1) break;
-        const int j = 8 * nt + g;
-        // right operand: k_j 2^(G_n - G_j)   (chunk_intra.py:253)
-        float rb0 = kval(j, ca) * p2d(n_ref, j, ca);
-        float rb1 = kval(j, cb) * p2d(n_ref, j, cb);
-        uint32_t bhi[2] = {to_tf32(rb0), to_tf32(rb1)};
-        const bool diag = (nt >> 1) == r;
-        if (diag) {
-          if (!fast) continue;  // exact pairwise evaluation below
-          uint32_t blo[2] = {to_tf32(rb0 - __uint_as_float(bhi[0])),
-                             to_tf32(rb1 - __uint_as_float(bhi[1]))};
-          mma_tf32_1688(acc[s], alo, bhi);
-          mma_tf32_1688(acc[s], ahi, blo);
-        }
-        mma_tf32_1688(acc[s], ahi, bhi);
+        if (s < r) rf[s] = sRf[r * kTile + 8 * nt + g];
       }
     }
-    if (!fast) {
-      // diagonal n-tile: exact per-pair exponents, as the token-parallel kernel
-      // (chunk_intra_token_parallel.py:114-123). Lane owns C(g,2t),(g,2t+1),(g+8,2t),(g+8,2t+1).
-      // the diagonal n-tile 2r+half sits at position r of this warp's list
-      const int nt = 2 * r + half;
-      float extra[4];
+#pragma unroll 1
+    for (int kk = 0; kk < P / 16; ++kk) {
+      uint32_t a[4];
+      ldsm_x4(a, smem_u32(sK + xswz<P>(n_ref + (lane & 15), 16 * kk + 8 * (lane >> 4))));
+      uint32_t eb[4] = {0u, 0u, 0u, 0u};
+      if constexpr (ERASE)
+        ldsm_x4(eb, smem_u32(sB + xswz<P>(n_ref + (lane & 15), 16 * kk + 8 * (lane >> 4))));
+      // left operand, fp32, for the two k8 slices: v[slice][reg]
+      float lv[2][4];
+      const int cA = 16 * kk + 2 * t;  // channel of the lo element of a[0]/a[1]
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int i = n_ref + g + ((q & 2) ? 8 : 0);
-        const int j = 8 * nt + 2 * t + (q & 1);
-        float sum = 0.f;
-        if (i < len && j < i) {
-          for (int c = 0; c < P; ++c)
-            sum += kbval(i, c) * kval(j, c) *
-                   fast_exp2(sE[i * Cfg::kLdE + c] - sE[j * Cfg::kLdE + c]);
+      for (int sl = 0; sl < 2; ++sl) {
+        const uint32_t r0 = a[2 * sl], r1 = a[2 * sl + 1];  // rows g / g+8
+        float x0 = bf_lo(r0), x1 = bf_hi(r0), x2 = bf_lo(r1), x3 = bf_hi(r1);
+        if constexpr (ERASE) {
+          x0 *= bf_lo(eb[2 * sl]);
+          x1 *= bf_hi(eb[2 * sl]);
+          x2 *= bf_lo(eb[2 * sl + 1]);
+          x3 *= bf_hi(eb[2 * sl + 1]);
         }
-        extra[q] = sum;
+        if constexpr (HEAD) {
+          lv[sl][0] = x0 * lf0;  // (row g,   k-slot t)
+          lv[sl][1] = x2 * lf1;  // (row g+8, k-slot t)
+          lv[sl][2] = x1 * lf0;  // (row g,   k-slot t+4)
+          lv[sl][3] = x3 * lf1;  // (row g+8, k-slot t+4)
+        } else {
+          const int c = cA + 8 * sl;
+          const float2 f0 = p2d2(i0, n_ref, c), f1 = p2d2(i1, n_ref, c);
+          lv[sl][0] = i0 < len ? x0 * f0.x : 0.f;
+          lv[sl][1] = i1 < len ? x2 * f1.x : 0.f;
+          lv[sl][2] = i0 < len ? x1 * f0.y : 0.f;
+          lv[sl][3] = i1 < len ? x3 * f1.y : 0.f;
+        }
       }
 #pragma unroll
-      for (int s = 0; s < 4; ++s)
-        if (s == r)
+      for (int s = 0; s < 4; ++s) {
+        if (s > r) break;
+        const int nt = half + 2 * s;
+        const bool diag = (s == r);
+        uint32_t bq[2];
+        ldsm_x2(bq, smem_u32(sK + xswz<P>(8 * nt + (lane & 7), 16 * kk + 8 * ((lane >> 3) & 1))));
+        if constexpr (HEAD) {
+          if (diag) {
+            // exact bf16 products; the per-pair exponent is applied after the sum
+            uint32_t af[4] = {a[0], a[1], a[2], a[3]};
+            if constexpr (ERASE) {
 #pragma unroll
-          for (int q = 0; q < 4; ++q) acc[s][q] += extra[q];
+              for (int q = 0; q < 4; ++q)
+                af[q] = pack_bf16x2(bf_lo(a[q]) * bf_lo(eb[q]), bf_hi(a[q]) * bf_hi(eb[q]));
+            }
+            // with an erase factor the fp32 product kb = k*b (16 significant bits) is split
+            // into bf16 hi + lo parts, so the two bf16 products sum to the exact fp32 value
+            mma_bf16_16816(acc[s], af, bq);
+            if constexpr (ERASE) {
+              uint32_t lo[4];
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const float p0 = bf_lo(a[q]) * bf_lo(eb[q]), p1 = bf_hi(a[q]) * bf_hi(eb[q]);
+                lo[q] = pack_bf16x2(p0 - bf_lo(af[q]), p1 - bf_hi(af[q]));
+              }
+              mma_bf16_16816(acc[s], lo, bq);
+            }
+            continue;
+          }
+#pragma unroll
+          for (int sl = 0; sl < 2; ++sl) {
+            const uint32_t rb = bq[sl];
+            uint32_t bb[2] = {to_tf32(bf_lo(rb) * rf[s]), to_tf32(bf_hi(rb) * rf[s])};
+            uint32_t aa[4] = {to_tf32(lv[sl][0]), to_tf32(lv[sl][1]), to_tf32(lv[sl][2]), to_tf32(lv[sl][3])};
+            mma_tf32_1688(acc[s], aa, bb);
+          }
+        } else {
+          const int j = 8 * nt + g;
+#pragma unroll
+          for (int sl = 0; sl < 2; ++sl) {
+            const int c = cA + 8 * sl;
+            const float2 f = p2d2(n_ref, j, c);
+            const float y0 = bf_lo(bq[sl]) * f.x, y1 = bf_hi(bq[sl]) * f.y;
+            uint32_t bh[2] = {to_tf32(y0), to_tf32(y1)};
+            uint32_t ah[4] = {to_tf32(lv[sl][0]), to_tf32(lv[sl][1]), to_tf32(lv[sl][2]), to_tf32(lv[sl][3])};
+            if (diag) {
+              if (!fast) continue;  // exact pairwise evaluation below
+              uint32_t bl[2] = {to_tf32(y0 - __uint_as_float(bh[0])), to_tf32(y1 - __uint_as_float(bh[1]))};
+              uint32_t al[4];
+#pragma unroll
+              for (int q = 0; q < 4; ++q) al[q] = to_tf32(lv[sl][q] - __uint_as_float(ah[q]));
+              mma_tf32_1688(acc[s], al, bh);
+              mma_tf32_1688(acc[s], ah, bl);
+            }
+            mma_tf32_1688(acc[s], ah, bh);
+          }
+        }
+      }
+    }
+    if constexpr (!HEAD) {
+      if (!fast) {
+        // diagonal n-tile with exact per-pair exponents (chunk_intra_token_parallel.py:114-123)
+        const int nt = 2 * r + half;
+        float extra[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int i = n_ref + g + ((q & 2) ? 8 : 0);
+          const int j = 8 * nt + 2 * t + (q & 1);
+          float sum = 0.f;
+          if (i < len && j < i) {
+            for (int c = 0; c < P; ++c) {
+              float kb = __bfloat162float(sK[xswz<P>(i, c)]);
+              if constexpr (ERASE) kb *= __bfloat162float(sB[xswz<P>(i, c)]);
+              sum += kb * __bfloat162float(sK[xswz<P>(j, c)]) *
+                     fast_exp2(sE[i * Cfg::kLdE + c] - sE[j * Cfg::kLdE + c]);
+            }
+          }
+          extra[q] = sum;
+        }
+#pragma unroll
+        for (int s = 0; s < 4; ++s)
+          if (s == r)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) acc[s][q] += extra[q];
+      }
     }
   }
 
-  // Write the score accumulators to sA (strictly lower on the diagonal blocks).
+  // scores -> sA (strictly lower on the diagonal blocks; per-head diagonal scaled by 2^(G_i-G_j))
   __device__ void store_scores(const float (&acc)[4][4]) {
     const int r = warp >> 1, half = warp & 1;
     const int g = lane >> 2, t = lane & 3;
 #pragma unroll
     for (int s = 0; s < 4; ++s) {
+      if (s > r) break;
       const int nt = half + 2 * s;
-      if (nt > 2 * r + 1) break;
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const int i = 16 * r + g + ((q & 2) ? 8 : 0);
         const int j = 8 * nt + 2 * t + (q & 1);
         float x = acc[s][q];
+        if constexpr (HEAD) {
+          if (s == r) x = (j < i && i < len) ? x * fast_exp2(sG[i] - sG[j]) : 0.f;
+        }
         if (j >= i || i >= len) x = 0.f;
         sA[i * Cfg::kLdA + j] = x;
       }
     }
   }
 
-  // Blocked inverse of (I + A) in place (chunk_intra.py:326-395). Diagonal inverse
-  // blocks stay on the diagonal; the off-diagonal inverse block (r, s), r > s, is kept
-  // in the unused upper slot (s, r) as a plain 16x16 matrix.
+  // Blocked inverse of (I + A) (chunk_intra.py:326-395). fp32 blocks stay in sA (diagonal
+  // in place, off-diagonal (r, s) in the unused upper slot (s, r)); every finished block is
+  // also written as bf16 into sAi (rows >= len zero).
   __device__ void solve() {
-    constexpr int LD = Cfg::kLdA;
-    // forward substitution on the four diagonal blocks, warp r handles block r
+    constexpr int LD = Cfg::kLdA, LDI = Cfg::kLdAi;
     if (warp < 4) {
       const int r = warp;
       const int c = lane & 15;
@@ -304,104 +445,110 @@ struct IntraKernel {
 #pragma unroll
       for (int i = 2; i < 16; ++i) {
         const float a = (c < i) ? -blk[i * LD + c] : 0.f;
-        float s = a;
+        float s0 = a, s1 = 0.f;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const float aj = __shfl_sync(0xffffffffu, a, j);
-          if (j < i) s = fmaf(aj, x[j], s);
+        for (int j = 0; j < 16; j += 2) {
+          const float aj0 = __shfl_sync(0xffffffffu, a, j);
+          const float aj1 = __shfl_sync(0xffffffffu, a, j + 1);
+          if (j < i) s0 = fmaf(aj0, x[j], s0);
+          if (j + 1 < i) s1 = fmaf(aj1, x[j + 1], s1);
         }
-        x[i] = s;
+        x[i] = s0 + s1;
       }
       __syncwarp();
       if (lane < 16) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) blk[j * LD + c] = x[j] + (j == c ? 1.f : 0.f);
+        for (int j = 0; j < 16; ++j) {
+          const float v = x[j] + (j == c ? 1.f : 0.f);
+          blk[j * LD + c] = v;
+          sAi[(16 * r + j) * LDI + 16 * r + c] = __float2bfloat16_rn((16 * r + j < len) ? v : 0.f);
+        }
       }
     }
     __syncthreads();
-    auto D_ = [&](int r) { return sA + (16 * r) * LD + 16 * r; };          // Ai_rr
-    auto Ak = [&](int r, int s) { return sA + (16 * r) * LD + 16 * s; };   // Akk_rs, r > s
-    auto Ao = [&](int r, int s) { return sA + (16 * s) * LD + 16 * r; };   // Ai_rs stored at (s, r)
+    auto Dg = [&](int r) { return sA + (16 * r) * LD + 16 * r; };         // Ai_rr
+    auto Ak = [&](int r, int s) { return sA + (16 * r) * LD + 16 * s; };  // Akk_rs, r > s
+    auto Ao = [&](int r, int s) { return sA + (16 * s) * LD + 16 * r; };  // Ai_rs kept at (s, r)
+    auto Ab = [&](int r, int s) { return sAi + (16 * r) * LDI + 16 * s; };
     float acc[2][4];
-    // stage 1: Ai_{s+1,s} = -(Ai_{s+1,s+1} Akk_{s+1,s}) Ai_{s,s}
-    if (warp < 3) {
+    if (warp < 3) {  // Ai_{s+1,s} = -(Ai_{s+1,s+1} Akk_{s+1,s}) Ai_{s,s}
       const int s = warp;
-      // scratch: slots (0,2), (1,3), (0,3) are free until stages 2-3
       float* tmp = (s == 0) ? Ao(2, 0) : (s == 1) ? Ao(3, 1) : Ao(3, 0);
       zero_acc(acc);
-      warp_tf32_16x16x16(acc, D_(s + 1), LD, Ak(s + 1, s), LD, lane);
-      warp_store_16x16(tmp, LD, acc, lane, 1.f);
+      warp_tf32_16x16x16(acc, Dg(s + 1), LD, Ak(s + 1, s), LD, lane);
+      {
+        const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          *reinterpret_cast<float2*>(tmp + g * LD + nt * 8 + 2 * t) = make_float2(acc[nt][0], acc[nt][1]);
+          *reinterpret_cast<float2*>(tmp + (g + 8) * LD + nt * 8 + 2 * t) = make_float2(acc[nt][2], acc[nt][3]);
+        }
+      }
       __syncwarp();
       zero_acc(acc);
-      warp_tf32_16x16x16(acc, tmp, LD, D_(s), LD, lane);
-      warp_store_16x16(Ao(s + 1, s), LD, acc, lane, -1.f);
+      warp_tf32_16x16x16(acc, tmp, LD, Dg(s), LD, lane);
+      warp_store_block(Ao(s + 1, s), LD, Ab(s + 1, s), LDI, acc, lane, -1.f, 16 * (s + 1), len);
     }
     __syncthreads();
-    // stage 2: Ai20 = -Ai22 (Akk20 Ai00 + Akk21 Ai10); Ai31 = -Ai33 (Akk31 Ai11 + Akk32 Ai21)
-    if (warp < 2) {
-      const int r = warp + 2;  // 2 or 3
+    if (warp < 2) {  // Ai20, Ai31
+      const int r = warp + 2;
       float* dst = Ao(r, r - 2);
       zero_acc(acc);
-      warp_tf32_16x16x16(acc, Ak(r, r - 2), LD, D_(r - 2), LD, lane);
+      warp_tf32_16x16x16(acc, Ak(r, r - 2), LD, Dg(r - 2), LD, lane);
       warp_tf32_16x16x16(acc, Ak(r, r - 1), LD, Ao(r - 1, r - 2), LD, lane);
-      warp_store_16x16(dst, LD, acc, lane, 1.f);
+      {
+        const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          *reinterpret_cast<float2*>(dst + g * LD + nt * 8 + 2 * t) = make_float2(acc[nt][0], acc[nt][1]);
+          *reinterpret_cast<float2*>(dst + (g + 8) * LD + nt * 8 + 2 * t) = make_float2(acc[nt][2], acc[nt][3]);
+        }
+      }
       __syncwarp();
       zero_acc(acc);
-      warp_tf32_16x16x16(acc, D_(r), LD, dst, LD, lane);
+      warp_tf32_16x16x16(acc, Dg(r), LD, dst, LD, lane);
       __syncwarp();
-      warp_store_16x16(dst, LD, acc, lane, -1.f);
+      warp_store_block(dst, LD, Ab(r, r - 2), LDI, acc, lane, -1.f, 16 * r, len);
     }
     __syncthreads();
-    // stage 3: Ai30 = -Ai33 (Akk30 Ai00 + Akk31 Ai10 + Akk32 Ai20)
-    if (warp == 0) {
+    if (warp == 0) {  // Ai30
       float* dst = Ao(3, 0);
       zero_acc(acc);
-      warp_tf32_16x16x16(acc, Ak(3, 0), LD, D_(0), LD, lane);
+      warp_tf32_16x16x16(acc, Ak(3, 0), LD, Dg(0), LD, lane);
       warp_tf32_16x16x16(acc, Ak(3, 1), LD, Ao(1, 0), LD, lane);
       warp_tf32_16x16x16(acc, Ak(3, 2), LD, Ao(2, 0), LD, lane);
-      warp_store_16x16(dst, LD, acc, lane, 1.f);
+      {
+        const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          *reinterpret_cast<float2*>(dst + g * LD + nt * 8 + 2 * t) = make_float2(acc[nt][0], acc[nt][1]);
+          *reinterpret_cast<float2*>(dst + (g + 8) * LD + nt * 8 + 2 * t) = make_float2(acc[nt][2], acc[nt][3]);
+        }
+      }
       __syncwarp();
       zero_acc(acc);
-      warp_tf32_16x16x16(acc, D_(3), LD, dst, LD, lane);
-      __syncwarp();
-      warp_store_16x16(dst, LD, acc, lane, -1.f);
-    }
-    __syncthreads();
-    // A^-1 -> bf16, rows beyond the chunk zero (chunk_intra.py:408-417)
-    for (int idx = tid; idx < kTile * kTile; idx += Cfg::kThreads) {
-      const int i = idx / kTile, j = idx % kTile;
-      const int r = i >> 4, s = j >> 4;
-      float x = 0.f;
-      if (i < len) {
-        if (r == s)
-          x = (j <= i) ? sA[i * LD + j] : 0.f;
-        else if (r > s)
-          x = sA[(16 * s + (i & 15)) * LD + 16 * r + (j & 15)];
-      }
-      sAi[i * Cfg::kLdAi + j] = __float2bfloat16_rn(x);
+      warp_tf32_16x16x16(acc, Dg(3), LD, dst, LD, lane);
+      warp_store_block(nullptr, LD, Ab(3, 0), LDI, acc, lane, -1.f, 48, len);
     }
     __syncthreads();
   }
 
-  // out[64][P] (bf16, global rows of stride ld) = A^-1 (64x64 lower) . sX (64 x P).
-  // Warp w: row block r = w/2, column half (w&1) of the panel; k-steps 0..r only.
-  __device__ void wy_product(__nv_bfloat16* out, int64_t ld) {
+  // sO (swizzled [64][P]) = A^-1 (lower) . sX (swizzled [64][P]); warp w: row block w/2,
+  // column half w&1, k-steps 0..r only.
+  __device__ void wy_product() {
     const int r = warp >> 1, half = warp & 1;
-    constexpr int NT = P / 16;  // n-tiles per warp (half of P / 8)
-    float acc[NT][4];
+    constexpr int NTW = P / 16;
+    float acc[NTW][4];
 #pragma unroll
-    for (int i = 0; i < NT; ++i)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+    for (int i = 0; i < NTW; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
     const int n_base = half * (P / 2);
     for (int ks = 0; ks <= r; ++ks) {
       uint32_t a[4];
       ldsm_x4(a, smem_u32(sAi + (16 * r + (lane & 15)) * Cfg::kLdAi + 16 * ks + 8 * (lane >> 4)));
 #pragma unroll
-      for (int np = 0; np < NT; np += 2) {
+      for (int np = 0; np < NTW; np += 2) {
         uint32_t b[4];
-        ldsm_x4_t(b, smem_u32(sX + (16 * ks + (lane & 15)) * Cfg::kLdK + n_base + 8 * np +
-                              8 * (lane >> 4)));
+        ldsm_x4_t(b, smem_u32(sX + xswz<P>(16 * ks + (lane & 15), n_base + 8 * np + 8 * (lane >> 4))));
         uint32_t b0[2] = {b[0], b[1]}, b1[2] = {b[2], b[3]};
         mma_bf16_16816(acc[np], a, b0);
         mma_bf16_16816(acc[np + 1], a, b1);
@@ -409,12 +556,21 @@ struct IntraKernel {
     }
     const int g = lane >> 2, t = lane & 3;
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
+    for (int nt = 0; nt < NTW; ++nt) {
       const int col = n_base + 8 * nt + 2 * t;
       const int i0 = 16 * r + g;
-      *reinterpret_cast<uint32_t*>(out + (int64_t)i0 * ld + col) = pack_bf16x2(acc[nt][0], acc[nt][1]);
-      *reinterpret_cast<uint32_t*>(out + (int64_t)(i0 + 8) * ld + col) =
-          pack_bf16x2(acc[nt][2], acc[nt][3]);
+      *reinterpret_cast<uint32_t*>(sO + xswz<P>(i0, col)) = pack_bf16x2(acc[nt][0], acc[nt][1]);
+      *reinterpret_cast<uint32_t*>(sO + xswz<P>(i0 + 8, col)) = pack_bf16x2(acc[nt][2], acc[nt][3]);
+    }
+  }
+
+  // swizzled sO -> global [64][D] rows (columns c0..c0+P), 16-byte coalesced stores
+  __device__ void store_tile(__nv_bfloat16* out, int c0) {
+    constexpr int kChunks = kTile * P / 8;
+#pragma unroll
+    for (int i = tid; i < kChunks; i += NT) {
+      const int row = i / (P / 8), col = (i % (P / 8)) * 8;
+      *reinterpret_cast<uint4*>(out + row * D + c0 + col) = *reinterpret_cast<const uint4*>(sO + xswz<P>(row, col));
     }
   }
 
@@ -427,6 +583,36 @@ struct IntraKernel {
     h = blockIdx.y;
     row_stride = (int64_t)p.H * D;
     const int64_t chunk_head = (int64_t)c * p.H + h;
+    __nv_bfloat16* gW = p.W + chunk_head * kTile * D;
+    __nv_bfloat16* gU = p.U + chunk_head * kTile * D;
+    __nv_bfloat16* gKG = p.KG + chunk_head * kTile * D;
+    float* gEl = p.Elast + chunk_head * D;
+
+    // ---- stage the first panel: k (+erase), v, w, per-channel decay ----
+    auto load_decay = [&](int c0) {
+      const float* base = p.g + (int64_t)tok0 * row_stride + (int64_t)h * D + c0;
+      constexpr int kChunks = kTile * P / 4;
+#pragma unroll
+      for (int i = tid; i < kChunks; i += NT) {
+        const int row = i / (P / 4), col = (i % (P / 4)) * 4;
+        const bool valid = row < len;
+        cp_async16_zfill(sE + row * Cfg::kLdE + col, valid ? base + (int64_t)row * row_stride + col : p.g, valid);
+      }
+    };
+    auto load_key_panel = [&](int c0) {
+      load_tile(sK, p.k, c0);
+      if constexpr (ERASE) load_tile(sB, p.erase, c0);
+      if constexpr (!HEAD) load_decay(c0);
+    };
+    auto load_value_panel = [&](int c0) {
+      load_tile(sV, p.v, c0);
+      if (p.write != nullptr) load_tile(sW, p.write, c0);
+    };
+    load_key_panel(0);
+    cp_async_commit();
+    load_value_panel(0);
+    cp_async_commit();
+    if constexpr (HEAD) head_factors(p);
 
     float acc[4][4];
 #pragma unroll
@@ -434,101 +620,161 @@ struct IntraKernel {
 #pragma unroll
       for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
 
-    // ---- key-key scores over all channel panels ----
-    for (int pn = 0; pn < Cfg::kPanels; ++pn) {
-      load_panel(p, pn * P);
-      scores_panel(acc);
+    auto prepare_key_panel = [&](int c0) {  // after the key panel landed
       __syncthreads();
+      if (p.beta_layout != 0) {
+        fold_beta(p, c0);
+        __syncthreads();
+      }
+      if constexpr (!HEAD) channel_tables();
+    };
+
+    // ---- key-key scores over the channel panels ----
+    for (int pn = 0; pn < Cfg::kPanels; ++pn) {
+      if (pn > 0) {
+        __syncthreads();
+        load_key_panel(pn * P);
+        cp_async_commit();
+        cp_async_wait<0>();
+      } else {
+        cp_async_wait<1>();
+      }
+      prepare_key_panel(pn * P);
+      scores_panel(acc);
     }
+    __syncthreads();
     store_scores(acc);
     __syncthreads();
     solve();
 
-    // ---- w and kg per channel panel ----
+    // ---- w, kg and 2^G_last per channel panel ----
     const int last = len - 1;
     for (int pn = 0; pn < Cfg::kPanels; ++pn) {
       const int c0 = pn * P;
-      if (Cfg::kPanels > 1) load_panel(p, c0);
+      if (Cfg::kPanels > 1) {
+        load_key_panel(c0);
+        cp_async_commit();
+        cp_async_wait<0>();
+        prepare_key_panel(c0);
+      }
       // staging operand bf16( bf16(k*b) * 2^G )   (wy_fast.py:110-116)
-      for (int idx = tid; idx < kTile * P; idx += Cfg::kThreads) {
-        const int i = idx / P, cc = idx % P;
-        float kb = kval(i, cc);
-        if constexpr (ERASE) kb = bf16_round(kb * __bfloat162float(sB[i * Cfg::kLdK + cc]));
-        sX[i * Cfg::kLdK + cc] = __float2bfloat16_rn(kb * p2(i, cc));
-      }
-      // kg = bf16(k * 2^(G_last - G)) (wy_fast.py:125-139) and 2^G_last
-      __nv_bfloat16* kg = p.KG + chunk_head * kTile * D + c0;
-      for (int idx = tid; idx < kTile * P / 2; idx += Cfg::kThreads) {
-        const int i = idx / (P / 2), cc = (idx % (P / 2)) * 2;
-        float x0 = 0.f, x1 = 0.f;
-        if (i < len) {
-          x0 = kval(i, cc) * p2d(last, i, cc);
-          x1 = kval(i, cc + 1) * p2d(last, i, cc + 1);
+      constexpr int kChunks = kTile * P / 8;
+      for (int i = tid; i < kChunks; i += NT) {
+        const int row = i / (P / 8), col = (i % (P / 8)) * 8;
+        uint4 kv = *reinterpret_cast<const uint4*>(sK + xswz<P>(row, col));
+        uint32_t* kw = reinterpret_cast<uint32_t*>(&kv);
+        uint4 kgv;
+        uint32_t* kgw = reinterpret_cast<uint32_t*>(&kgv);
+        if constexpr (ERASE) {
+          const uint4 bv = *reinterpret_cast<const uint4*>(sB + xswz<P>(row, col));
+          const uint32_t* bw = reinterpret_cast<const uint32_t*>(&bv);
+          // kg uses k, the w operand uses bf16(k*b)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float k0 = bf_lo(kw[e]), k1 = bf_hi(kw[e]);
+            float e0, e1, q0, q1;
+            if constexpr (HEAD) {
+              e0 = e1 = sEh[row];
+              q0 = q1 = sKgf[row];
+            } else {
+              const float2 ev = p22(row, col + 2 * e), qv = p2d2(last, row, col + 2 * e);
+              e0 = ev.x; e1 = ev.y;
+              q0 = row < len ? qv.x : 0.f;
+              q1 = row < len ? qv.y : 0.f;
+            }
+            kgw[e] = pack_bf16x2(k0 * q0, k1 * q1);
+            kw[e] = pack_bf16x2(bf16_round(k0 * bf_lo(bw[e])) * e0, bf16_round(k1 * bf_hi(bw[e])) * e1);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float k0 = bf_lo(kw[e]), k1 = bf_hi(kw[e]);
+            float e0, e1, q0, q1;
+            if constexpr (HEAD) {
+              e0 = e1 = sEh[row];
+              q0 = q1 = sKgf[row];
+            } else {
+              const float2 ev = p22(row, col + 2 * e), qv = p2d2(last, row, col + 2 * e);
+              e0 = ev.x; e1 = ev.y;
+              q0 = row < len ? qv.x : 0.f;
+              q1 = row < len ? qv.y : 0.f;
+            }
+            kgw[e] = pack_bf16x2(k0 * q0, k1 * q1);
+            kw[e] = pack_bf16x2(k0 * e0, k1 * e1);
+          }
         }
-        *reinterpret_cast<uint32_t*>(kg + (int64_t)i * D + cc) = pack_bf16x2(x0, x1);
+        *reinterpret_cast<uint4*>(sX + xswz<P>(row, col)) = kv;
+        *reinterpret_cast<uint4*>(gKG + row * D + c0 + col) = kgv;  // wy_fast.py:125-139
       }
-      if (tid < P) p.Elast[chunk_head * D + c0 + tid] = p2(last, tid);
+      if (tid < P) {
+        if constexpr (HEAD)
+          gEl[c0 + tid] = sSeg[0];
+        else
+          gEl[c0 + tid] = fast ? sE[last * Cfg::kLdE + tid] : fast_exp2(sE[last * Cfg::kLdE + tid]);
+      }
       __syncthreads();
-      wy_product(p.W + chunk_head * kTile * D + c0, D);
+      wy_product();
       __syncthreads();
+      store_tile(gW, c0);
     }
 
     // ---- u per value panel: A^-1 bf16(v * w)   (wy_fast.py:92-102) ----
     for (int pn = 0; pn < Cfg::kPanels; ++pn) {
       const int c0 = pn * P;
-      const int64_t base = (int64_t)tok0 * row_stride + (int64_t)h * D + c0;
-      constexpr int kVecPerRow = P / 8;
-      for (int idx = tid; idx < kTile * kVecPerRow; idx += Cfg::kThreads) {
-        const int i = idx / kVecPerRow, cv = (idx % kVecPerRow) * 8;
-        uint4 vv = make_uint4(0, 0, 0, 0);
-        if (i < len) {
-          const int64_t off = base + (int64_t)i * row_stride + cv;
-          vv = *reinterpret_cast<const uint4*>(p.v + off);
-          if (p.write != nullptr) {
-            uint4 ww = *reinterpret_cast<const uint4*>(p.write + off);
-            uint32_t* vw = reinterpret_cast<uint32_t*>(&vv);
-            const uint32_t* wg = reinterpret_cast<const uint32_t*>(&ww);
+      if (pn > 0) {
+        load_value_panel(c0);
+        cp_async_commit();
+      }
+      cp_async_wait<0>();
+      __syncthreads();
+      constexpr int kChunks = kTile * P / 8;
+      for (int i = tid; i < kChunks; i += NT) {
+        const int row = i / (P / 8), col = (i % (P / 8)) * 8;
+        uint4 vv = *reinterpret_cast<const uint4*>(sV + xswz<P>(row, col));
+        if (p.write != nullptr) {
+          const uint4 ww = *reinterpret_cast<const uint4*>(sW + xswz<P>(row, col));
+          uint32_t* vw = reinterpret_cast<uint32_t*>(&vv);
+          const uint32_t* wg = reinterpret_cast<const uint32_t*>(&ww);
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              float2 a = unpack_bf16x2(vw[e]), b = unpack_bf16x2(wg[e]);
-              vw[e] = pack_bf16x2(a.x * b.x, a.y * b.y);
-            }
-          }
+          for (int e = 0; e < 4; ++e) vw[e] = pack_bf16x2(bf_lo(vw[e]) * bf_lo(wg[e]), bf_hi(vw[e]) * bf_hi(wg[e]));
         }
-        *reinterpret_cast<uint4*>(sX + i * Cfg::kLdK + cv) = vv;
+        *reinterpret_cast<uint4*>(sX + xswz<P>(row, col)) = vv;
       }
       __syncthreads();
-      wy_product(p.U + chunk_head * kTile * D + c0, D);
+      wy_product();
       __syncthreads();
+      store_tile(gU, c0);
     }
   }
 };
 
-template <int D, bool ERASE>
+template <int D, bool HEAD, bool ERASE>
 __global__ void __launch_bounds__(256) intra_kernel(IntraParams p) {
   extern __shared__ __align__(128) unsigned char smem_intra[];
-  using Cfg = IntraCfg<D>;
-  IntraKernel<D, ERASE> k;
-  unsigned char* ptr = smem_intra;
-  k.sE = reinterpret_cast<float*>(ptr);
-  ptr += Cfg::kBytesE;
-  k.sEi = reinterpret_cast<float*>(ptr);
-  ptr += Cfg::kBytesE;
-  k.sK = reinterpret_cast<__nv_bfloat16*>(ptr);
-  ptr += Cfg::kBytesK;
-  if constexpr (ERASE) {
-    k.sB = reinterpret_cast<__nv_bfloat16*>(ptr);
-    ptr += Cfg::kBytesK;
-  } else {
-    k.sB = nullptr;
-  }
-  k.sA = reinterpret_cast<float*>(ptr);
-  k.sX = reinterpret_cast<__nv_bfloat16*>(ptr);
-  ptr += Cfg::kBytesA;
-  k.sAi = reinterpret_cast<__nv_bfloat16*>(ptr);
+  using Cfg = IntraCfg<D, HEAD, ERASE>;
+  IntraKernel<D, HEAD, ERASE> k;
+  unsigned char* base = smem_intra;
+  k.sK = reinterpret_cast<__nv_bfloat16*>(base + Cfg::offK);
+  k.sB = reinterpret_cast<__nv_bfloat16*>(base + Cfg::offB);
+  k.sV = reinterpret_cast<__nv_bfloat16*>(base + Cfg::offV);
+  k.sW = reinterpret_cast<__nv_bfloat16*>(base + Cfg::offW);
+  k.sO = reinterpret_cast<__nv_bfloat16*>(base + Cfg::offO);
+  k.sE = reinterpret_cast<float*>(base + Cfg::offE);
+  k.sEi = reinterpret_cast<float*>(base + Cfg::offEi);
+  k.sA = reinterpret_cast<float*>(base + Cfg::offA);
+  k.sX = reinterpret_cast<__nv_bfloat16*>(base + Cfg::offA);
+  k.sAi = reinterpret_cast<__nv_bfloat16*>(base + Cfg::offAi);
+  __shared__ float s_small[kTile * 8 + Cfg::kThreads];
+  k.sG = s_small;
+  k.sLf = s_small + kTile;
+  k.sEh = s_small + 2 * kTile;
+  k.sKgf = s_small + 3 * kTile;
+  k.sRf = s_small + 4 * kTile;  // [4][64]
+  k.sSeg = s_small + 8 * kTile;
   k.tid = threadIdx.x;
   k.lane = threadIdx.x & 31;
   k.warp = threadIdx.x >> 5;
+  k.fast = true;
   k.run(p);
 }
 
