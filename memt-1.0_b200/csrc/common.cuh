@@ -113,6 +113,49 @@ __device__ __forceinline__ void cp_async_wait() {
 }
 
 // ---------------------------------------------------------------------------
+// mbarrier + bulk (TMA, untiled) copies global -> shared. No cluster multicast anywhere.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint32_t mbar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(mbar), "r"(count));
+}
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;\n" ::);
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t mbar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(mbar), "r"(bytes));
+}
+// Bounded wait for the phase with the given parity; false after ~2^24 polls (seconds).
+__device__ __forceinline__ bool mbar_wait(uint32_t mbar, uint32_t parity) {
+  for (int i = 0; i < (1 << 24); ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(mbar), "r"(parity)
+        : "memory");
+    if (ok) return true;
+  }
+  return false;
+}
+// 1-D bulk copy; addresses 16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t mbar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(mbar)
+      : "memory");
+}
+
+// XOR-swizzled bf16 tile with RL elements per row (RL % 64 == 0): the low three bits of the
+// 16-byte chunk index are XORed with (row & 7), so ldmatrix over 8 consecutive rows and
+// fragment-wise 4-byte accesses are bank-conflict free. The intra kernel writes its outputs in
+// this layout so the scan can move whole tiles with one bulk copy.
+template <int RL>
+__device__ __forceinline__ int swz(int row, int col) {
+  return row * RL + ((((col >> 3) ^ row) & 7) | ((col >> 3) & ~7)) * 8 + (col & 7);
+}
+
+// ---------------------------------------------------------------------------
 // chunk table entry written by the plan kernel
 // ---------------------------------------------------------------------------
 struct ChunkDesc {
@@ -165,7 +208,7 @@ struct IntraParams {
 };
 
 struct ScanParams {
-  const WsHeader* hdr;
+  WsHeader* hdr;
   const int32_t* sample_off;  // [N+1] chunk offsets per sample
   int32_t N, H;
   const __nv_bfloat16* W;

@@ -36,11 +36,6 @@
 
 namespace memt {
 
-template <int RL>
-__device__ __forceinline__ int xswz(int row, int col) {
-  return row * RL + ((((col >> 3) ^ row) & 7) | ((col >> 3) & ~7)) * 8 + (col & 7);
-}
-
 template <int D, bool HEAD, bool ERASE>
 struct IntraCfg {
   static constexpr int kPanel = D < 128 ? D : 128;
@@ -144,7 +139,7 @@ struct IntraKernel {
     for (int i = tid; i < kChunks; i += NT) {
       const int row = i / (P / 8), col = (i % (P / 8)) * 8;
       const bool valid = row < len;
-      cp_async16_zfill(dst + xswz<P>(row, col), valid ? base + (int64_t)row * row_stride + col : src, valid);
+      cp_async16_zfill(dst + swz<P>(row, col), valid ? base + (int64_t)row * row_stride + col : src, valid);
     }
   }
 
@@ -154,7 +149,7 @@ struct IntraKernel {
     for (int i = tid; i < kChunks; i += NT) {
       const int row = i / (P / 8), col = (i % (P / 8)) * 8;
       if (row >= len) continue;
-      uint4* ptr = reinterpret_cast<uint4*>(sK + xswz<P>(row, col));
+      uint4* ptr = reinterpret_cast<uint4*>(sK + swz<P>(row, col));
       uint4 kv = *ptr;
       float sb[8];
       if (p.beta_layout == 1) {
@@ -288,10 +283,10 @@ struct IntraKernel {
 #pragma unroll 1
     for (int kk = 0; kk < P / 16; ++kk) {
       uint32_t a[4];
-      ldsm_x4(a, smem_u32(sK + xswz<P>(n_ref + (lane & 15), 16 * kk + 8 * (lane >> 4))));
+      ldsm_x4(a, smem_u32(sK + swz<P>(n_ref + (lane & 15), 16 * kk + 8 * (lane >> 4))));
       uint32_t eb[4] = {0u, 0u, 0u, 0u};
       if constexpr (ERASE)
-        ldsm_x4(eb, smem_u32(sB + xswz<P>(n_ref + (lane & 15), 16 * kk + 8 * (lane >> 4))));
+        ldsm_x4(eb, smem_u32(sB + swz<P>(n_ref + (lane & 15), 16 * kk + 8 * (lane >> 4))));
       // left operand, fp32, for the two k8 slices: v[slice][reg]
       float lv[2][4];
       const int cA = 16 * kk + 2 * t;  // channel of the lo element of a[0]/a[1]
@@ -325,7 +320,7 @@ struct IntraKernel {
         const int nt = half + 2 * s;
         const bool diag = (s == r);
         uint32_t bq[2];
-        ldsm_x2(bq, smem_u32(sK + xswz<P>(8 * nt + (lane & 7), 16 * kk + 8 * ((lane >> 3) & 1))));
+        ldsm_x2(bq, smem_u32(sK + swz<P>(8 * nt + (lane & 7), 16 * kk + 8 * ((lane >> 3) & 1))));
         if constexpr (HEAD) {
           if (diag) {
             // exact bf16 products; the per-pair exponent is applied after the sum
@@ -391,9 +386,9 @@ struct IntraKernel {
           float sum = 0.f;
           if (i < len && j < i) {
             for (int c = 0; c < P; ++c) {
-              float kb = __bfloat162float(sK[xswz<P>(i, c)]);
-              if constexpr (ERASE) kb *= __bfloat162float(sB[xswz<P>(i, c)]);
-              sum += kb * __bfloat162float(sK[xswz<P>(j, c)]) *
+              float kb = __bfloat162float(sK[swz<P>(i, c)]);
+              if constexpr (ERASE) kb *= __bfloat162float(sB[swz<P>(i, c)]);
+              sum += kb * __bfloat162float(sK[swz<P>(j, c)]) *
                      fast_exp2(sE[i * Cfg::kLdE + c] - sE[j * Cfg::kLdE + c]);
             }
           }
@@ -548,7 +543,7 @@ struct IntraKernel {
 #pragma unroll
       for (int np = 0; np < NTW; np += 2) {
         uint32_t b[4];
-        ldsm_x4_t(b, smem_u32(sX + xswz<P>(16 * ks + (lane & 15), n_base + 8 * np + 8 * (lane >> 4))));
+        ldsm_x4_t(b, smem_u32(sX + swz<P>(16 * ks + (lane & 15), n_base + 8 * np + 8 * (lane >> 4))));
         uint32_t b0[2] = {b[0], b[1]}, b1[2] = {b[2], b[3]};
         mma_bf16_16816(acc[np], a, b0);
         mma_bf16_16816(acc[np + 1], a, b1);
@@ -559,18 +554,31 @@ struct IntraKernel {
     for (int nt = 0; nt < NTW; ++nt) {
       const int col = n_base + 8 * nt + 2 * t;
       const int i0 = 16 * r + g;
-      *reinterpret_cast<uint32_t*>(sO + xswz<P>(i0, col)) = pack_bf16x2(acc[nt][0], acc[nt][1]);
-      *reinterpret_cast<uint32_t*>(sO + xswz<P>(i0 + 8, col)) = pack_bf16x2(acc[nt][2], acc[nt][3]);
+      *reinterpret_cast<uint32_t*>(sO + swz<P>(i0, col)) = pack_bf16x2(acc[nt][0], acc[nt][1]);
+      *reinterpret_cast<uint32_t*>(sO + swz<P>(i0 + 8, col)) = pack_bf16x2(acc[nt][2], acc[nt][3]);
     }
   }
 
-  // swizzled sO -> global [64][D] rows (columns c0..c0+P), 16-byte coalesced stores
+  // sO -> global tile [64][D] in the scan's layout swz<D>: row r holds the shared row image of
+  // each 128-wide panel unchanged (for D = 256 the XOR acts on the low three chunk bits only,
+  // so the panel images at c0 = 0 and 128 concatenate to swz<256>). 16-byte coalesced stores.
   __device__ void store_tile(__nv_bfloat16* out, int c0) {
     constexpr int kChunks = kTile * P / 8;
 #pragma unroll
     for (int i = tid; i < kChunks; i += NT) {
+      const int row = i / (P / 8), j = (i % (P / 8)) * 8;
+      *reinterpret_cast<uint4*>(out + row * D + c0 + j) = *reinterpret_cast<const uint4*>(sO + row * P + j);
+    }
+  }
+  // sO -> u in the scan's value-panel layout [D/64][64][64], each panel swz<64>
+  __device__ void store_u(__nv_bfloat16* out, int c0) {
+    constexpr int kChunks = kTile * P / 8;
+#pragma unroll
+    for (int i = tid; i < kChunks; i += NT) {
       const int row = i / (P / 8), col = (i % (P / 8)) * 8;
-      *reinterpret_cast<uint4*>(out + row * D + c0 + col) = *reinterpret_cast<const uint4*>(sO + xswz<P>(row, col));
+      const int pv = (c0 + col) >> 6, cc = (c0 + col) & 63;
+      *reinterpret_cast<uint4*>(out + pv * (kTile * 64) + swz<64>(row, cc)) =
+          *reinterpret_cast<const uint4*>(sO + swz<P>(row, col));
     }
   }
 
@@ -661,12 +669,12 @@ struct IntraKernel {
       constexpr int kChunks = kTile * P / 8;
       for (int i = tid; i < kChunks; i += NT) {
         const int row = i / (P / 8), col = (i % (P / 8)) * 8;
-        uint4 kv = *reinterpret_cast<const uint4*>(sK + xswz<P>(row, col));
+        uint4 kv = *reinterpret_cast<const uint4*>(sK + swz<P>(row, col));
         uint32_t* kw = reinterpret_cast<uint32_t*>(&kv);
         uint4 kgv;
         uint32_t* kgw = reinterpret_cast<uint32_t*>(&kgv);
         if constexpr (ERASE) {
-          const uint4 bv = *reinterpret_cast<const uint4*>(sB + xswz<P>(row, col));
+          const uint4 bv = *reinterpret_cast<const uint4*>(sB + swz<P>(row, col));
           const uint32_t* bw = reinterpret_cast<const uint32_t*>(&bv);
           // kg uses k, the w operand uses bf16(k*b)
 #pragma unroll
@@ -703,8 +711,9 @@ struct IntraKernel {
             kw[e] = pack_bf16x2(k0 * e0, k1 * e1);
           }
         }
-        *reinterpret_cast<uint4*>(sX + xswz<P>(row, col)) = kv;
-        *reinterpret_cast<uint4*>(gKG + row * D + c0 + col) = kgv;  // wy_fast.py:125-139
+        *reinterpret_cast<uint4*>(sX + swz<P>(row, col)) = kv;
+        // kg in the scan's layout (wy_fast.py:125-139)
+        *reinterpret_cast<uint4*>(gKG + row * D + c0 + (swz<P>(row, col) - row * P)) = kgv;
       }
       if (tid < P) {
         if constexpr (HEAD)
@@ -730,20 +739,20 @@ struct IntraKernel {
       constexpr int kChunks = kTile * P / 8;
       for (int i = tid; i < kChunks; i += NT) {
         const int row = i / (P / 8), col = (i % (P / 8)) * 8;
-        uint4 vv = *reinterpret_cast<const uint4*>(sV + xswz<P>(row, col));
+        uint4 vv = *reinterpret_cast<const uint4*>(sV + swz<P>(row, col));
         if (p.write != nullptr) {
-          const uint4 ww = *reinterpret_cast<const uint4*>(sW + xswz<P>(row, col));
+          const uint4 ww = *reinterpret_cast<const uint4*>(sW + swz<P>(row, col));
           uint32_t* vw = reinterpret_cast<uint32_t*>(&vv);
           const uint32_t* wg = reinterpret_cast<const uint32_t*>(&ww);
 #pragma unroll
           for (int e = 0; e < 4; ++e) vw[e] = pack_bf16x2(bf_lo(vw[e]) * bf_lo(wg[e]), bf_hi(vw[e]) * bf_hi(wg[e]));
         }
-        *reinterpret_cast<uint4*>(sX + xswz<P>(row, col)) = vv;
+        *reinterpret_cast<uint4*>(sX + swz<P>(row, col)) = vv;
       }
       __syncthreads();
       wy_product();
       __syncthreads();
-      store_tile(gU, c0);
+      store_u(gU, c0);
     }
   }
 };

@@ -6,14 +6,12 @@ namespace memt {
 
 template <int D>
 static int launch_scan_t(const ScanParams& p, cudaStream_t s) {
-  constexpr int BV = 64;
-  constexpr int NW = D <= 128 ? 4 : 8;
-  using Cfg = ScanCfg<D, BV, NW>;
-  cudaError_t e = ensure_smem(scan_kernel<D, BV, NW>, Cfg::kSmem);
+  using Cfg = ScanCfg<D>;
+  cudaError_t e = ensure_smem(scan_kernel<D>, Cfg::kSmem);
   if (e != cudaSuccess) return cuda_status(e);
-  const unsigned grid = static_cast<unsigned>(p.N) * p.H * (D / BV);
+  const unsigned grid = static_cast<unsigned>(p.N) * p.H * (D / Cfg::BV);
   ProfScope prof(kProfScan, s);
-  scan_kernel<D, BV, NW><<<grid, Cfg::kThreads, Cfg::kSmem, s>>>(p);
+  scan_kernel<D><<<grid, Cfg::kThreads, Cfg::kSmem, s>>>(p);
   return cuda_status(cudaGetLastError());
 }
 
