@@ -138,6 +138,31 @@ size_t memt_gdn2_update_workspace_size(int32_t num_samples, int64_t total_tokens
 int memt_gdn2_update(const memt_gdn2_update_args *args, void *workspace, size_t workspace_bytes,
                      memt_stream_t stream);
 
+/* ---- the update without any allocation ---------------------------------
+ *
+ * No counterpart in the reference: it exists for callers that cannot allocate device memory
+ * when they call the update, for example serving engines that size their device memory pool
+ * once at start-up and forbid allocations inside a step, or hosts that reach this library
+ * through a C FFI without a caching allocator, where a cudaMalloc/cudaFree pair around every
+ * call would be slow (cudaFree synchronises the device). It runs the same kernels as
+ * memt_gdn2_update but takes its scratch from a static device array of
+ * MEMT_NOALLOC_SCRATCH_BYTES (64 MiB) that the library holds on each device where this entry
+ * point has been called, until the process exits. Nothing is allocated: no cudaMalloc,
+ * cudaFree or allocating library routine is called.
+ *
+ * Limits and rules:
+ *   - problems whose memt_gdn2_update_workspace_size exceeds MEMT_NOALLOC_SCRATCH_BYTES are
+ *     rejected with MEMT_ERR_WORKSPACE before any launch (at d = 128 that is about 1,300
+ *     (64-token chunk, head) tiles, e.g. 5,000 tokens of 16 heads);
+ *   - the first call on a device looks up the array's device address (cudaGetSymbolAddress)
+ *     with that device current; make that first call before any stream capture;
+ *   - all calls on a device share the one array: calls that overlap on the GPU (different
+ *     streams, or different host threads without ordering) race. Every byte a call reads from
+ *     the array it has written earlier in the same call, so nothing needs clearing between
+ *     calls. */
+#define MEMT_NOALLOC_SCRATCH_BYTES (64u << 20)
+int memt_gdn2_update_noalloc(const memt_gdn2_update_args *args, memt_stream_t stream);
+
 /* Device status word the last update left in this workspace (0 = clean; bit 0: a sample
  * had negative length or offsets outside [0, L]; bit 1: chunk table overflow). Reading it
  * synchronises the stream; intended for tests and debugging. */
