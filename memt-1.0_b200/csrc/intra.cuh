@@ -6,8 +6,9 @@
 //   diagonal key-key blocks              _vendor/fla/ops/gdn2/chunk_intra_token_parallel.py:25-132
 //   off-diagonal blocks + blocked solve  _vendor/fla/ops/gdn2/chunk_intra.py:153-417
 //   WY operands u, w, kg                 _vendor/fla/ops/gdn2/wy_fast.py:36-142
-// and writes only what the state scan consumes: w, u, kg (bf16, [chunk][head][64][D])
-// and the chunk's total decay 2^G_last (fp32, [chunk][head][D]).
+// and writes only what the state scan consumes: w and kg ([chunk][head][64][D]), u
+// ([chunk][head][D/64][64][64]), all bf16 in the scan's swizzled tile layout, and the chunk's
+// total decay 2^G_last (fp32, [chunk][head][D]).
 //
 // Numerics follow the reference's GPU rounding points: fp32 cumulative log2 decay;
 // exact-fp32 diagonal 16x16 key-key blocks; tf32 off-diagonal blocks built from operands
@@ -20,7 +21,12 @@
 // XOR-swizzled shared tiles. The tf32 score products take their fragments straight from
 // ldmatrix: the k dimension is permuted so that the bf16 pair (2t, 2t+1) a lane receives
 // feeds k-slots t and t+4 of an m16n8k8 fragment (a permutation of the summation index
-// leaves the product unchanged).
+// leaves the product unchanged). Fragment loads of a k-step are issued before its MMAs.
+//
+// Work split: the 20 (16-row block, 8-column tile) pieces of the lower-triangular score
+// matrix are spread over the 8 warps (at most 3 each, one row block per warp). For D <= 128
+// warps 0-3 run the serial blocked solve while warps 4-7 stage the u and w operands and
+// write kg (named barriers keep the two groups independent).
 //
 // Gate layouts:
 //   per head (one decay per token): every factor is a row or column scalar. The diagonal
@@ -48,7 +54,7 @@ struct IntraCfg {
   static constexpr size_t kBytesE = HEAD ? 0 : size_t(kTile) * kLdE * 4;
   static constexpr size_t kBytesA = size_t(kTile) * kLdA * 4;
   static constexpr size_t kBytesAi = size_t(kTile) * kLdAi * 2;
-  // sK | sB? | sV | sW | sO | sE? | sEi? | sA (aliased by sX) | sAi
+  // sK | sB? | sV | sW (later the w operand) | sO | sE? | sEi? | sA | sAi
   static constexpr size_t offK = 0;
   static constexpr size_t offB = offK + kTileB;
   static constexpr size_t offV = offB + (ERASE ? kTileB : 0);
@@ -59,29 +65,36 @@ struct IntraCfg {
   static constexpr size_t offA = offEi + kBytesE;
   static constexpr size_t offAi = offA + kBytesA;
   static constexpr size_t kSmem = offAi + kBytesAi;
-  static_assert(kTileB <= kBytesA, "staging tile aliases the score buffer");
+  static constexpr int kSmall = 9 * kTile + kThreads;  // static per-head factors + scan totals
 };
+
+__device__ __forceinline__ void named_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(nthreads) : "memory");
+}
 
 // 16x16x16 tf32 product on one warp: acc[nt] += A (16x16 fp32, row-major, lda) . B (16x16,
 // [k][n], ldb); acc[nt] is the C fragment of columns 8*nt..8*nt+7.
 __device__ __forceinline__ void warp_tf32_16x16x16(float (&acc)[2][4], const float* A, int lda,
                                                    const float* B, int ldb, int lane) {
   const int g = lane >> 2, t = lane & 3;
+  uint32_t a[2][4], b[2][2][2];
 #pragma unroll
-  for (int kk = 0; kk < 16; kk += 8) {
-    uint32_t a[4];
-    a[0] = to_tf32(A[g * lda + kk + t]);
-    a[1] = to_tf32(A[(g + 8) * lda + kk + t]);
-    a[2] = to_tf32(A[g * lda + kk + t + 4]);
-    a[3] = to_tf32(A[(g + 8) * lda + kk + t + 4]);
+  for (int kq = 0; kq < 2; ++kq) {
+    const int kk = 8 * kq;
+    a[kq][0] = to_tf32(A[g * lda + kk + t]);
+    a[kq][1] = to_tf32(A[(g + 8) * lda + kk + t]);
+    a[kq][2] = to_tf32(A[g * lda + kk + t + 4]);
+    a[kq][3] = to_tf32(A[(g + 8) * lda + kk + t + 4]);
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
-      uint32_t b[2];
-      b[0] = to_tf32(B[(kk + t) * ldb + nt * 8 + g]);
-      b[1] = to_tf32(B[(kk + t + 4) * ldb + nt * 8 + g]);
-      mma_tf32_1688(acc[nt], a, b);
+      b[kq][nt][0] = to_tf32(B[(kk + t) * ldb + nt * 8 + g]);
+      b[kq][nt][1] = to_tf32(B[(kk + t + 4) * ldb + nt * 8 + g]);
     }
   }
+#pragma unroll
+  for (int kq = 0; kq < 2; ++kq)
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) mma_tf32_1688(acc[nt], a[kq], b[kq][nt]);
 }
 
 __device__ __forceinline__ void zero_acc(float (&acc)[2][4]) {
@@ -89,6 +102,15 @@ __device__ __forceinline__ void zero_acc(float (&acc)[2][4]) {
   for (int i = 0; i < 2; ++i)
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+}
+
+__device__ __forceinline__ void warp_store_f32(float* C, int ldc, const float (&acc)[2][4], int lane) {
+  const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+    *reinterpret_cast<float2*>(C + g * ldc + nt * 8 + 2 * t) = make_float2(acc[nt][0], acc[nt][1]);
+    *reinterpret_cast<float2*>(C + (g + 8) * ldc + nt * 8 + 2 * t) = make_float2(acc[nt][2], acc[nt][3]);
+  }
 }
 
 // Store a 16x16 C fragment pair as fp32 (sign applied) into A and, rows masked by `len`,
@@ -115,16 +137,33 @@ __device__ __forceinline__ void warp_store_block(float* A, int lda, __nv_bfloat1
 __device__ __forceinline__ float bf_lo(uint32_t u) { return __uint_as_float(u << 16); }
 __device__ __forceinline__ float bf_hi(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
 
+// Score pieces of each warp: one row block r, up to three 8-column tiles (-1 = none).
+// Row block r has 2(r+1) tiles; 20 tiles over 8 warps, at most 3 per warp.
+__device__ __forceinline__ void score_pieces(int warp, int& r, int (&nt)[3]) {
+  switch (warp) {
+    case 0: r = 0; nt[0] = 0; nt[1] = 1; nt[2] = -1; break;
+    case 1: r = 1; nt[0] = 0; nt[1] = 2; nt[2] = -1; break;
+    case 2: r = 1; nt[0] = 1; nt[1] = 3; nt[2] = -1; break;
+    case 3: r = 2; nt[0] = 0; nt[1] = 2; nt[2] = 4; break;
+    case 4: r = 2; nt[0] = 1; nt[1] = 3; nt[2] = 5; break;
+    case 5: r = 3; nt[0] = 0; nt[1] = 3; nt[2] = 6; break;
+    case 6: r = 3; nt[0] = 1; nt[1] = 4; nt[2] = 7; break;
+    default: r = 3; nt[0] = 2; nt[1] = 5; nt[2] = -1; break;
+  }
+}
+
 template <int D, bool HEAD, bool ERASE>
 struct IntraKernel {
   using Cfg = IntraCfg<D, HEAD, ERASE>;
   static constexpr int P = Cfg::kPanel;
   static constexpr int NT = Cfg::kThreads;
+  static constexpr bool kOverlap = Cfg::kPanels == 1;  // solve || staging (D <= 128)
 
-  __nv_bfloat16 *sK, *sB, *sV, *sW, *sO, *sX, *sAi;
+  __nv_bfloat16 *sK, *sB, *sV, *sW, *sO, *sAi;
   float *sE, *sEi, *sA;
-  // per-head factors: G, left (row) factor, right factors per row block, 2^G, 2^(G_last-G)
-  float *sG, *sLf, *sRf, *sEh, *sKgf;
+  // per-head factors: G, left (row) factor, right factors per row block, 2^G, 2^(G_last-G),
+  // bf16(sqrt(beta)) per token
+  float *sG, *sLf, *sRf, *sEh, *sKgf, *sBeta;
   float* sSeg;
 
   int tid, lane, warp, len, tok0, h;
@@ -143,6 +182,16 @@ struct IntraKernel {
     }
   }
 
+  // per-token bf16(sqrt(beta)) of a per-head beta (warp 1)
+  __device__ void head_beta(const IntraParams& p) {
+    if (warp != 1 || p.beta_layout != 1) return;
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int i = 2 * lane + q;
+      sBeta[i] = i < len ? bf16_round(sqrtf(__bfloat162float(p.beta[(int64_t)(tok0 + i) * p.H + h]))) : 0.f;
+    }
+  }
+
   // Fold sqrt(beta) into k in place: k' = bf16( bf16(sqrt(beta)) * k ) (models/qwen/layer.py:81-96)
   __device__ void fold_beta(const IntraParams& p, int c0) {
     constexpr int kChunks = kTile * P / 8;
@@ -153,7 +202,7 @@ struct IntraKernel {
       uint4 kv = *ptr;
       float sb[8];
       if (p.beta_layout == 1) {
-        const float s = bf16_round(sqrtf(__bfloat162float(p.beta[(int64_t)(tok0 + row) * p.H + h])));
+        const float s = sBeta[row];
 #pragma unroll
         for (int e = 0; e < 8; ++e) sb[e] = s;
       } else {
@@ -178,8 +227,8 @@ struct IntraKernel {
     if (warp != 0) return;
     // G_t = (sum_{s<=t} g_s) / ln2 over the 64 tokens; lane owns tokens 2*lane, 2*lane+1
     const int t0 = 2 * lane, t1 = 2 * lane + 1;
-    float g0 = t0 < len ? p.g[(int64_t)(tok0 + t0) * p.H + h] : 0.f;
-    float g1 = t1 < len ? p.g[(int64_t)(tok0 + t1) * p.H + h] : 0.f;
+    const float g0 = t0 < len ? p.g[(int64_t)(tok0 + t0) * p.H + h] : 0.f;
+    const float g1 = t1 < len ? p.g[(int64_t)(tok0 + t1) * p.H + h] : 0.f;
     float s = g0 + g1;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -197,14 +246,14 @@ struct IntraKernel {
       const int i = 2 * lane + q;
       const float Gi = sG[i];
       const float Gn = sG[i & ~15];
-      sLf[i] = fast_exp2(Gi - Gn);                 // left factor 2^(G_i - G_n(i))
-      sEh[i] = fast_exp2(Gi);                      // 2^G_i
+      sLf[i] = fast_exp2(Gi - Gn);                   // left factor 2^(G_i - G_n(i))
+      sEh[i] = fast_exp2(Gi);                        // 2^G_i
       sKgf[i] = i < len ? fast_exp2(Gl - Gi) : 0.f;  // 2^(G_last - G_i)
 #pragma unroll
-      for (int r = 1; r < 4; ++r)                  // right factors 2^(G_n(r) - G_j), j < 16r
+      for (int r = 1; r < 4; ++r)                    // right factors 2^(G_n(r) - G_j), j < 16r
         sRf[r * kTile + i] = i < 16 * r ? fast_exp2(sG[16 * r] - Gi) : 0.f;
     }
-    if (lane == 0) sSeg[0] = fast_exp2(Gl);        // 2^G_last
+    if (lane == 0) sSeg[0] = fast_exp2(Gl);          // 2^G_last
   }
 
   // ---- decay, per-channel layout: cumulative sum and factor tables of one panel ----
@@ -262,94 +311,104 @@ struct IntraKernel {
     return make_float2(fast_exp2(e.x), fast_exp2(e.y));
   }
 
-  // ---- key-key scores of this panel, accumulated into acc (warp: row block r = w/2,
-  //      n-tiles half, half+2, ..., the diagonal n-tile last) ----
-  __device__ void scores_panel(float (&acc)[4][4]) {
-    const int r = warp >> 1, half = warp & 1;
+  // ---- key-key scores of this panel, accumulated into acc[piece] ----
+  __device__ void scores_panel(float (&acc)[3][4]) {
+    int r, nts[3];
+    score_pieces(warp, r, nts);
     if (16 * r >= len) return;  // whole row block beyond the chunk (chunk_intra.py:242-278)
     const int g = lane >> 2, t = lane & 3;
     const int n_ref = 16 * r;
     const int i0 = n_ref + g, i1 = n_ref + g + 8;
-    float lf0 = 0.f, lf1 = 0.f, rf[4] = {0.f, 0.f, 0.f, 0.f};
+    bool offdiag = false;
+#pragma unroll
+    for (int s = 0; s < 3; ++s) offdiag = offdiag || (nts[s] >= 0 && (nts[s] >> 1) < r);
+    float lf0 = 0.f, lf1 = 0.f, rf[3] = {0.f, 0.f, 0.f};
     if constexpr (HEAD) {
       lf0 = i0 < len ? sLf[i0] : 0.f;
       lf1 = i1 < len ? sLf[i1] : 0.f;
 #pragma unroll
-      for (int s = 0; s < 4; ++s) {
-        const int nt = half + 2 * s;
-        if (s < r) rf[s] = sRf[r * kTile + 8 * nt + g];
-      }
+      for (int s = 0; s < 3; ++s)
+        if (nts[s] >= 0 && (nts[s] >> 1) < r) rf[s] = sRf[r * kTile + 8 * nts[s] + g];
     }
 #pragma unroll 1
     for (int kk = 0; kk < P / 16; ++kk) {
-      uint32_t a[4];
+      // all fragment loads of the k-step first
+      uint32_t a[4], eb[4] = {0u, 0u, 0u, 0u}, bq[3][2];
       ldsm_x4(a, smem_u32(sK + swz<P>(n_ref + (lane & 15), 16 * kk + 8 * (lane >> 4))));
-      uint32_t eb[4] = {0u, 0u, 0u, 0u};
       if constexpr (ERASE)
         ldsm_x4(eb, smem_u32(sB + swz<P>(n_ref + (lane & 15), 16 * kk + 8 * (lane >> 4))));
-      // left operand, fp32, for the two k8 slices: v[slice][reg]
-      float lv[2][4];
-      const int cA = 16 * kk + 2 * t;  // channel of the lo element of a[0]/a[1]
 #pragma unroll
-      for (int sl = 0; sl < 2; ++sl) {
-        const uint32_t r0 = a[2 * sl], r1 = a[2 * sl + 1];  // rows g / g+8
-        float x0 = bf_lo(r0), x1 = bf_hi(r0), x2 = bf_lo(r1), x3 = bf_hi(r1);
-        if constexpr (ERASE) {
-          x0 *= bf_lo(eb[2 * sl]);
-          x1 *= bf_hi(eb[2 * sl]);
-          x2 *= bf_lo(eb[2 * sl + 1]);
-          x3 *= bf_hi(eb[2 * sl + 1]);
-        }
-        if constexpr (HEAD) {
-          lv[sl][0] = x0 * lf0;  // (row g,   k-slot t)
-          lv[sl][1] = x2 * lf1;  // (row g+8, k-slot t)
-          lv[sl][2] = x1 * lf0;  // (row g,   k-slot t+4)
-          lv[sl][3] = x3 * lf1;  // (row g+8, k-slot t+4)
-        } else {
-          const int c = cA + 8 * sl;
-          const float2 f0 = p2d2(i0, n_ref, c), f1 = p2d2(i1, n_ref, c);
-          lv[sl][0] = i0 < len ? x0 * f0.x : 0.f;
-          lv[sl][1] = i1 < len ? x2 * f1.x : 0.f;
-          lv[sl][2] = i0 < len ? x1 * f0.y : 0.f;
-          lv[sl][3] = i1 < len ? x3 * f1.y : 0.f;
+      for (int s = 0; s < 3; ++s)
+        if (nts[s] >= 0)
+          ldsm_x2(bq[s], smem_u32(sK + swz<P>(8 * nts[s] + (lane & 7), 16 * kk + 8 * ((lane >> 3) & 1))));
+      // left operand (tf32, two k8 slices) when the warp owns an off-diagonal piece, or per
+      // channel (the diagonal pieces then use 3xTF32 as well)
+      const int cA = 16 * kk + 2 * t;  // channel of the lo element of a[0]/a[1]
+      float lv[2][4];
+      uint32_t ah[2][4], al[2][4];
+      if (!HEAD || offdiag) {
+#pragma unroll
+        for (int sl = 0; sl < 2; ++sl) {
+          const uint32_t r0 = a[2 * sl], r1 = a[2 * sl + 1];  // rows g / g+8
+          float x0 = bf_lo(r0), x1 = bf_hi(r0), x2 = bf_lo(r1), x3 = bf_hi(r1);
+          if constexpr (ERASE) {
+            x0 *= bf_lo(eb[2 * sl]);
+            x1 *= bf_hi(eb[2 * sl]);
+            x2 *= bf_lo(eb[2 * sl + 1]);
+            x3 *= bf_hi(eb[2 * sl + 1]);
+          }
+          if constexpr (HEAD) {
+            lv[sl][0] = x0 * lf0;  // (row g,   k-slot t)
+            lv[sl][1] = x2 * lf1;  // (row g+8, k-slot t)
+            lv[sl][2] = x1 * lf0;  // (row g,   k-slot t+4)
+            lv[sl][3] = x3 * lf1;  // (row g+8, k-slot t+4)
+          } else {
+            const int c = cA + 8 * sl;
+            const float2 f0 = p2d2(i0, n_ref, c), f1 = p2d2(i1, n_ref, c);
+            lv[sl][0] = i0 < len ? x0 * f0.x : 0.f;
+            lv[sl][1] = i1 < len ? x2 * f1.x : 0.f;
+            lv[sl][2] = i0 < len ? x1 * f0.y : 0.f;
+            lv[sl][3] = i1 < len ? x3 * f1.y : 0.f;
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            ah[sl][q] = to_tf32(lv[sl][q]);
+            if constexpr (!HEAD) al[sl][q] = to_tf32(lv[sl][q] - __uint_as_float(ah[sl][q]));
+          }
         }
       }
 #pragma unroll
-      for (int s = 0; s < 4; ++s) {
-        if (s > r) break;
-        const int nt = half + 2 * s;
-        const bool diag = (s == r);
-        uint32_t bq[2];
-        ldsm_x2(bq, smem_u32(sK + swz<P>(8 * nt + (lane & 7), 16 * kk + 8 * ((lane >> 3) & 1))));
+      for (int s = 0; s < 3; ++s) {
+        if (nts[s] < 0) continue;
+        const int nt = nts[s];
+        const bool diag = (nt >> 1) == r;
         if constexpr (HEAD) {
           if (diag) {
-            // exact bf16 products; the per-pair exponent is applied after the sum
-            uint32_t af[4] = {a[0], a[1], a[2], a[3]};
+            // exact bf16 products; the per-pair exponent is applied after the sum. With an
+            // erase factor the fp32 product kb = k*b (16 significant bits) is split into bf16
+            // hi + lo parts, so the two bf16 products sum to the exact fp32 value.
             if constexpr (ERASE) {
-#pragma unroll
-              for (int q = 0; q < 4; ++q)
-                af[q] = pack_bf16x2(bf_lo(a[q]) * bf_lo(eb[q]), bf_hi(a[q]) * bf_hi(eb[q]));
-            }
-            // with an erase factor the fp32 product kb = k*b (16 significant bits) is split
-            // into bf16 hi + lo parts, so the two bf16 products sum to the exact fp32 value
-            mma_bf16_16816(acc[s], af, bq);
-            if constexpr (ERASE) {
-              uint32_t lo[4];
+              uint32_t hi[4], lo[4];
 #pragma unroll
               for (int q = 0; q < 4; ++q) {
                 const float p0 = bf_lo(a[q]) * bf_lo(eb[q]), p1 = bf_hi(a[q]) * bf_hi(eb[q]);
-                lo[q] = pack_bf16x2(p0 - bf_lo(af[q]), p1 - bf_hi(af[q]));
+                hi[q] = pack_bf16x2(p0, p1);
+                lo[q] = pack_bf16x2(p0 - bf_lo(hi[q]), p1 - bf_hi(hi[q]));
               }
-              mma_bf16_16816(acc[s], lo, bq);
+              mma_bf16_16816(acc[s], hi, bq[s]);
+              mma_bf16_16816(acc[s], lo, bq[s]);
+            } else {
+              mma_bf16_16816(acc[s], a, bq[s]);
             }
-            continue;
-          }
+          } else {
+            uint32_t bb[2][2];
 #pragma unroll
-          for (int sl = 0; sl < 2; ++sl) {
-            const uint32_t rb = bq[sl];
-            uint32_t bb[2] = {to_tf32(bf_lo(rb) * rf[s]), to_tf32(bf_hi(rb) * rf[s])};
-            uint32_t aa[4] = {to_tf32(lv[sl][0]), to_tf32(lv[sl][1]), to_tf32(lv[sl][2]), to_tf32(lv[sl][3])};
-            mma_tf32_1688(acc[s], aa, bb);
+            for (int sl = 0; sl < 2; ++sl) {
+              bb[sl][0] = to_tf32(bf_lo(bq[s][sl]) * rf[s]);
+              bb[sl][1] = to_tf32(bf_hi(bq[s][sl]) * rf[s]);
+            }
+            mma_tf32_1688(acc[s], ah[0], bb[0]);
+            mma_tf32_1688(acc[s], ah[1], bb[1]);
           }
         } else {
           const int j = 8 * nt + g;
@@ -357,67 +416,61 @@ struct IntraKernel {
           for (int sl = 0; sl < 2; ++sl) {
             const int c = cA + 8 * sl;
             const float2 f = p2d2(n_ref, j, c);
-            const float y0 = bf_lo(bq[sl]) * f.x, y1 = bf_hi(bq[sl]) * f.y;
+            const float y0 = bf_lo(bq[s][sl]) * f.x, y1 = bf_hi(bq[s][sl]) * f.y;
             uint32_t bh[2] = {to_tf32(y0), to_tf32(y1)};
-            uint32_t ah[4] = {to_tf32(lv[sl][0]), to_tf32(lv[sl][1]), to_tf32(lv[sl][2]), to_tf32(lv[sl][3])};
             if (diag) {
               if (!fast) continue;  // exact pairwise evaluation below
               uint32_t bl[2] = {to_tf32(y0 - __uint_as_float(bh[0])), to_tf32(y1 - __uint_as_float(bh[1]))};
-              uint32_t al[4];
-#pragma unroll
-              for (int q = 0; q < 4; ++q) al[q] = to_tf32(lv[sl][q] - __uint_as_float(ah[q]));
-              mma_tf32_1688(acc[s], al, bh);
-              mma_tf32_1688(acc[s], ah, bl);
+              mma_tf32_1688(acc[s], al[sl], bh);
+              mma_tf32_1688(acc[s], ah[sl], bl);
             }
-            mma_tf32_1688(acc[s], ah, bh);
+            mma_tf32_1688(acc[s], ah[sl], bh);
           }
         }
       }
     }
     if constexpr (!HEAD) {
       if (!fast) {
-        // diagonal n-tile with exact per-pair exponents (chunk_intra_token_parallel.py:114-123)
-        const int nt = 2 * r + half;
-        float extra[4];
+        // diagonal pieces with exact per-pair exponents (chunk_intra_token_parallel.py:114-123)
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int i = n_ref + g + ((q & 2) ? 8 : 0);
-          const int j = 8 * nt + 2 * t + (q & 1);
-          float sum = 0.f;
-          if (i < len && j < i) {
-            for (int c = 0; c < P; ++c) {
-              float kb = __bfloat162float(sK[swz<P>(i, c)]);
-              if constexpr (ERASE) kb *= __bfloat162float(sB[swz<P>(i, c)]);
-              sum += kb * __bfloat162float(sK[swz<P>(j, c)]) *
-                     fast_exp2(sE[i * Cfg::kLdE + c] - sE[j * Cfg::kLdE + c]);
+        for (int s = 0; s < 3; ++s) {
+          if (nts[s] < 0 || (nts[s] >> 1) != r) continue;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int i = n_ref + g + ((q & 2) ? 8 : 0);
+            const int j = 8 * nts[s] + 2 * t + (q & 1);
+            float sum = 0.f;
+            if (i < len && j < i) {
+              for (int c = 0; c < P; ++c) {
+                float kb = __bfloat162float(sK[swz<P>(i, c)]);
+                if constexpr (ERASE) kb *= __bfloat162float(sB[swz<P>(i, c)]);
+                sum += kb * __bfloat162float(sK[swz<P>(j, c)]) *
+                       fast_exp2(sE[i * Cfg::kLdE + c] - sE[j * Cfg::kLdE + c]);
+              }
             }
+            acc[s][q] += sum;
           }
-          extra[q] = sum;
         }
-#pragma unroll
-        for (int s = 0; s < 4; ++s)
-          if (s == r)
-#pragma unroll
-            for (int q = 0; q < 4; ++q) acc[s][q] += extra[q];
       }
     }
   }
 
   // scores -> sA (strictly lower on the diagonal blocks; per-head diagonal scaled by 2^(G_i-G_j))
-  __device__ void store_scores(const float (&acc)[4][4]) {
-    const int r = warp >> 1, half = warp & 1;
+  __device__ void store_scores(const float (&acc)[3][4]) {
+    int r, nts[3];
+    score_pieces(warp, r, nts);
     const int g = lane >> 2, t = lane & 3;
 #pragma unroll
-    for (int s = 0; s < 4; ++s) {
-      if (s > r) break;
-      const int nt = half + 2 * s;
+    for (int s = 0; s < 3; ++s) {
+      if (nts[s] < 0) continue;
+      const bool diag = (nts[s] >> 1) == r;
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const int i = 16 * r + g + ((q & 2) ? 8 : 0);
-        const int j = 8 * nt + 2 * t + (q & 1);
+        const int j = 8 * nts[s] + 2 * t + (q & 1);
         float x = acc[s][q];
         if constexpr (HEAD) {
-          if (s == r) x = (j < i && i < len) ? x * fast_exp2(sG[i] - sG[j]) : 0.f;
+          if (diag) x = (j < i && i < len) ? x * fast_exp2(sG[i] - sG[j]) : 0.f;
         }
         if (j >= i || i >= len) x = 0.f;
         sA[i * Cfg::kLdA + j] = x;
@@ -425,12 +478,12 @@ struct IntraKernel {
     }
   }
 
-  // Blocked inverse of (I + A) (chunk_intra.py:326-395). fp32 blocks stay in sA (diagonal
-  // in place, off-diagonal (r, s) in the unused upper slot (s, r)); every finished block is
-  // also written as bf16 into sAi (rows >= len zero).
+  // Blocked inverse of (I + A) (chunk_intra.py:326-395), run by warps 0-3 only (named
+  // barrier 1). fp32 blocks stay in sA (diagonal in place, off-diagonal (r, s) in the unused
+  // upper slot (s, r)); every finished block is also written as bf16 into sAi (rows >= len zero).
   __device__ void solve() {
     constexpr int LD = Cfg::kLdA, LDI = Cfg::kLdAi;
-    if (warp < 4) {
+    {
       const int r = warp;
       const int c = lane & 15;
       float* blk = sA + (16 * r) * LD + 16 * r;
@@ -460,7 +513,7 @@ struct IntraKernel {
         }
       }
     }
-    __syncthreads();
+    named_sync(1, 128);
     auto Dg = [&](int r) { return sA + (16 * r) * LD + 16 * r; };         // Ai_rr
     auto Ak = [&](int r, int s) { return sA + (16 * r) * LD + 16 * s; };  // Akk_rs, r > s
     auto Ao = [&](int r, int s) { return sA + (16 * s) * LD + 16 * r; };  // Ai_rs kept at (s, r)
@@ -471,66 +524,106 @@ struct IntraKernel {
       float* tmp = (s == 0) ? Ao(2, 0) : (s == 1) ? Ao(3, 1) : Ao(3, 0);
       zero_acc(acc);
       warp_tf32_16x16x16(acc, Dg(s + 1), LD, Ak(s + 1, s), LD, lane);
-      {
-        const int g = lane >> 2, t = lane & 3;
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          *reinterpret_cast<float2*>(tmp + g * LD + nt * 8 + 2 * t) = make_float2(acc[nt][0], acc[nt][1]);
-          *reinterpret_cast<float2*>(tmp + (g + 8) * LD + nt * 8 + 2 * t) = make_float2(acc[nt][2], acc[nt][3]);
-        }
-      }
+      warp_store_f32(tmp, LD, acc, lane);
       __syncwarp();
       zero_acc(acc);
       warp_tf32_16x16x16(acc, tmp, LD, Dg(s), LD, lane);
       warp_store_block(Ao(s + 1, s), LD, Ab(s + 1, s), LDI, acc, lane, -1.f, 16 * (s + 1), len);
     }
-    __syncthreads();
+    named_sync(1, 128);
     if (warp < 2) {  // Ai20, Ai31
       const int r = warp + 2;
       float* dst = Ao(r, r - 2);
       zero_acc(acc);
       warp_tf32_16x16x16(acc, Ak(r, r - 2), LD, Dg(r - 2), LD, lane);
       warp_tf32_16x16x16(acc, Ak(r, r - 1), LD, Ao(r - 1, r - 2), LD, lane);
-      {
-        const int g = lane >> 2, t = lane & 3;
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          *reinterpret_cast<float2*>(dst + g * LD + nt * 8 + 2 * t) = make_float2(acc[nt][0], acc[nt][1]);
-          *reinterpret_cast<float2*>(dst + (g + 8) * LD + nt * 8 + 2 * t) = make_float2(acc[nt][2], acc[nt][3]);
-        }
-      }
+      warp_store_f32(dst, LD, acc, lane);
       __syncwarp();
       zero_acc(acc);
       warp_tf32_16x16x16(acc, Dg(r), LD, dst, LD, lane);
       __syncwarp();
       warp_store_block(dst, LD, Ab(r, r - 2), LDI, acc, lane, -1.f, 16 * r, len);
     }
-    __syncthreads();
+    named_sync(1, 128);
     if (warp == 0) {  // Ai30
       float* dst = Ao(3, 0);
       zero_acc(acc);
       warp_tf32_16x16x16(acc, Ak(3, 0), LD, Dg(0), LD, lane);
       warp_tf32_16x16x16(acc, Ak(3, 1), LD, Ao(1, 0), LD, lane);
       warp_tf32_16x16x16(acc, Ak(3, 2), LD, Ao(2, 0), LD, lane);
-      {
-        const int g = lane >> 2, t = lane & 3;
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          *reinterpret_cast<float2*>(dst + g * LD + nt * 8 + 2 * t) = make_float2(acc[nt][0], acc[nt][1]);
-          *reinterpret_cast<float2*>(dst + (g + 8) * LD + nt * 8 + 2 * t) = make_float2(acc[nt][2], acc[nt][3]);
-        }
-      }
+      warp_store_f32(dst, LD, acc, lane);
       __syncwarp();
       zero_acc(acc);
       warp_tf32_16x16x16(acc, Dg(3), LD, dst, LD, lane);
       warp_store_block(nullptr, LD, Ab(3, 0), LDI, acc, lane, -1.f, 48, len);
     }
-    __syncthreads();
   }
 
-  // sO (swizzled [64][P]) = A^-1 (lower) . sX (swizzled [64][P]); warp w: row block w/2,
+  // u operand in place: sV = bf16(v * w)   (wy_fast.py:98-100); threads [t0, t0 + n)
+  __device__ void stage_u(const IntraParams& p, int t0, int n) {
+    if (p.write == nullptr) return;
+    constexpr int kChunks = kTile * P / 8;
+    for (int i = tid - t0; i < kChunks; i += n) {
+      const int row = i / (P / 8), col = (i % (P / 8)) * 8;
+      uint4 vv = *reinterpret_cast<const uint4*>(sV + swz<P>(row, col));
+      const uint4 ww = *reinterpret_cast<const uint4*>(sW + swz<P>(row, col));
+      uint32_t* vw = reinterpret_cast<uint32_t*>(&vv);
+      const uint32_t* wg = reinterpret_cast<const uint32_t*>(&ww);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) vw[e] = pack_bf16x2(bf_lo(vw[e]) * bf_lo(wg[e]), bf_hi(vw[e]) * bf_hi(wg[e]));
+      *reinterpret_cast<uint4*>(sV + swz<P>(row, col)) = vv;
+    }
+  }
+
+  // w operand bf16( bf16(k*b) * 2^G ) into sW (wy_fast.py:110-116), kg = bf16(k 2^(G_last-G))
+  // to global (wy_fast.py:125-139) and 2^G_last; threads [t0, t0 + n)
+  __device__ void stage_w_kg(__nv_bfloat16* gKG, float* gEl, int c0, int t0, int n) {
+    const int last = len - 1;
+    constexpr int kChunks = kTile * P / 8;
+    for (int i = tid - t0; i < kChunks; i += n) {
+      const int row = i / (P / 8), col = (i % (P / 8)) * 8;
+      uint4 kv = *reinterpret_cast<const uint4*>(sK + swz<P>(row, col));
+      uint32_t* kw = reinterpret_cast<uint32_t*>(&kv);
+      uint4 kgv;
+      uint32_t* kgw = reinterpret_cast<uint32_t*>(&kgv);
+      uint4 bv = make_uint4(0, 0, 0, 0);
+      if constexpr (ERASE) bv = *reinterpret_cast<const uint4*>(sB + swz<P>(row, col));
+      const uint32_t* bw = reinterpret_cast<const uint32_t*>(&bv);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float k0 = bf_lo(kw[e]), k1 = bf_hi(kw[e]);
+        float e0, e1, q0, q1;
+        if constexpr (HEAD) {
+          e0 = e1 = sEh[row];
+          q0 = q1 = sKgf[row];
+        } else {
+          const float2 ev = p22(row, col + 2 * e), qv = p2d2(last, row, col + 2 * e);
+          e0 = ev.x;
+          e1 = ev.y;
+          q0 = row < len ? qv.x : 0.f;
+          q1 = row < len ? qv.y : 0.f;
+        }
+        kgw[e] = pack_bf16x2(k0 * q0, k1 * q1);
+        if constexpr (ERASE)
+          kw[e] = pack_bf16x2(bf16_round(k0 * bf_lo(bw[e])) * e0, bf16_round(k1 * bf_hi(bw[e])) * e1);
+        else
+          kw[e] = pack_bf16x2(k0 * e0, k1 * e1);
+      }
+      *reinterpret_cast<uint4*>(sW + swz<P>(row, col)) = kv;
+      *reinterpret_cast<uint4*>(gKG + row * D + c0 + (swz<P>(row, col) - row * P)) = kgv;
+    }
+    const int j = tid - t0;
+    if (j >= 0 && j < P) {
+      if constexpr (HEAD)
+        gEl[c0 + j] = sSeg[0];
+      else
+        gEl[c0 + j] = fast ? sE[last * Cfg::kLdE + j] : fast_exp2(sE[last * Cfg::kLdE + j]);
+    }
+  }
+
+  // sO (swizzled [64][P]) = A^-1 (lower) . src (swizzled [64][P]); warp w: row block w/2,
   // column half w&1, k-steps 0..r only.
-  __device__ void wy_product() {
+  __device__ void wy_product(const __nv_bfloat16* src, __nv_bfloat16* dst) {
     const int r = warp >> 1, half = warp & 1;
     constexpr int NTW = P / 16;
     float acc[NTW][4];
@@ -538,13 +631,14 @@ struct IntraKernel {
     for (int i = 0; i < NTW; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
     const int n_base = half * (P / 2);
     for (int ks = 0; ks <= r; ++ks) {
-      uint32_t a[4];
+      uint32_t a[4], b[NTW / 2][4];
       ldsm_x4(a, smem_u32(sAi + (16 * r + (lane & 15)) * Cfg::kLdAi + 16 * ks + 8 * (lane >> 4)));
 #pragma unroll
+      for (int np = 0; np < NTW; np += 2)
+        ldsm_x4_t(b[np / 2], smem_u32(src + swz<P>(16 * ks + (lane & 15), n_base + 8 * np + 8 * (lane >> 4))));
+#pragma unroll
       for (int np = 0; np < NTW; np += 2) {
-        uint32_t b[4];
-        ldsm_x4_t(b, smem_u32(sX + swz<P>(16 * ks + (lane & 15), n_base + 8 * np + 8 * (lane >> 4))));
-        uint32_t b0[2] = {b[0], b[1]}, b1[2] = {b[2], b[3]};
+        uint32_t b0[2] = {b[np / 2][0], b[np / 2][1]}, b1[2] = {b[np / 2][2], b[np / 2][3]};
         mma_bf16_16816(acc[np], a, b0);
         mma_bf16_16816(acc[np + 1], a, b1);
       }
@@ -554,31 +648,31 @@ struct IntraKernel {
     for (int nt = 0; nt < NTW; ++nt) {
       const int col = n_base + 8 * nt + 2 * t;
       const int i0 = 16 * r + g;
-      *reinterpret_cast<uint32_t*>(sO + swz<P>(i0, col)) = pack_bf16x2(acc[nt][0], acc[nt][1]);
-      *reinterpret_cast<uint32_t*>(sO + swz<P>(i0 + 8, col)) = pack_bf16x2(acc[nt][2], acc[nt][3]);
+      *reinterpret_cast<uint32_t*>(dst + swz<P>(i0, col)) = pack_bf16x2(acc[nt][0], acc[nt][1]);
+      *reinterpret_cast<uint32_t*>(dst + swz<P>(i0 + 8, col)) = pack_bf16x2(acc[nt][2], acc[nt][3]);
     }
   }
 
   // sO -> global tile [64][D] in the scan's layout swz<D>: row r holds the shared row image of
   // each 128-wide panel unchanged (for D = 256 the XOR acts on the low three chunk bits only,
   // so the panel images at c0 = 0 and 128 concatenate to swz<256>). 16-byte coalesced stores.
-  __device__ void store_tile(__nv_bfloat16* out, int c0) {
+  __device__ void store_tile(__nv_bfloat16* out, int c0, const __nv_bfloat16* src) {
     constexpr int kChunks = kTile * P / 8;
 #pragma unroll
     for (int i = tid; i < kChunks; i += NT) {
       const int row = i / (P / 8), j = (i % (P / 8)) * 8;
-      *reinterpret_cast<uint4*>(out + row * D + c0 + j) = *reinterpret_cast<const uint4*>(sO + row * P + j);
+      *reinterpret_cast<uint4*>(out + row * D + c0 + j) = *reinterpret_cast<const uint4*>(src + row * P + j);
     }
   }
   // sO -> u in the scan's value-panel layout [D/64][64][64], each panel swz<64>
-  __device__ void store_u(__nv_bfloat16* out, int c0) {
+  __device__ void store_u(__nv_bfloat16* out, int c0, const __nv_bfloat16* src) {
     constexpr int kChunks = kTile * P / 8;
 #pragma unroll
     for (int i = tid; i < kChunks; i += NT) {
       const int row = i / (P / 8), col = (i % (P / 8)) * 8;
       const int pv = (c0 + col) >> 6, cc = (c0 + col) & 63;
       *reinterpret_cast<uint4*>(out + pv * (kTile * 64) + swz<64>(row, cc)) =
-          *reinterpret_cast<const uint4*>(sO + swz<P>(row, col));
+          *reinterpret_cast<const uint4*>(src + swz<P>(row, col));
     }
   }
 
@@ -596,7 +690,6 @@ struct IntraKernel {
     __nv_bfloat16* gKG = p.KG + chunk_head * kTile * D;
     float* gEl = p.Elast + chunk_head * D;
 
-    // ---- stage the first panel: k (+erase), v, w, per-channel decay ----
     auto load_decay = [&](int c0) {
       const float* base = p.g + (int64_t)tok0 * row_stride + (int64_t)h * D + c0;
       constexpr int kChunks = kTile * P / 4;
@@ -616,18 +709,6 @@ struct IntraKernel {
       load_tile(sV, p.v, c0);
       if (p.write != nullptr) load_tile(sW, p.write, c0);
     };
-    load_key_panel(0);
-    cp_async_commit();
-    load_value_panel(0);
-    cp_async_commit();
-    if constexpr (HEAD) head_factors(p);
-
-    float acc[4][4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
-
     auto prepare_key_panel = [&](int c0) {  // after the key panel landed
       __syncthreads();
       if (p.beta_layout != 0) {
@@ -636,6 +717,20 @@ struct IntraKernel {
       }
       if constexpr (!HEAD) channel_tables();
     };
+
+    // ---- issue every load of the first panel, then the per-token factors ----
+    load_key_panel(0);
+    cp_async_commit();
+    if constexpr (kOverlap) load_value_panel(0);
+    cp_async_commit();
+    if constexpr (HEAD) head_factors(p);
+    head_beta(p);
+
+    float acc[3][4];
+#pragma unroll
+    for (int i = 0; i < 3; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
 
     // ---- key-key scores over the channel panels ----
     for (int pn = 0; pn < Cfg::kPanels; ++pn) {
@@ -652,107 +747,57 @@ struct IntraKernel {
     }
     __syncthreads();
     store_scores(acc);
+    cp_async_wait<0>();  // every thread's copies of v and w (issued at the start) are complete
     __syncthreads();
-    solve();
 
-    // ---- w, kg and 2^G_last per channel panel ----
-    const int last = len - 1;
-    for (int pn = 0; pn < Cfg::kPanels; ++pn) {
-      const int c0 = pn * P;
-      if (Cfg::kPanels > 1) {
-        load_key_panel(c0);
-        cp_async_commit();
-        cp_async_wait<0>();
-        prepare_key_panel(c0);
-      }
-      // staging operand bf16( bf16(k*b) * 2^G )   (wy_fast.py:110-116)
-      constexpr int kChunks = kTile * P / 8;
-      for (int i = tid; i < kChunks; i += NT) {
-        const int row = i / (P / 8), col = (i % (P / 8)) * 8;
-        uint4 kv = *reinterpret_cast<const uint4*>(sK + swz<P>(row, col));
-        uint32_t* kw = reinterpret_cast<uint32_t*>(&kv);
-        uint4 kgv;
-        uint32_t* kgw = reinterpret_cast<uint32_t*>(&kgv);
-        if constexpr (ERASE) {
-          const uint4 bv = *reinterpret_cast<const uint4*>(sB + swz<P>(row, col));
-          const uint32_t* bw = reinterpret_cast<const uint32_t*>(&bv);
-          // kg uses k, the w operand uses bf16(k*b)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float k0 = bf_lo(kw[e]), k1 = bf_hi(kw[e]);
-            float e0, e1, q0, q1;
-            if constexpr (HEAD) {
-              e0 = e1 = sEh[row];
-              q0 = q1 = sKgf[row];
-            } else {
-              const float2 ev = p22(row, col + 2 * e), qv = p2d2(last, row, col + 2 * e);
-              e0 = ev.x; e1 = ev.y;
-              q0 = row < len ? qv.x : 0.f;
-              q1 = row < len ? qv.y : 0.f;
-            }
-            kgw[e] = pack_bf16x2(k0 * q0, k1 * q1);
-            kw[e] = pack_bf16x2(bf16_round(k0 * bf_lo(bw[e])) * e0, bf16_round(k1 * bf_hi(bw[e])) * e1);
-          }
-        } else {
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float k0 = bf_lo(kw[e]), k1 = bf_hi(kw[e]);
-            float e0, e1, q0, q1;
-            if constexpr (HEAD) {
-              e0 = e1 = sEh[row];
-              q0 = q1 = sKgf[row];
-            } else {
-              const float2 ev = p22(row, col + 2 * e), qv = p2d2(last, row, col + 2 * e);
-              e0 = ev.x; e1 = ev.y;
-              q0 = row < len ? qv.x : 0.f;
-              q1 = row < len ? qv.y : 0.f;
-            }
-            kgw[e] = pack_bf16x2(k0 * q0, k1 * q1);
-            kw[e] = pack_bf16x2(k0 * e0, k1 * e1);
-          }
-        }
-        *reinterpret_cast<uint4*>(sX + swz<P>(row, col)) = kv;
-        // kg in the scan's layout (wy_fast.py:125-139)
-        *reinterpret_cast<uint4*>(gKG + row * D + c0 + (swz<P>(row, col) - row * P)) = kgv;
-      }
-      if (tid < P) {
-        if constexpr (HEAD)
-          gEl[c0 + tid] = sSeg[0];
-        else
-          gEl[c0 + tid] = fast ? sE[last * Cfg::kLdE + tid] : fast_exp2(sE[last * Cfg::kLdE + tid]);
+    if constexpr (kOverlap) {
+      // warps 0-3: blocked solve; warps 4-7: u operand (v * w in place), then w operand
+      // (into the consumed w-gate tile) and kg
+      if (warp < 4) {
+        solve();
+      } else {
+        stage_u(p, 128, 128);
+        named_sync(2, 128);  // w gate consumed: sW can take the w operand
+        stage_w_kg(gKG, gEl, 0, 128, 128);
       }
       __syncthreads();
-      wy_product();
+      wy_product(sW, sO);  // w = A^-1 . w operand
       __syncthreads();
-      store_tile(gW, c0);
+      store_tile(gW, 0, sO);
+      wy_product(sV, sW);  // u = A^-1 . bf16(v*w); sW is free after the barrier above
+      __syncthreads();
+      store_u(gU, 0, sW);
+      return;
     }
 
-    // ---- u per value panel: A^-1 bf16(v * w)   (wy_fast.py:92-102) ----
+    // ---- D = 256: panels one after the other ----
+    if (warp < 4) solve();
+    __syncthreads();
     for (int pn = 0; pn < Cfg::kPanels; ++pn) {
       const int c0 = pn * P;
-      if (pn > 0) {
-        load_value_panel(c0);
-        cp_async_commit();
-      }
+      load_key_panel(c0);
+      cp_async_commit();
+      cp_async_wait<0>();
+      prepare_key_panel(c0);
+      stage_w_kg(gKG, gEl, c0, 0, NT);
+      __syncthreads();
+      wy_product(sW, sO);
+      __syncthreads();
+      store_tile(gW, c0, sO);
+      __syncthreads();
+    }
+    for (int pn = 0; pn < Cfg::kPanels; ++pn) {
+      const int c0 = pn * P;
+      load_value_panel(c0);
+      cp_async_commit();
       cp_async_wait<0>();
       __syncthreads();
-      constexpr int kChunks = kTile * P / 8;
-      for (int i = tid; i < kChunks; i += NT) {
-        const int row = i / (P / 8), col = (i % (P / 8)) * 8;
-        uint4 vv = *reinterpret_cast<const uint4*>(sV + swz<P>(row, col));
-        if (p.write != nullptr) {
-          const uint4 ww = *reinterpret_cast<const uint4*>(sW + swz<P>(row, col));
-          uint32_t* vw = reinterpret_cast<uint32_t*>(&vv);
-          const uint32_t* wg = reinterpret_cast<const uint32_t*>(&ww);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) vw[e] = pack_bf16x2(bf_lo(vw[e]) * bf_lo(wg[e]), bf_hi(vw[e]) * bf_hi(wg[e]));
-        }
-        *reinterpret_cast<uint4*>(sX + swz<P>(row, col)) = vv;
-      }
+      stage_u(p, 0, NT);
       __syncthreads();
-      wy_product();
+      wy_product(sV, sO);
       __syncthreads();
-      store_u(gU, c0);
+      store_u(gU, c0, sO);
+      __syncthreads();
     }
   }
 };
@@ -771,15 +816,15 @@ __global__ void __launch_bounds__(256) intra_kernel(IntraParams p) {
   k.sE = reinterpret_cast<float*>(base + Cfg::offE);
   k.sEi = reinterpret_cast<float*>(base + Cfg::offEi);
   k.sA = reinterpret_cast<float*>(base + Cfg::offA);
-  k.sX = reinterpret_cast<__nv_bfloat16*>(base + Cfg::offA);
   k.sAi = reinterpret_cast<__nv_bfloat16*>(base + Cfg::offAi);
-  __shared__ float s_small[kTile * 8 + Cfg::kThreads];
+  __shared__ float s_small[Cfg::kSmall];
   k.sG = s_small;
   k.sLf = s_small + kTile;
   k.sEh = s_small + 2 * kTile;
   k.sKgf = s_small + 3 * kTile;
-  k.sRf = s_small + 4 * kTile;  // [4][64]
-  k.sSeg = s_small + 8 * kTile;
+  k.sRf = s_small + 4 * kTile;  // [4][64], rows 1..3 used
+  k.sBeta = s_small + 8 * kTile;
+  k.sSeg = s_small + 9 * kTile;
   k.tid = threadIdx.x;
   k.lane = threadIdx.x & 31;
   k.warp = threadIdx.x >> 5;
