@@ -32,11 +32,13 @@ __device__ __forceinline__ float2 unpack_bf16x2(uint32_t u) {
   return __bfloat1622float2(v);
 }
 
-// fp32 -> tf32, round to nearest, ties away from zero (what Triton emits for tf32 dots).
+// fp32 -> tf32, round to nearest, ties away from zero (the rounding Triton applies to the
+// fp32 operands of its tf32 dots). On the sign-magnitude bit pattern, adding half a tf32 ulp
+// (bit 12) and clearing the 13 dropped bits rounds the magnitude half away from zero; the
+// carry into the exponent is the correct rounding, infinities are unchanged. Two integer
+// ops instead of a conversion instruction.
 __device__ __forceinline__ uint32_t to_tf32(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return r;
+  return (__float_as_uint(x) + 0x1000u) & 0xffffe000u;
 }
 
 __device__ __forceinline__ float fast_exp2(float x) {

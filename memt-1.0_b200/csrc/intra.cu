@@ -1,4 +1,5 @@
-// Launcher for the intra-chunk WY kernel (intra.cuh).
+// Launcher for the intra-chunk WY kernel (intra.cuh): a persistent grid of
+// (SM count x resident CTAs per SM) CTAs striding over the (chunk, head) units.
 #include "intra.cuh"
 #include "launch.h"
 
@@ -7,11 +8,16 @@ namespace memt {
 template <int D, bool HEAD, bool ERASE>
 static int launch_intra_t(const IntraParams& p, int64_t max_chunks, cudaStream_t s) {
   using Cfg = IntraCfg<D, HEAD, ERASE>;
-  cudaError_t e = ensure_smem(intra_kernel<D, HEAD, ERASE>, Cfg::kSmem);
+  auto kernel = intra_kernel<D, HEAD, ERASE>;
+  cudaError_t e = ensure_smem(kernel, Cfg::kSmem);
   if (e != cudaSuccess) return cuda_status(e);
-  dim3 grid(static_cast<unsigned>(max_chunks), p.H);
+  int slots = 0;
+  e = resident_slots(kernel, Cfg::kThreads, Cfg::kSmem, &slots);
+  if (e != cudaSuccess) return cuda_status(e);
+  const int64_t units = max_chunks * p.H;
+  const unsigned grid = static_cast<unsigned>(units < slots ? units : slots);
   ProfScope prof(kProfIntra, s);
-  intra_kernel<D, HEAD, ERASE><<<grid, Cfg::kThreads, Cfg::kSmem, s>>>(p);
+  kernel<<<grid, Cfg::kThreads, Cfg::kSmem, s>>>(p);
   return cuda_status(cudaGetLastError());
 }
 

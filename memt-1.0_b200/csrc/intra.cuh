@@ -97,6 +97,37 @@ __device__ __forceinline__ void warp_tf32_16x16x16(float (&acc)[2][4], const flo
     for (int nt = 0; nt < 2; ++nt) mma_tf32_1688(acc[nt], a[kq], b[kq][nt]);
 }
 
+// acc[nt] += A . (B0 + B1 [+ B2]): the B operand is the fp32 sum of two or three 16x16
+// blocks (added left to right, then rounded to tf32), as the reference sums separate dots
+// before the outer product (chunk_intra.py:377-395).
+__device__ __forceinline__ void warp_tf32_A_sumB(float (&acc)[2][4], const float* A, int lda, const float* B0,
+                                                 const float* B1, const float* B2, int ldb, int lane) {
+  const int g = lane >> 2, t = lane & 3;
+  uint32_t a[2][4], b[2][2][2];
+#pragma unroll
+  for (int kq = 0; kq < 2; ++kq) {
+    const int kk = 8 * kq;
+    a[kq][0] = to_tf32(A[g * lda + kk + t]);
+    a[kq][1] = to_tf32(A[(g + 8) * lda + kk + t]);
+    a[kq][2] = to_tf32(A[g * lda + kk + t + 4]);
+    a[kq][3] = to_tf32(A[(g + 8) * lda + kk + t + 4]);
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int o = (kk + t + 4 * e) * ldb + nt * 8 + g;
+        float s = B0[o] + B1[o];
+        if (B2 != nullptr) s += B2[o];
+        b[kq][nt][e] = to_tf32(s);
+      }
+    }
+  }
+#pragma unroll
+  for (int kq = 0; kq < 2; ++kq)
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) mma_tf32_1688(acc[nt], a[kq], b[kq][nt]);
+}
+
 __device__ __forceinline__ void zero_acc(float (&acc)[2][4]) {
 #pragma unroll
   for (int i = 0; i < 2; ++i)
@@ -163,8 +194,11 @@ struct IntraKernel {
   float *sE, *sEi, *sA;
   // per-head factors: G, left (row) factor, right factors per row block, 2^G, 2^(G_last-G),
   // bf16(sqrt(beta)) per token
-  float *sG, *sLf, *sRf, *sEh, *sKgf, *sBeta;
+  float *sG, *sLf, *sRf, *sEh, *sKgf;
+  float* sPre;  // [2][128]: per-token scalars of the current / next unit (fetch_scalars)
+  int pre;      // which half of sPre belongs to the current unit
   float* sSeg;
+  float* sScr;  // 4 fp32 16x16 scratch blocks of the blocked solve
 
   int tid, lane, warp, len, tok0, h;
   int64_t row_stride;
@@ -172,28 +206,38 @@ struct IntraKernel {
 
   // async copy of one [64][P] bf16 panel (rows >= len zero-filled) into a swizzled tile
   __device__ __forceinline__ void load_tile(__nv_bfloat16* dst, const __nv_bfloat16* src, int c0) {
-    const __nv_bfloat16* base = src + (int64_t)tok0 * row_stride + (int64_t)h * D + c0;
+    load_tile_for(dst, src, c0, tok0, len, h, 0, NT);
+  }
+  // the same for an explicit (token range, head) and the threads [t0, t0 + n)
+  __device__ __forceinline__ void load_tile_for(__nv_bfloat16* dst, const __nv_bfloat16* src, int c0, int tk0,
+                                                int ln, int hd, int t0, int n) {
+    const __nv_bfloat16* base = src + (int64_t)tk0 * row_stride + (int64_t)hd * D + c0;
     constexpr int kChunks = kTile * P / 8;
-#pragma unroll
-    for (int i = tid; i < kChunks; i += NT) {
+    const int len = ln;
+    for (int i = tid - t0; i < kChunks; i += n) {
       const int row = i / (P / 8), col = (i % (P / 8)) * 8;
       const bool valid = row < len;
       cp_async16_zfill(dst + swz<P>(row, col), valid ? base + (int64_t)row * row_stride + col : src, valid);
     }
   }
 
-  // per-token bf16(sqrt(beta)) of a per-head beta (warp 1)
-  __device__ void head_beta(const IntraParams& p) {
-    if (warp != 1 || p.beta_layout != 1) return;
-#pragma unroll
-    for (int q = 0; q < 2; ++q) {
-      const int i = 2 * lane + q;
-      sBeta[i] = i < len ? bf16_round(sqrtf(__bfloat162float(p.beta[(int64_t)(tok0 + i) * p.H + h]))) : 0.f;
+  // Per-token scalars of a unit into buf: [0, 64) the per-head log-decay, [64, 128)
+  // bf16(sqrt(beta)) of a per-head beta. Threads [t0, t0 + 64); issued one unit ahead so the
+  // global-load latency hides behind the previous unit's solve.
+  __device__ void fetch_scalars(const IntraParams& p, int tk0, int ln, int hd, float* buf, int t0) {
+    const int i = tid - t0;
+    if (i < 0 || i >= kTile) return;
+    float gv = 0.f, bv = 0.f;
+    if (i < ln) {
+      if constexpr (HEAD) gv = p.g[(int64_t)(tk0 + i) * p.H + hd];
+      if (p.beta_layout == 1) bv = bf16_round(sqrtf(__bfloat162float(p.beta[(int64_t)(tk0 + i) * p.H + hd])));
     }
+    buf[i] = gv;
+    buf[kTile + i] = bv;
   }
 
   // Fold sqrt(beta) into k in place: k' = bf16( bf16(sqrt(beta)) * k ) (models/qwen/layer.py:81-96)
-  __device__ void fold_beta(const IntraParams& p, int c0) {
+  __device__ void fold_beta(const IntraParams& p, __nv_bfloat16* sK, int c0) {
     constexpr int kChunks = kTile * P / 8;
     for (int i = tid; i < kChunks; i += NT) {
       const int row = i / (P / 8), col = (i % (P / 8)) * 8;
@@ -202,7 +246,7 @@ struct IntraKernel {
       uint4 kv = *ptr;
       float sb[8];
       if (p.beta_layout == 1) {
-        const float s = sBeta[row];
+        const float s = sPre[pre * 2 * kTile + kTile + row];
 #pragma unroll
         for (int e = 0; e < 8; ++e) sb[e] = s;
       } else {
@@ -227,8 +271,8 @@ struct IntraKernel {
     if (warp != 0) return;
     // G_t = (sum_{s<=t} g_s) / ln2 over the 64 tokens; lane owns tokens 2*lane, 2*lane+1
     const int t0 = 2 * lane, t1 = 2 * lane + 1;
-    const float g0 = t0 < len ? p.g[(int64_t)(tok0 + t0) * p.H + h] : 0.f;
-    const float g1 = t1 < len ? p.g[(int64_t)(tok0 + t1) * p.H + h] : 0.f;
+    const float g0 = sPre[pre * 2 * kTile + t0];  // zero beyond the chunk
+    const float g1 = sPre[pre * 2 * kTile + t1];
     float s = g0 + g1;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -312,7 +356,7 @@ struct IntraKernel {
   }
 
   // ---- key-key scores of this panel, accumulated into acc[piece] ----
-  __device__ void scores_panel(float (&acc)[3][4]) {
+  __device__ void scores_panel(float (&acc)[3][4], const __nv_bfloat16* sK) {
     int r, nts[3];
     score_pieces(warp, r, nts);
     if (16 * r >= len) return;  // whole row block beyond the chunk (chunk_intra.py:242-278)
@@ -330,7 +374,7 @@ struct IntraKernel {
       for (int s = 0; s < 3; ++s)
         if (nts[s] >= 0 && (nts[s] >> 1) < r) rf[s] = sRf[r * kTile + 8 * nts[s] + g];
     }
-#pragma unroll 1
+#pragma unroll 2
     for (int kk = 0; kk < P / 16; ++kk) {
       // all fragment loads of the k-step first
       uint32_t a[4], eb[4] = {0u, 0u, 0u, 0u}, bq[3][2];
@@ -531,31 +575,38 @@ struct IntraKernel {
       warp_store_block(Ao(s + 1, s), LD, Ab(s + 1, s), LDI, acc, lane, -1.f, 16 * (s + 1), len);
     }
     named_sync(1, 128);
-    if (warp < 2) {  // Ai20, Ai31
-      const int r = warp + 2;
-      float* dst = Ao(r, r - 2);
+    // Ai20 = -Ai22 (Akk20 Ai00 + Akk21 Ai10), Ai31 = -Ai33 (Akk31 Ai11 + Akk32 Ai21):
+    // one dot per warp into the scratch blocks, then the two outer products
+    {
+      constexpr int LS = 16;
+      // warp 0: Akk20 Ai00, 1: Akk21 Ai10, 2: Akk31 Ai11, 3: Akk32 Ai21
+      const int lr = 2 + (warp >> 1), ls = (warp >> 1) + (warp & 1);
+      const float* rhs = (warp & 1) ? Ao(ls, ls - 1) : Dg(ls);
       zero_acc(acc);
-      warp_tf32_16x16x16(acc, Ak(r, r - 2), LD, Dg(r - 2), LD, lane);
-      warp_tf32_16x16x16(acc, Ak(r, r - 1), LD, Ao(r - 1, r - 2), LD, lane);
-      warp_store_f32(dst, LD, acc, lane);
-      __syncwarp();
-      zero_acc(acc);
-      warp_tf32_16x16x16(acc, Dg(r), LD, dst, LD, lane);
-      __syncwarp();
-      warp_store_block(dst, LD, Ab(r, r - 2), LDI, acc, lane, -1.f, 16 * r, len);
-    }
-    named_sync(1, 128);
-    if (warp == 0) {  // Ai30
-      float* dst = Ao(3, 0);
-      zero_acc(acc);
-      warp_tf32_16x16x16(acc, Ak(3, 0), LD, Dg(0), LD, lane);
-      warp_tf32_16x16x16(acc, Ak(3, 1), LD, Ao(1, 0), LD, lane);
-      warp_tf32_16x16x16(acc, Ak(3, 2), LD, Ao(2, 0), LD, lane);
-      warp_store_f32(dst, LD, acc, lane);
-      __syncwarp();
-      zero_acc(acc);
-      warp_tf32_16x16x16(acc, Dg(3), LD, dst, LD, lane);
-      warp_store_block(nullptr, LD, Ab(3, 0), LDI, acc, lane, -1.f, 48, len);
+      warp_tf32_16x16x16(acc, Ak(lr, ls), LD, rhs, LD, lane);
+      warp_store_f32(sScr + warp * 256, LS, acc, lane);
+      named_sync(1, 128);
+      if (warp < 2) {
+        const int r = warp + 2;
+        zero_acc(acc);
+        warp_tf32_A_sumB(acc, Dg(r), LD, sScr + (2 * warp) * 256, sScr + (2 * warp + 1) * 256, nullptr, LS, lane);
+        warp_store_block(Ao(r, r - 2), LD, Ab(r, r - 2), LDI, acc, lane, -1.f, 16 * r, len);
+      }
+      named_sync(1, 128);
+      // Ai30 = -Ai33 (Akk30 Ai00 + Akk31 Ai10 + Akk32 Ai20)
+      if (warp < 3) {
+        // warp s: Akk3s Ai_s0
+        const float* rhs = (warp == 0) ? Dg(0) : Ao(warp, 0);
+        zero_acc(acc);
+        warp_tf32_16x16x16(acc, Ak(3, warp), LD, rhs, LD, lane);
+        warp_store_f32(sScr + warp * 256, LS, acc, lane);
+      }
+      named_sync(1, 128);
+      if (warp == 0) {
+        zero_acc(acc);
+        warp_tf32_A_sumB(acc, Dg(3), LD, sScr, sScr + 256, sScr + 512, LS, lane);
+        warp_store_block(nullptr, LD, Ab(3, 0), LDI, acc, lane, -1.f, 48, len);
+      }
     }
   }
 
@@ -575,14 +626,14 @@ struct IntraKernel {
     }
   }
 
-  // w operand bf16( bf16(k*b) * 2^G ) into sW (wy_fast.py:110-116), kg = bf16(k 2^(G_last-G))
+  // w operand bf16( bf16(k*b) * 2^G ) in place of k (wy_fast.py:110-116), kg = bf16(k 2^(G_last-G))
   // to global (wy_fast.py:125-139) and 2^G_last; threads [t0, t0 + n)
-  __device__ void stage_w_kg(__nv_bfloat16* gKG, float* gEl, int c0, int t0, int n) {
+  __device__ void stage_w_kg(__nv_bfloat16* kt, __nv_bfloat16* gKG, float* gEl, int c0, int t0, int n) {
     const int last = len - 1;
     constexpr int kChunks = kTile * P / 8;
     for (int i = tid - t0; i < kChunks; i += n) {
       const int row = i / (P / 8), col = (i % (P / 8)) * 8;
-      uint4 kv = *reinterpret_cast<const uint4*>(sK + swz<P>(row, col));
+      uint4 kv = *reinterpret_cast<const uint4*>(kt + swz<P>(row, col));
       uint32_t* kw = reinterpret_cast<uint32_t*>(&kv);
       uint4 kgv;
       uint32_t* kgw = reinterpret_cast<uint32_t*>(&kgv);
@@ -609,7 +660,7 @@ struct IntraKernel {
         else
           kw[e] = pack_bf16x2(k0 * e0, k1 * e1);
       }
-      *reinterpret_cast<uint4*>(sW + swz<P>(row, col)) = kv;
+      *reinterpret_cast<uint4*>(kt + swz<P>(row, col)) = kv;  // w operand replaces k in place
       *reinterpret_cast<uint4*>(gKG + row * D + c0 + (swz<P>(row, col) - row * P)) = kgv;
     }
     const int j = tid - t0;
@@ -676,19 +727,24 @@ struct IntraKernel {
     }
   }
 
-  __device__ void run(const IntraParams& p) {
-    const int c = blockIdx.x;
-    if (c >= p.hdr->num_chunks) return;
+  // ---- persistent loop over (chunk, head) units: unit = chunk * H + head ----
+  __device__ void set_unit(const IntraParams& p, int64_t unit) {
+    const int c = static_cast<int>(unit / p.H);
+    h = static_cast<int>(unit % p.H);
     const ChunkDesc d = p.table[c];
     tok0 = d.tok0;
     len = d.len;
-    h = blockIdx.y;
+  }
+
+  __device__ void run(const IntraParams& p) {
+    const int64_t units = (int64_t)p.hdr->num_chunks * p.H;
+    int64_t unit = blockIdx.x;
+    if (unit >= units) return;
     row_stride = (int64_t)p.H * D;
-    const int64_t chunk_head = (int64_t)c * p.H + h;
-    __nv_bfloat16* gW = p.W + chunk_head * kTile * D;
-    __nv_bfloat16* gU = p.U + chunk_head * kTile * D;
-    __nv_bfloat16* gKG = p.KG + chunk_head * kTile * D;
-    float* gEl = p.Elast + chunk_head * D;
+    // next unit's k streams into the spare tile during the solve (per-head decay, no erase)
+    constexpr bool kPrefetch = kOverlap && HEAD && !ERASE;
+    __nv_bfloat16* kcur = sK;
+    __nv_bfloat16* kspare = sO;
 
     auto load_decay = [&](int c0) {
       const float* base = p.g + (int64_t)tok0 * row_stride + (int64_t)h * D + c0;
@@ -701,7 +757,7 @@ struct IntraKernel {
       }
     };
     auto load_key_panel = [&](int c0) {
-      load_tile(sK, p.k, c0);
+      load_tile(kcur, p.k, c0);
       if constexpr (ERASE) load_tile(sB, p.erase, c0);
       if constexpr (!HEAD) load_decay(c0);
     };
@@ -712,98 +768,131 @@ struct IntraKernel {
     auto prepare_key_panel = [&](int c0) {  // after the key panel landed
       __syncthreads();
       if (p.beta_layout != 0) {
-        fold_beta(p, c0);
+        fold_beta(p, kcur, c0);
         __syncthreads();
       }
       if constexpr (!HEAD) channel_tables();
     };
 
-    // ---- issue every load of the first panel, then the per-token factors ----
+    set_unit(p, unit);
     load_key_panel(0);
     cp_async_commit();
-    if constexpr (kOverlap) load_value_panel(0);
-    cp_async_commit();
-    if constexpr (HEAD) head_factors(p);
-    head_beta(p);
+    pre = 0;
+    fetch_scalars(p, tok0, len, h, sPre, 0);
+    for (;;) {
+      const int64_t next = unit + gridDim.x;
+      const bool has_next = next < units;
+      const int64_t chunk_head = unit;  // == chunk * H + head
+      __nv_bfloat16* gW = p.W + chunk_head * kTile * D;
+      __nv_bfloat16* gU = p.U + chunk_head * kTile * D;
+      __nv_bfloat16* gKG = p.KG + chunk_head * kTile * D;
+      float* gEl = p.Elast + chunk_head * D;
 
-    float acc[3][4];
-#pragma unroll
-    for (int i = 0; i < 3; ++i)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+      if constexpr (kOverlap) load_value_panel(0);
+      cp_async_commit();
+      if constexpr (HEAD) {
+        __syncthreads();  // the unit's scalars (fetched one unit ahead) are visible
+        head_factors(p);
+      }
 
-    // ---- key-key scores over the channel panels ----
-    for (int pn = 0; pn < Cfg::kPanels; ++pn) {
-      if (pn > 0) {
+      float acc[3][4];
+#pragma unroll
+      for (int i = 0; i < 3; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+
+      // ---- key-key scores over the channel panels ----
+      for (int pn = 0; pn < Cfg::kPanels; ++pn) {
+        if (pn > 0) {
+          __syncthreads();
+          load_key_panel(pn * P);
+          cp_async_commit();
+          cp_async_wait<0>();
+        } else {
+          cp_async_wait<1>();  // the key group (older than the value group) landed
+        }
+        prepare_key_panel(pn * P);
+        scores_panel(acc, kcur);
+      }
+      __syncthreads();
+      store_scores(acc);
+      cp_async_wait<0>();  // every thread's copies of v and w are complete
+      __syncthreads();
+
+      if constexpr (kOverlap) {
+        // warps 0-3: blocked solve; warps 4-7: prefetch of the next unit's k, u operand
+        // (v * w in place), then w operand (in place of k) and kg
+        if (warp < 4) {
+          solve();
+        } else {
+          if (has_next) {
+            const int c2 = static_cast<int>(next / p.H), h2 = static_cast<int>(next % p.H);
+            const ChunkDesc d2 = p.table[c2];
+            fetch_scalars(p, d2.tok0, d2.len, h2, sPre + (pre ^ 1) * 2 * kTile, 128);
+            if constexpr (kPrefetch) load_tile_for(kspare, p.k, 0, d2.tok0, d2.len, h2, 128, 128);
+          }
+          if constexpr (kPrefetch) cp_async_commit();
+          stage_u(p, 128, 128);
+          named_sync(2, 128);
+          stage_w_kg(kcur, gKG, gEl, 0, 128, 128);
+        }
         __syncthreads();
-        load_key_panel(pn * P);
+        wy_product(kcur, sW);  // w = A^-1 . w operand; the w-gate tile is free
+        __syncthreads();
+        store_tile(gW, 0, sW);
+        wy_product(sV, kcur);  // u = A^-1 . bf16(v*w); the w operand is consumed
+        __syncthreads();
+        store_u(gU, 0, kcur);
+      } else {
+        // ---- D = 256: panels one after the other ----
+        if (warp < 4) solve();
+        __syncthreads();
+        for (int pn = 0; pn < Cfg::kPanels; ++pn) {
+          const int c0 = pn * P;
+          load_key_panel(c0);
+          cp_async_commit();
+          cp_async_wait<0>();
+          prepare_key_panel(c0);
+          stage_w_kg(kcur, gKG, gEl, c0, 0, NT);
+          __syncthreads();
+          wy_product(kcur, sO);
+          __syncthreads();
+          store_tile(gW, c0, sO);
+          __syncthreads();
+        }
+        for (int pn = 0; pn < Cfg::kPanels; ++pn) {
+          const int c0 = pn * P;
+          load_value_panel(c0);
+          cp_async_commit();
+          cp_async_wait<0>();
+          __syncthreads();
+          stage_u(p, 0, NT);
+          __syncthreads();
+          wy_product(sV, sO);
+          __syncthreads();
+          store_u(gU, c0, sO);
+        }
+      }
+      if (!has_next) break;
+      unit = next;
+      set_unit(p, unit);
+      __syncthreads();  // the last tile stores read shared memory the next unit overwrites
+      if constexpr (!kOverlap) fetch_scalars(p, tok0, len, h, sPre + (pre ^ 1) * 2 * kTile, 0);
+      pre ^= 1;
+      if constexpr (kPrefetch) {
+        __nv_bfloat16* tmp = kcur;
+        kcur = kspare;
+        kspare = tmp;
+      } else {
+        load_key_panel(0);
         cp_async_commit();
-        cp_async_wait<0>();
-      } else {
-        cp_async_wait<1>();
       }
-      prepare_key_panel(pn * P);
-      scores_panel(acc);
-    }
-    __syncthreads();
-    store_scores(acc);
-    cp_async_wait<0>();  // every thread's copies of v and w (issued at the start) are complete
-    __syncthreads();
-
-    if constexpr (kOverlap) {
-      // warps 0-3: blocked solve; warps 4-7: u operand (v * w in place), then w operand
-      // (into the consumed w-gate tile) and kg
-      if (warp < 4) {
-        solve();
-      } else {
-        stage_u(p, 128, 128);
-        named_sync(2, 128);  // w gate consumed: sW can take the w operand
-        stage_w_kg(gKG, gEl, 0, 128, 128);
-      }
-      __syncthreads();
-      wy_product(sW, sO);  // w = A^-1 . w operand
-      __syncthreads();
-      store_tile(gW, 0, sO);
-      wy_product(sV, sW);  // u = A^-1 . bf16(v*w); sW is free after the barrier above
-      __syncthreads();
-      store_u(gU, 0, sW);
-      return;
-    }
-
-    // ---- D = 256: panels one after the other ----
-    if (warp < 4) solve();
-    __syncthreads();
-    for (int pn = 0; pn < Cfg::kPanels; ++pn) {
-      const int c0 = pn * P;
-      load_key_panel(c0);
-      cp_async_commit();
-      cp_async_wait<0>();
-      prepare_key_panel(c0);
-      stage_w_kg(gKG, gEl, c0, 0, NT);
-      __syncthreads();
-      wy_product(sW, sO);
-      __syncthreads();
-      store_tile(gW, c0, sO);
-      __syncthreads();
-    }
-    for (int pn = 0; pn < Cfg::kPanels; ++pn) {
-      const int c0 = pn * P;
-      load_value_panel(c0);
-      cp_async_commit();
-      cp_async_wait<0>();
-      __syncthreads();
-      stage_u(p, 0, NT);
-      __syncthreads();
-      wy_product(sV, sO);
-      __syncthreads();
-      store_u(gU, c0, sO);
-      __syncthreads();
     }
   }
 };
 
 template <int D, bool HEAD, bool ERASE>
-__global__ void __launch_bounds__(256) intra_kernel(IntraParams p) {
+__global__ void __launch_bounds__(256, 2) intra_kernel(IntraParams p) {
   extern __shared__ __align__(128) unsigned char smem_intra[];
   using Cfg = IntraCfg<D, HEAD, ERASE>;
   IntraKernel<D, HEAD, ERASE> k;
@@ -818,12 +907,15 @@ __global__ void __launch_bounds__(256) intra_kernel(IntraParams p) {
   k.sA = reinterpret_cast<float*>(base + Cfg::offA);
   k.sAi = reinterpret_cast<__nv_bfloat16*>(base + Cfg::offAi);
   __shared__ float s_small[Cfg::kSmall];
+  __shared__ __align__(16) float s_scr[4 * 256];
+  k.sScr = s_scr;
   k.sG = s_small;
   k.sLf = s_small + kTile;
   k.sEh = s_small + 2 * kTile;
   k.sKgf = s_small + 3 * kTile;
   k.sRf = s_small + 4 * kTile;  // [4][64], rows 1..3 used
-  k.sBeta = s_small + 8 * kTile;
+  __shared__ float s_pre[4 * kTile];
+  k.sPre = s_pre;
   k.sSeg = s_small + 9 * kTile;
   k.tid = threadIdx.x;
   k.lane = threadIdx.x & 31;

@@ -3,6 +3,7 @@
 
 #include <cuda_runtime.h>
 
+#include <map>
 #include <mutex>
 #include <set>
 #include <utility>
@@ -42,6 +43,31 @@ struct ProfScope {
   ProfScope(int family, cudaStream_t stream) : s(stream) { prof_begin(family, stream, &token); }
   ~ProfScope() { prof_end(token, s); }
 };
+
+// CTAs of this kernel that fit on the device at once (SM count x occupancy), cached per
+// (kernel, device).
+template <typename Kernel>
+cudaError_t resident_slots(Kernel kernel, int threads, size_t smem, int* slots) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> cache;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  auto key = std::make_pair(reinterpret_cast<const void*>(kernel), dev);
+  auto it = cache.find(key);
+  if (it != cache.end()) {
+    *slots = it->second;
+    return cudaSuccess;
+  }
+  int sms = 0, per_sm = 0;
+  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem);
+  if (e != cudaSuccess) return e;
+  *slots = sms * (per_sm > 0 ? per_sm : 1);
+  cache[key] = *slots;
+  return cudaSuccess;
+}
 
 int launch_plan(const int32_t* cu, int32_t N, int64_t L, int32_t chunk_tokens, int32_t max_chunks,
                 WsHeader* hdr, ChunkDesc* table, int32_t* sample_off, cudaStream_t s);
