@@ -7,14 +7,19 @@ namespace memt {
 constexpr int kGemvTokens = 4;     // tokens per GEMV CTA
 constexpr int kGemvMaxBlock = 16;  // blocks up to this many tokens use the GEMV kernel
 
+// decode (one token per block) uses a one-token CTA; otherwise kGemvTokens per CTA
 template <int D, bool EXACT>
 static int launch_gemv(const ReadParams& p, int64_t maxlen, cudaStream_t s) {
-  int64_t groups = (maxlen + kGemvTokens - 1) / kGemvTokens;
+  const int tq = maxlen <= 1 ? 1 : kGemvTokens;
+  int64_t groups = (maxlen + tq - 1) / tq;
   if (groups < 1) groups = 1;
   if (groups > 65535) return MEMT_ERR_UNSUPPORTED;
   dim3 grid(static_cast<unsigned>(p.num_blocks) * p.H, static_cast<unsigned>(groups));
   ProfScope prof(kProfReadGemv, s);
-  read_gemv_kernel<D, kGemvTokens, EXACT><<<grid, 256, 0, s>>>(p);
+  if (tq == 1)
+    read_gemv_kernel<D, 1, EXACT><<<grid, 256, 0, s>>>(p);
+  else
+    read_gemv_kernel<D, kGemvTokens, EXACT><<<grid, 256, 0, s>>>(p);
   return cuda_status(cudaGetLastError());
 }
 

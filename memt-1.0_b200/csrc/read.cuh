@@ -36,12 +36,25 @@ __device__ __forceinline__ float gated_norm_value(float o, float rstd, float w, 
 }
 
 // ---------------------------------------------------------------------------
-// GEMV: CTA = (block, head, group of TQ tokens), 256 threads
+// GEMV: CTA = (block, head, group of TQ tokens), 256 threads.
+// The fp32 state is the only large operand, so every thread issues its state loads
+// (16 x 128-bit for D = 128, double-buffered batches for D = 256) before the query,
+// gate and residual loads and the query normalisation: the state stream and the
+// prologue latencies overlap and each SM keeps >= 64 KB in flight.
 // ---------------------------------------------------------------------------
+template <int D>
+struct GemvCfg {
+  static constexpr int kTPR = D / 4;                     // threads per state row (one float4 each)
+  static constexpr int kRPP = 256 / kTPR;                // rows per pass
+  static constexpr int kPer = D / kRPP;                  // float4 loads per thread
+  static constexpr int kBatch = kPer < 16 ? kPer : (D >= 256 ? 8 : 16);
+  static constexpr int kBatches = kPer / kBatch;
+};
+
 template <int D, int TQ, bool EXACT>
-__global__ void __launch_bounds__(256) read_gemv_kernel(ReadParams p) {
-  constexpr int TPR = D / 4;        // threads per state row (one float4 each)
-  constexpr int RPP = 256 / TPR;    // rows per pass
+__global__ void __launch_bounds__(256, 2) read_gemv_kernel(ReadParams p) {
+  using Cfg = GemvCfg<D>;
+  constexpr int RPP = Cfg::kRPP, TPR = Cfg::kTPR, BATCH = Cfg::kBatch;
   __shared__ float s_q[TQ][D];
   __shared__ float s_red[RPP][TQ][D];
   __shared__ float s_ss[TQ][8];
@@ -54,7 +67,29 @@ __global__ void __launch_bounds__(256) read_gemv_kernel(ReadParams p) {
   const int nt = (int)((eos - t0) < TQ ? (eos - t0) : TQ);
   const int64_t qrow = (int64_t)p.H * D;
 
-  // queries (optionally l2-normalised, fp32 sum of squares, bf16 output as in FLA l2norm)
+  // 1. state stream: first batch in flight before anything else
+  const int cg = tid % TPR, ro = tid / TPR;
+  const float4* S4 = reinterpret_cast<const float4*>(p.states + ((int64_t)n * p.H + h) * D * D) + ro * TPR + cg;
+  float4 cur[BATCH];
+#pragma unroll
+  for (int i = 0; i < BATCH; ++i) cur[i] = __ldg(S4 + (int64_t)i * RPP * TPR);
+
+  // 2. prologue loads: queries, and for the fused epilogue this thread's gate and residual
+  const int v = tid;
+  float gt[TQ], res[TQ];
+#pragma unroll
+  for (int j = 0; j < TQ; ++j) gt[j] = res[j] = 0.f;
+  if (p.fused && v < D) {
+#pragma unroll
+    for (int j = 0; j < TQ; ++j) {
+      if (j < nt) {
+        const int64_t tok = t0 + j;
+        gt[j] = __bfloat162float(p.gate[tok * qrow + (int64_t)h * D + v]);
+        if (p.residual != nullptr)
+          res[j] = __bfloat162float(p.residual[tok * p.row_stride + (int64_t)(p.head_offset + h) * D + v]);
+      }
+    }
+  }
   for (int idx = tid; idx < TQ * D; idx += 256) {
     const int j = idx / D, c = idx % D;
     float x = 0.f;
@@ -66,6 +101,7 @@ __global__ void __launch_bounds__(256) read_gemv_kernel(ReadParams p) {
     s_q[j][c] = x;
   }
   __syncthreads();
+  // queries optionally l2-normalised (fp32 sum of squares, bf16 output as in FLA l2norm)
   if (p.normalize_q) {
     const int warp = tid >> 5, lane = tid & 31;
     if (warp < TQ) {
@@ -82,27 +118,39 @@ __global__ void __launch_bounds__(256) read_gemv_kernel(ReadParams p) {
     __syncthreads();
   }
 
-  const int cg = tid % TPR, ro = tid / TPR;
-  const float4* S4 = reinterpret_cast<const float4*>(p.states + ((int64_t)n * p.H + h) * D * D);
+  // 3. products, batch by batch (the next batch is in flight while one is consumed)
   float acc[TQ][4];
 #pragma unroll
   for (int j = 0; j < TQ; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-#pragma unroll 8
-  for (int row = ro; row < D; row += RPP) {
-    float4 s = __ldg(S4 + row * TPR + cg);
-    if (!EXACT) {
-      s.x = bf16_round(s.x);
-      s.y = bf16_round(s.y);
-      s.z = bf16_round(s.z);
-      s.w = bf16_round(s.w);
+#pragma unroll
+  for (int b = 0; b < Cfg::kBatches; ++b) {
+    float4 nxt[BATCH];
+    if (b + 1 < Cfg::kBatches) {
+#pragma unroll
+      for (int i = 0; i < BATCH; ++i) nxt[i] = __ldg(S4 + (int64_t)((b + 1) * BATCH + i) * RPP * TPR);
     }
 #pragma unroll
-    for (int j = 0; j < TQ; ++j) {
-      const float qv = s_q[j][row];
-      acc[j][0] = fmaf(qv, s.x, acc[j][0]);
-      acc[j][1] = fmaf(qv, s.y, acc[j][1]);
-      acc[j][2] = fmaf(qv, s.z, acc[j][2]);
-      acc[j][3] = fmaf(qv, s.w, acc[j][3]);
+    for (int i = 0; i < BATCH; ++i) {
+      float4 s = cur[i];
+      if (!EXACT) {
+        s.x = bf16_round(s.x);
+        s.y = bf16_round(s.y);
+        s.z = bf16_round(s.z);
+        s.w = bf16_round(s.w);
+      }
+      const int row = ro + (b * BATCH + i) * RPP;
+#pragma unroll
+      for (int j = 0; j < TQ; ++j) {
+        const float qv = s_q[j][row];
+        acc[j][0] = fmaf(qv, s.x, acc[j][0]);
+        acc[j][1] = fmaf(qv, s.y, acc[j][1]);
+        acc[j][2] = fmaf(qv, s.z, acc[j][2]);
+        acc[j][3] = fmaf(qv, s.w, acc[j][3]);
+      }
+    }
+    if (b + 1 < Cfg::kBatches) {
+#pragma unroll
+      for (int i = 0; i < BATCH; ++i) cur[i] = nxt[i];
     }
   }
 #pragma unroll
@@ -112,12 +160,12 @@ __global__ void __launch_bounds__(256) read_gemv_kernel(ReadParams p) {
 
   if (!p.fused) {
     for (int idx = tid; idx < nt * D; idx += 256) {
-      const int j = idx / D, v = idx % D;
+      const int j = idx / D, c = idx % D;
       float o = 0.f;
 #pragma unroll
-      for (int r = 0; r < RPP; ++r) o += s_red[r][j][v];
+      for (int r = 0; r < RPP; ++r) o += s_red[r][j][c];
       o *= p.scale;
-      const int64_t off = (t0 + j) * qrow + (int64_t)h * D + v;
+      const int64_t off = (t0 + j) * qrow + (int64_t)h * D + c;
       if (p.out_bf16)
         static_cast<__nv_bfloat16*>(p.out)[off] = __float2bfloat16_rn(o);
       else
@@ -126,8 +174,7 @@ __global__ void __launch_bounds__(256) read_gemv_kernel(ReadParams p) {
     return;
   }
 
-  // fused epilogue: one value per thread and token (D <= 256)
-  const int v = tid;
+  // 4. fused epilogue: one value per thread and token (D <= 256)
   float o[TQ];
 #pragma unroll
   for (int j = 0; j < TQ; ++j) {
@@ -146,16 +193,17 @@ __global__ void __launch_bounds__(256) read_gemv_kernel(ReadParams p) {
   __syncthreads();
   if (v < D) {
     const float w = __bfloat162float(p.norm_w[v]);
-    for (int j = 0; j < nt; ++j) {
+#pragma unroll
+    for (int j = 0; j < TQ; ++j) {
+      if (j >= nt) break;
       float ss = 0.f;
 #pragma unroll
       for (int wi = 0; wi < 8; ++wi) ss += s_ss[j][wi];
       const float rstd = rsqrtf(ss / D + p.norm_eps);
       const int64_t tok = t0 + j;
-      const float gt = __bfloat162float(p.gate[tok * qrow + (int64_t)h * D + v]);
-      float y = bf16_round(gated_norm_value(o[j], rstd, w, gt, p.softcap));
+      float y = bf16_round(gated_norm_value(o[j], rstd, w, gt[j], p.softcap));
       const int64_t oo = tok * p.row_stride + (int64_t)(p.head_offset + h) * D + v;
-      if (p.residual != nullptr) y = __bfloat162float(p.residual[oo]) + y;
+      if (p.residual != nullptr) y = res[j] + y;
       static_cast<__nv_bfloat16*>(p.out)[oo] = __float2bfloat16_rn(y);
     }
   }
