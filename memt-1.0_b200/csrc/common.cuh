@@ -126,6 +126,9 @@ __device__ __forceinline__ void mbar_fence_init() {
 __device__ __forceinline__ void mbar_expect_tx(uint32_t mbar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(mbar), "r"(bytes));
 }
+__device__ __forceinline__ void mbar_arrive(uint32_t mbar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(mbar) : "memory");
+}
 // Bounded wait for the phase with the given parity; false after ~2^24 polls (seconds).
 __device__ __forceinline__ bool mbar_wait(uint32_t mbar, uint32_t parity) {
   for (int i = 0; i < (1 << 24); ++i) {
@@ -155,6 +158,14 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
 template <int RL>
 __device__ __forceinline__ int swz(int row, int col) {
   return row * RL + ((((col >> 3) ^ row) & 7) | ((col >> 3) & ~7)) * 8 + (col & 7);
+}
+
+// Element offset in a bf16 [64][D] tile stored as D/64 panels of [64][64], each swz<64>:
+// 128-byte rows whose 16-byte chunks are XOR-permuted by (row & 7). With a 1024-byte aligned
+// base this is the canonical SWIZZLE_128B operand layout of tcgen05 shared-memory
+// descriptors (K-major when the 64 columns are the reduction index, MN-major otherwise).
+__device__ __forceinline__ int pswz(int row, int col) {
+  return (col >> 6) * (kTile * 64) + swz<64>(row, col & 63);
 }
 
 // ---------------------------------------------------------------------------

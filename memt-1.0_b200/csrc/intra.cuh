@@ -661,7 +661,7 @@ struct IntraKernel {
           kw[e] = pack_bf16x2(k0 * e0, k1 * e1);
       }
       *reinterpret_cast<uint4*>(kt + swz<P>(row, col)) = kv;  // w operand replaces k in place
-      *reinterpret_cast<uint4*>(gKG + row * D + c0 + (swz<P>(row, col) - row * P)) = kgv;
+      *reinterpret_cast<uint4*>(gKG + pswz(row, c0 + col)) = kgv;
     }
     const int j = tid - t0;
     if (j >= 0 && j < P) {
@@ -704,26 +704,15 @@ struct IntraKernel {
     }
   }
 
-  // sO -> global tile [64][D] in the scan's layout swz<D>: row r holds the shared row image of
-  // each 128-wide panel unchanged (for D = 256 the XOR acts on the low three chunk bits only,
-  // so the panel images at c0 = 0 and 128 concatenate to swz<256>). 16-byte coalesced stores.
-  __device__ void store_tile(__nv_bfloat16* out, int c0, const __nv_bfloat16* src) {
-    constexpr int kChunks = kTile * P / 8;
-#pragma unroll
-    for (int i = tid; i < kChunks; i += NT) {
-      const int row = i / (P / 8), j = (i % (P / 8)) * 8;
-      *reinterpret_cast<uint4*>(out + row * D + c0 + j) = *reinterpret_cast<const uint4*>(src + row * P + j);
-    }
-  }
-  // sO -> u in the scan's value-panel layout [D/64][64][64], each panel swz<64>
-  __device__ void store_u(__nv_bfloat16* out, int c0, const __nv_bfloat16* src) {
+  // shared [64][P] tile (swz<P>) -> global [64][D] tile in the panel layout the scan reads
+  // (pswz: 64-column panels, each swz<64>, the canonical 128-byte-swizzled operand layout of
+  // the tensor-core descriptors); 16-byte stores
+  __device__ void store_panels(__nv_bfloat16* out, int c0, const __nv_bfloat16* src) {
     constexpr int kChunks = kTile * P / 8;
 #pragma unroll
     for (int i = tid; i < kChunks; i += NT) {
       const int row = i / (P / 8), col = (i % (P / 8)) * 8;
-      const int pv = (c0 + col) >> 6, cc = (c0 + col) & 63;
-      *reinterpret_cast<uint4*>(out + pv * (kTile * 64) + swz<64>(row, cc)) =
-          *reinterpret_cast<const uint4*>(src + swz<P>(row, col));
+      *reinterpret_cast<uint4*>(out + pswz(row, c0 + col)) = *reinterpret_cast<const uint4*>(src + swz<P>(row, col));
     }
   }
 
@@ -839,10 +828,10 @@ struct IntraKernel {
         __syncthreads();
         wy_product(kcur, sW);  // w = A^-1 . w operand; the w-gate tile is free
         __syncthreads();
-        store_tile(gW, 0, sW);
+        store_panels(gW, 0, sW);
         wy_product(sV, kcur);  // u = A^-1 . bf16(v*w); the w operand is consumed
         __syncthreads();
-        store_u(gU, 0, kcur);
+        store_panels(gU, 0, kcur);
       } else {
         // ---- D = 256: panels one after the other ----
         if (warp < 4) solve();
@@ -857,7 +846,7 @@ struct IntraKernel {
           __syncthreads();
           wy_product(kcur, sO);
           __syncthreads();
-          store_tile(gW, c0, sO);
+          store_panels(gW, c0, sO);
           __syncthreads();
         }
         for (int pn = 0; pn < Cfg::kPanels; ++pn) {
@@ -870,7 +859,7 @@ struct IntraKernel {
           __syncthreads();
           wy_product(sV, sO);
           __syncthreads();
-          store_u(gU, c0, sO);
+          store_panels(gU, c0, sO);
         }
       }
       if (!has_next) break;

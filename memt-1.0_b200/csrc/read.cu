@@ -1,6 +1,7 @@
 // Launchers for the snapshot readout kernels (read.cuh).
 #include "launch.h"
 #include "read.cuh"
+#include "read_tc.cuh"
 
 namespace memt {
 
@@ -38,7 +39,26 @@ static int launch_tile(const ReadParams& p, int64_t maxlen, cudaStream_t s) {
   return cuda_status(cudaGetLastError());
 }
 
+// d = 128, bf16 queries, plain read: tcgen05 kernel with TMA query tiles
+static int launch_read_tc(const ReadParams& p, int64_t maxlen, cudaStream_t s) {
+  ReadTcParams P;
+  P.p = p;
+  const uint64_t row = static_cast<uint64_t>(p.H) * ReadTcCfg::D;
+  cudaError_t e = make_tmap_bf16_2d(&P.q_map, p.q, row, static_cast<uint64_t>(p.L), row * 2, 64, ReadTcCfg::kTok);
+  if (e == cudaSuccess) e = ensure_smem(read_tc_kernel, ReadTcCfg::kSmem);
+  if (e != cudaSuccess) return cuda_status(e);
+  const int64_t per = int64_t(kReadTcTiles) * ReadTcCfg::kTok;
+  int64_t groups = (maxlen + per - 1) / per;
+  if (groups < 1) groups = 1;
+  if (groups > 65535) return MEMT_ERR_UNSUPPORTED;
+  dim3 grid(static_cast<unsigned>(p.num_blocks) * p.H, static_cast<unsigned>(groups));
+  ProfScope prof(kProfReadTile, s);
+  read_tc_kernel<<<grid, ReadTcCfg::kThreads, ReadTcCfg::kSmem, s>>>(P);
+  return cuda_status(cudaGetLastError());
+}
+
 int launch_read(const ReadParams& p, int D, bool exact, int64_t maxlen, cudaStream_t s) {
+  if (D == 128 && !exact && !p.fused && maxlen > kGemvMaxBlock) return launch_read_tc(p, maxlen, s);
   if (exact || maxlen <= kGemvMaxBlock) {
     switch (D) {
       case 64: return exact ? launch_gemv<64, true>(p, maxlen, s) : launch_gemv<64, false>(p, maxlen, s);

@@ -1,0 +1,174 @@
+// Snapshot read o = scale * q . bf16(S) on tcgen05 tensor cores for d = 128 and blocks of
+// many tokens (the commit read of token_memory_packed, models/qwen/ops/read.py:42-89 and
+// models/deepseek/ops/read.py:6-31): one CTA per (block, head, run of up to kReadTcTiles
+// 128-token tiles).
+//
+//   * the block's fp32 snapshot is read once, rounded to bf16 (read.py:64) and written as the
+//     MN-major B operand [128 key rows][2 x 64 values] in shared memory;
+//   * 128-token query tiles arrive by TMA (2-D tensor map over the [L, H*D] query rows, two
+//     64-key boxes with the 128-byte swizzle = the K-major A operand), double-buffered;
+//   * a control warp issues the 128x128x128 MMA of each tile into one of two tensor-memory
+//     accumulators and refills the query stage once the MMA has consumed it;
+//   * eight worker warps drain the other accumulator: warp w reads tokens 32 (w % 4).. and
+//     columns 64 (w / 4).., scales, rounds and stores 128 contiguous bytes per token.
+// Rows past the block end (the tile straddles into the next block or past L) are computed
+// from whatever the TMA brought (zeros past L) and not stored. Every wait is bounded.
+#pragma once
+
+#include "common.cuh"
+#include "read.cuh"
+#include "tc.cuh"
+#include "tma.h"
+
+namespace memt {
+
+constexpr int kReadTcTiles = 8;  // 128-token tiles per CTA
+
+struct ReadTcParams {
+  CUtensorMap q_map;  // bf16 [L, H*D], boxes of 64 x 128
+  ReadParams p;
+};
+
+struct ReadTcCfg {
+  static constexpr int D = 128, kTok = 128;
+  static constexpr int kWorkers = 256;
+  static constexpr int kThreads = kWorkers + 32;
+  static constexpr uint32_t kBytesS = D * D * 2;          // 32 KB
+  static constexpr uint32_t kBytesQ = kTok * D * 2;       // 32 KB per stage
+  static constexpr uint32_t kOffQ = kBytesS;
+  static constexpr uint32_t kOffBar = kOffQ + 2 * kBytesQ;
+  static constexpr size_t kSmem = kOffBar + 128 + 1024;
+  static constexpr uint32_t kTmemCols = 256;
+};
+
+__global__ void __launch_bounds__(ReadTcCfg::kThreads, 1) read_tc_kernel(const __grid_constant__ ReadTcParams P) {
+  using Cfg = ReadTcCfg;
+  constexpr int D = Cfg::D;
+  const ReadParams& p = P.p;
+  extern __shared__ __align__(1024) unsigned char smem_read_tc[];
+  unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_read_tc) + 1023) &
+                                                       ~static_cast<uintptr_t>(1023));
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int n = blockIdx.x / p.H, h = blockIdx.x % p.H;
+  int64_t bos, eos;
+  block_range(p, n, bos, eos);
+  const int64_t first = bos + (int64_t)blockIdx.y * kReadTcTiles * Cfg::kTok;
+  if (first >= eos) return;
+  int ntiles = (int)((eos - first + Cfg::kTok - 1) / Cfg::kTok);
+  if (ntiles > kReadTcTiles) ntiles = kReadTcTiles;
+
+  // barriers: 0/1 query stage full (TMA), 2/3 accumulator full (commit),
+  // 4/5 accumulator drained (workers), 6 snapshot operand written (workers)
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + Cfg::kOffBar);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + Cfg::kOffBar + 64);
+  auto B = [&](int i) { return smem_u32(&bar[i]); };
+  unsigned char* sS = sm;
+  const uint32_t sQ = smem_u32(sm + Cfg::kOffQ);
+
+  if (tid == 0) {
+    for (int i = 0; i < 4; ++i) mbar_init(B(i), 1);
+    for (int i = 4; i < 7; ++i) mbar_init(B(i), Cfg::kWorkers);
+    mbar_fence_init();
+  }
+  if (warp == 8) tc::alloc(smem_u32(tmem_slot), Cfg::kTmemCols);
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  bool alive = true;
+  auto wait = [&](int b, uint32_t parity) {
+    if (alive && !mbar_wait(B(b), parity)) alive = false;
+  };
+
+  if (warp == 8) {
+    if (lane == 0) {
+      auto load_q = [&](int i) {
+        const int s = i & 1;
+        const int y = static_cast<int>(first + (int64_t)i * Cfg::kTok);
+        mbar_expect_tx(B(s), Cfg::kBytesQ);
+        tma_load_2d(sQ + s * Cfg::kBytesQ, &P.q_map, h * D, y, B(s));
+        tma_load_2d(sQ + s * Cfg::kBytesQ + Cfg::kBytesQ / 2, &P.q_map, h * D + 64, y, B(s));
+      };
+      load_q(0);
+      if (ntiles > 1) load_q(1);
+      wait(6, 0);
+      constexpr uint32_t kId = tc::idesc(tc::kBF16, 128, 128, false, true);  // q K-major, S MN-major
+      const uint32_t ss = smem_u32(sS);
+      for (int i = 0; i < ntiles; ++i) {
+        const int s = i & 1;
+        wait(s, (i >> 1) & 1);
+        if (i >= 2) wait(4 + s, ((i >> 1) - 1) & 1);
+        tc::fence_after();
+        const uint32_t q = sQ + s * Cfg::kBytesQ;
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks)
+          tc::mma_bf16(tmem + 128 * s, tc::desc_kmajor(q + (ks >> 2) * (Cfg::kBytesQ / 2), (ks & 3) * 32),
+                       tc::desc_mnmajor(ss, Cfg::kBytesS / 2, ks), kId, ks > 0);
+        tc::commit(B(2 + s));
+        if (i + 2 < ntiles) {  // the stage is free once this MMA has read it
+          wait(2 + s, (i >> 1) & 1);
+          load_q(i + 2);
+        }
+      }
+    }
+  } else {
+    // snapshot -> bf16 MN-major operand: thread t converts row t / 2, values 64 (t % 2) ..
+    {
+      const int row = tid >> 1, pan = tid & 1;
+      const float4* src = reinterpret_cast<const float4*>(p.states + ((int64_t)n * p.H + h) * D * D +
+                                                          (int64_t)row * D + 64 * pan);
+      unsigned char* dst = sS + pan * (Cfg::kBytesS / 2) + (row >> 3) * 1024 + (row & 7) * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const float4 a = __ldg(src + 2 * c), b = __ldg(src + 2 * c + 1);
+        uint4 pk;
+        pk.x = pack_bf16x2(a.x, a.y);
+        pk.y = pack_bf16x2(a.z, a.w);
+        pk.z = pack_bf16x2(b.x, b.y);
+        pk.w = pack_bf16x2(b.z, b.w);
+        *reinterpret_cast<uint4*>(dst + ((c ^ (row & 7)) << 4)) = pk;
+      }
+      tc::fence_smem_async();
+      mbar_arrive(B(6));
+    }
+    const int quarter = warp & 3, half = warp >> 2;
+    const int64_t qrow = (int64_t)p.H * D;
+    for (int i = 0; i < ntiles; ++i) {
+      const int s = i & 1;
+      wait(2 + s, (i >> 1) & 1);
+      __syncwarp();
+      tc::fence_after();
+      float o[2][32];
+      tc::ld32(tc::lane_addr(tmem + 128 * s, 32 * quarter, 64 * half), o[0]);
+      tc::ld32(tc::lane_addr(tmem + 128 * s, 32 * quarter, 64 * half + 32), o[1]);
+      tc::fence_before();
+      mbar_arrive(B(4 + s));  // the accumulator may be overwritten
+      const int64_t tok = first + (int64_t)i * Cfg::kTok + 32 * quarter + lane;
+      if (tok < eos) {
+        const int64_t off = tok * qrow + (int64_t)h * D + 64 * half;
+        if (p.out_bf16) {
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + off);
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const float* v = &o[c >> 2][(c & 3) * 8];
+            dst[c] = make_uint4(pack_bf16x2(v[0] * p.scale, v[1] * p.scale), pack_bf16x2(v[2] * p.scale, v[3] * p.scale),
+                                pack_bf16x2(v[4] * p.scale, v[5] * p.scale), pack_bf16x2(v[6] * p.scale, v[7] * p.scale));
+          }
+        } else {
+          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + off);
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            const float* v = &o[c >> 3][(c & 7) * 4];
+            dst[c] = make_float4(v[0] * p.scale, v[1] * p.scale, v[2] * p.scale, v[3] * p.scale);
+          }
+        }
+      }
+    }
+  }
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 8) tc::dealloc(tmem, Cfg::kTmemCols);
+}
+
+}  // namespace memt

@@ -1,6 +1,7 @@
 // Launcher for the inter-chunk state scan (scan.cuh).
 #include "launch.h"
 #include "scan.cuh"
+#include "scan_tc.cuh"
 
 namespace memt {
 
@@ -15,10 +16,20 @@ static int launch_scan_t(const ScanParams& p, cudaStream_t s) {
   return cuda_status(cudaGetLastError());
 }
 
+// d = 128: tcgen05 kernel, one CTA per (sample, head)
+static int launch_scan_tc(const ScanParams& p, cudaStream_t s) {
+  cudaError_t e = ensure_smem(scan_tc_kernel, ScanTcCfg::kSmem);
+  if (e != cudaSuccess) return cuda_status(e);
+  const unsigned grid = static_cast<unsigned>(p.N) * p.H;
+  ProfScope prof(kProfScan, s);
+  scan_tc_kernel<<<grid, ScanTcCfg::kThreads, ScanTcCfg::kSmem, s>>>(p);
+  return cuda_status(cudaGetLastError());
+}
+
 int launch_scan(int D, const ScanParams& p, cudaStream_t s) {
   switch (D) {
     case 64: return launch_scan_t<64>(p, s);
-    case 128: return launch_scan_t<128>(p, s);
+    case 128: return launch_scan_tc(p, s);
     case 256: return launch_scan_t<256>(p, s);
     default: return MEMT_ERR_UNSUPPORTED;
   }

@@ -7,8 +7,8 @@
 // The fp32 state panel [D x 64] stays in registers for the whole sample (C fragments of the
 // second product, one 16-row m-tile per warp). The next chunk's w, kg, u panel and 2^G_last
 // arrive with four bulk (TMA) copies issued by one thread into the other stage while the
-// current chunk computes; the intra kernel stored them in exactly the swizzled shared-memory
-// layout used here. Rows of padded tokens are zero in w, u and kg, so no masking is needed.
+// current chunk computes; the intra kernel stored them in exactly the shared-memory layout
+// used here (64-column panels, each swz<64>). Rows of padded tokens are zero in w, u and kg, so no masking is needed.
 #pragma once
 
 #include "common.cuh"
@@ -116,7 +116,7 @@ __global__ void __launch_bounds__(ScanCfg<D>::kThreads) scan_kernel(ScanParams p
 #pragma unroll
       for (int ks = 0; ks < D / 16; ++ks) {
         uint32_t a[4];
-        ldsm_x4(a, smem_u32(w + swz<D>(16 * xrb + (lane & 15), 16 * ks + 8 * (lane >> 4))));
+        ldsm_x4(a, smem_u32(w + pswz(16 * xrb + (lane & 15), 16 * ks + 8 * (lane >> 4))));
 #pragma unroll
         for (int np = 0; np < Cfg::kXNT; np += 2) {
           uint32_t b[4];
@@ -157,7 +157,7 @@ __global__ void __launch_bounds__(ScanCfg<D>::kThreads) scan_kernel(ScanParams p
         const int tok = 16 * ks + (lane & 7) + 8 * (lane >> 4);
         const int chn = warp * 16 + 8 * ((lane >> 3) & 1);
         uint32_t a[4];
-        ldsm_x4_t(a, smem_u32(kg + swz<D>(tok, chn)));
+        ldsm_x4_t(a, smem_u32(kg + pswz(tok, chn)));
 #pragma unroll
         for (int np = 0; np < Cfg::kNT; np += 2) {
           uint32_t b[4];

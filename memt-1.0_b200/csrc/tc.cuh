@@ -1,0 +1,108 @@
+// Fifth-generation tensor cores (tcgen05) for sm_100a: tensor-memory allocation, shared-memory
+// operand descriptors, single-thread MMA issue with mbarrier completion, and tensor-memory
+// loads. Only the forms used by this library: cta_group::1, M = 128, bf16 (kind::f16) and
+// tf32 (kind::tf32) operands with fp32 accumulation, 128-byte swizzled operand tiles.
+//
+// Operand tiles (see pswz in common.cuh): rows of 128 bytes, 8-row groups of 1024 bytes
+// (SBO), 16-byte chunks XOR-permuted by (row & 7); tile bases 1024-byte aligned.
+//   K-major: rows are the M (or N) index, the 128 bytes hold 64 bf16 / 32 fp32 of K; a K
+//            step of 16 bf16 (8 tf32) advances the start address by 32 bytes inside a row,
+//            further 128-byte K blocks are separate row tiles.
+//   MN-major: rows are the K index, the 128 bytes hold 64 bf16 of M (N); LBO is the byte
+//            distance between 64-wide M (N) panels; a K step of 16 advances by 2 x SBO.
+// The tf32 kind truncates fp32 operands to tf32; callers that need round-to-nearest store
+// operands already rounded.
+// Accumulator (M = 128): row i of D is tensor-memory lane i, column j is column j (fp32).
+// Warp w of a CTA reads lanes 32 (w % 4) .. 32 (w % 4) + 31.
+#pragma once
+
+#include <cstdint>
+
+namespace memt {
+namespace tc {
+
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;  // descriptor version for sm_100
+  d |= static_cast<uint64_t>(2) << 61;  // 128-byte swizzle
+  return d;
+}
+
+// K-major operand tile, K step 16 bf16 / 8 tf32 at byte offset koff (< 128) inside the rows
+__device__ __forceinline__ uint64_t desc_kmajor(uint32_t tile, uint32_t koff) {
+  return desc_sw128(tile + koff, 16, 1024);
+}
+// MN-major operand tile whose 64-wide panels lie panel_bytes apart; K step ks (16 rows)
+__device__ __forceinline__ uint64_t desc_mnmajor(uint32_t tile, uint32_t panel_bytes, int ks) {
+  return desc_sw128(tile + static_cast<uint32_t>(ks) * 2048u, panel_bytes, 1024);
+}
+
+enum : int { kF16 = 0, kBF16 = 1, kTF32 = 2 };
+// instruction descriptor: fp32 accumulator, dense, no negation
+__host__ __device__ constexpr uint32_t idesc(int fmt, int M, int N, bool a_mn, bool b_mn) {
+  return (1u << 4) | (static_cast<uint32_t>(fmt) << 7) | (static_cast<uint32_t>(fmt) << 10) |
+         (static_cast<uint32_t>(a_mn) << 15) | (static_cast<uint32_t>(b_mn) << 16) |
+         (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// D[tmem] (+)= A . B, issued by one thread
+__device__ __forceinline__ void mma_bf16(uint32_t d, uint64_t a, uint64_t b, uint32_t id, bool acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(id), "r"(static_cast<uint32_t>(acc)));
+}
+__device__ __forceinline__ void mma_tf32(uint32_t d, uint64_t a, uint64_t b, uint32_t id, bool acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(id), "r"(static_cast<uint32_t>(acc)));
+}
+// arrive on the mbarrier once all previously issued MMAs of this thread have completed
+__device__ __forceinline__ void commit(uint32_t mbar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(mbar)
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// make generic-proxy shared-memory writes visible to the tensor cores (async proxy)
+__device__ __forceinline__ void fence_smem_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// warp-wide; the allocated base address is written to *slot (shared memory)
+__device__ __forceinline__ void alloc(uint32_t slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot), "r"(ncols));
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+}
+__device__ __forceinline__ void dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols));
+}
+
+// 32 lanes x 32 consecutive fp32 columns: thread t of the warp gets lane (base lane + t).
+// The load and its wait are one asm statement, so no use of the registers can be scheduled
+// before the data has arrived.
+__device__ __forceinline__ void ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ uint32_t lane_addr(uint32_t base, int lane0, int col) {
+  return base + (static_cast<uint32_t>(lane0) << 16) + static_cast<uint32_t>(col);
+}
+
+}  // namespace tc
+}  // namespace memt
