@@ -4,20 +4,17 @@
 // every chunk of the sample in order:
 //     v_new = u - w . bf16(S)                         (state.py:95-98)
 //     S     = diag(2^G_last) S + kg^T . bf16(v_new)   (state.py:101-112)
-// Value columns never mix, so the 128 state columns form two independent half-chains a and b
-// (columns 0-63 and 64-127) that share the chunk's w and kg tiles. They run in ping-pong so
-// that one half-chain's tensor-core latency hides behind the other's elementwise work:
-//     update S_a -> [X_a = w . bf16(S_a)] ; update S_b -> [X_b]
-//     v_new_a    -> [P_a = kg^T . v_new_a] ; v_new_b -> [P_b]
-// where [..] is an MMA issued by a dedicated control warp (tcgen05, shared-memory operands,
-// tensor-memory accumulators) and the rest runs on eight worker warps:
-//   * the fp32 state lives in registers for the whole sample: worker (warp w, lane l) owns key
-//     row 32 (w % 4) + l, columns 32 (w / 4) .. + 31 of each half-chain;
-//   * X_h (M = 64 tokens, N = 64) and P_h (M = 128 keys, N = 64) come back through tensor
-//     memory; workers write bf16(S_h) and bf16(v_new_h) straight into the swizzled operand
-//     tiles of the next MMA and hand them over with mbarrier arrivals;
-//   * w, kg, u of chunk c + 2 and 2^G_last arrive by bulk copies into a three-deep ring (the
-//     intra kernel stores them in the operand layout, pswz).
+// The chunks of a sample form a dependent chain, so the kernel minimises the latency of one
+// chunk step. A tcgen05 MMA costs about the same per K = 16 slice for any N up to 128, so both
+// products use the full M = 128 shape (12 MMAs per chunk):
+//     X^T = bf16(S)^T . w^T   M = 128 values, N = 64 tokens, K = 128 keys  (tensor memory 128..191)
+//     P   = kg^T . v_new      M = 128 keys,   N = 128 values, K = 64 tokens (tensor memory 0..127)
+// A control warp issues the MMAs and the bulk copies; eight worker warps hold the fp32 state
+// in registers (thread = key row 32 (w % 4) + lane, values 64 (w / 4) .. + 63), fold P into it
+// (S = 2^G_last S + P), and write bf16(S) and bf16(u - X) straight into the swizzled operand
+// tiles of the next MMA, handing them over with one mbarrier arrival per warp.
+// w, kg, u of chunk c + 2 and 2^G_last stream into a three-deep ring by bulk copies (the intra
+// kernel stores them in the operand layout, pswz).
 // Every wait is bounded: a thread whose wait runs out flags the workspace header and stops
 // waiting; the CTA then frees its tensor memory and leaves the final state untouched.
 #pragma once
@@ -29,17 +26,17 @@ namespace memt {
 
 struct ScanTcCfg {
   static constexpr int D = 128;
-  static constexpr int kWorkers = 256;
-  static constexpr int kThreads = kWorkers + 32;  // + control warp
+  static constexpr int kWorkerWarps = 8;
+  static constexpr int kThreads = (kWorkerWarps + 1) * 32;  // + control warp
   static constexpr int kStages = 3;
   static constexpr uint32_t kBytesTile = uint32_t(kTile) * D * 2;  // 16 KB: w, kg or u of one chunk
   static constexpr uint32_t kBytesEl = D * 4;
   static constexpr uint32_t kStageStride = 3 * kBytesTile + 1024;  // tiles + 2^G_last, 1 KB aligned
-  static constexpr uint32_t kOffSb = kStages * kStageStride;       // bf16(S) operands: 2 x [128][64]
-  static constexpr uint32_t kOffVn = kOffSb + 2 * kBytesTile;       // bf16(v_new) operands: 2 x [64][64]
+  static constexpr uint32_t kOffSb = kStages * kStageStride;       // bf16(S)^T operand, 32 KB
+  static constexpr uint32_t kOffVn = kOffSb + 2 * kBytesTile;       // bf16(v_new) operand, 16 KB
   static constexpr uint32_t kOffBar = kOffVn + kBytesTile;
   static constexpr size_t kSmem = kOffBar + 256 + 1024;  // + alignment slack for the 1 KB base
-  static constexpr uint32_t kTmemCols = 256;             // P_a, P_b, X_a, X_b: 64 columns each
+  static constexpr uint32_t kTmemCols = 256;
 };
 
 __global__ void __launch_bounds__(ScanTcCfg::kThreads, 1) scan_tc_kernel(ScanParams p) {
@@ -51,8 +48,8 @@ __global__ void __launch_bounds__(ScanTcCfg::kThreads, 1) scan_tc_kernel(ScanPar
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int h = blockIdx.x % p.H, n = blockIdx.x / p.H;
 
-  // barriers: 0-2 stage ring; 3/4 X_a/X_b and 5/6 P_a/P_b (tcgen05.commit);
-  // 7/8 bf16(S_a)/(S_b) and 9/10 v_new_a/v_new_b written (one arrival per worker)
+  // barriers: 0-2 stage ring; 3 X^T ready, 4 P ready (tcgen05.commit);
+  // 5 bf16(S)^T written, 6 v_new written (one arrival per worker warp)
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + Cfg::kOffBar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + Cfg::kOffBar + 128);
   auto B = [&](int i) { return smem_u32(&bar[i]); };
@@ -61,24 +58,24 @@ __global__ void __launch_bounds__(ScanTcCfg::kThreads, 1) scan_tc_kernel(ScanPar
   auto st_kg = [&](int st) { return s_base + st * Cfg::kStageStride + Cfg::kBytesTile; };
   auto st_u = [&](int st) { return sm + st * Cfg::kStageStride + 2 * Cfg::kBytesTile; };
   auto st_el = [&](int st) { return reinterpret_cast<const float*>(sm + st * Cfg::kStageStride + 3 * Cfg::kBytesTile); };
-  unsigned char* sSb = sm + Cfg::kOffSb;  // half-chain hc at + hc * 16 KB: [128 key rows][64 values]
-  unsigned char* sVn = sm + Cfg::kOffVn;  // half-chain hc at + hc * 8 KB:  [64 token rows][64 values]
+  unsigned char* sSb = sm + Cfg::kOffSb;  // Sb^T: 2 value panels of [128 key rows][64 values]
+  unsigned char* sVn = sm + Cfg::kOffVn;  // v_new: [128 value rows][64 tokens]
 
   const int c0 = p.sample_off[n], c1 = p.sample_off[n + 1];
   const int nchunks = c1 - c0;
 
   if (tid == 0) {
-    for (int i = 0; i < 7; ++i) mbar_init(B(i), 1);
-    for (int i = 7; i < 11; ++i) mbar_init(B(i), Cfg::kWorkers);
+    for (int i = 0; i < 5; ++i) mbar_init(B(i), 1);
+    mbar_init(B(5), Cfg::kWorkerWarps);
+    mbar_init(B(6), Cfg::kWorkerWarps);
     mbar_fence_init();
   }
-  if (warp == 8) tc::alloc(smem_u32(tmem_slot), Cfg::kTmemCols);
+  if (warp == Cfg::kWorkerWarps) tc::alloc(smem_u32(tmem_slot), Cfg::kTmemCols);
   tc::fence_before();
   __syncthreads();
   tc::fence_after();
   const uint32_t tmem = *tmem_slot;
-  auto tP = [&](int hc) { return tmem + 64 * hc; };
-  auto tX = [&](int hc) { return tmem + 128 + 64 * hc; };
+  const uint32_t tP = tmem, tX = tmem + 128;
 
   bool alive = true;
   auto wait = [&](int b, uint32_t parity) {
@@ -88,157 +85,149 @@ __global__ void __launch_bounds__(ScanTcCfg::kThreads, 1) scan_tc_kernel(ScanPar
     }
   };
 
-  // worker geometry (unused by the control warp)
   const int quarter = warp & 3, half = (warp >> 2) & 1;
-  const int key = 32 * quarter + lane;  // state row
-  const int tok = 16 * quarter + lane;  // token row of X / v_new (lanes 0-15)
-  const int64_t state_off = ((int64_t)n * p.H + h) * D * D + (int64_t)key * D + 32 * half;
-  float S[2][32];
+  const int key = 32 * quarter + lane;  // state row; also the value row of X^T and v_new
+  const int64_t state_off = ((int64_t)n * p.H + h) * D * D + (int64_t)key * D + 64 * half;
+  float S[64];
 
-  if (warp == 8) {
-    // ---------------- control warp: bulk copies and MMA issue (lane 0) ----------------
-    if (lane == 0) {
-      auto prefetch = [&](int c, int st) {
-        const int64_t ch = (int64_t)c * p.H + h;
-        const uint32_t mb = B(st);
-        mbar_expect_tx(mb, 3 * Cfg::kBytesTile + Cfg::kBytesEl);
-        bulk_g2s(st_w(st), p.W + ch * kTile * D, Cfg::kBytesTile, mb);
-        bulk_g2s(st_kg(st), p.KG + ch * kTile * D, Cfg::kBytesTile, mb);
-        bulk_g2s(smem_u32(st_u(st)), p.U + ch * kTile * D, Cfg::kBytesTile, mb);
-        bulk_g2s(smem_u32(st_el(st)), p.Elast + ch * D, Cfg::kBytesEl, mb);
-      };
+  if (warp == Cfg::kWorkerWarps) {
+    // ---------------- control warp (converged; one elected lane issues) ----------------
+    auto prefetch = [&](int c, int st) {
+      const int64_t ch = (int64_t)c * p.H + h;
+      const uint32_t mb = B(st);
+      mbar_expect_tx(mb, 3 * Cfg::kBytesTile + Cfg::kBytesEl);
+      bulk_g2s(st_w(st), p.W + ch * kTile * D, Cfg::kBytesTile, mb);
+      bulk_g2s(st_kg(st), p.KG + ch * kTile * D, Cfg::kBytesTile, mb);
+      bulk_g2s(smem_u32(st_u(st)), p.U + ch * kTile * D, Cfg::kBytesTile, mb);
+      bulk_g2s(smem_u32(st_el(st)), p.Elast + ch * D, Cfg::kBytesEl, mb);
+    };
+    if (tc::elect_one())
       for (int i = 0; i < Cfg::kStages - 1 && i < nchunks; ++i) prefetch(c0 + i, i);
-      constexpr uint32_t kIdX = tc::idesc(tc::kBF16, 64, 64, false, true);  // w K-major, S MN-major
-      constexpr uint32_t kIdP = tc::idesc(tc::kBF16, 128, 64, true, true);  // kg^T MN-major, v_new MN-major
-      const uint32_t sb = smem_u32(sSb), vn = smem_u32(sVn);
-      for (int it = 0; it < nchunks; ++it) {
-        const int st = it % Cfg::kStages;
-        const uint32_t ph = it & 1;
-        wait(st, (it / Cfg::kStages) & 1);
-        const uint32_t w = st_w(st), kg = st_kg(st);
-        for (int hc = 0; hc < 2; ++hc) {  // X_h = w . bf16(S_h)
-          wait(7 + hc, ph);
-          tc::fence_after();
+    __syncwarp();
+    constexpr uint32_t kIdX = tc::idesc(tc::kBF16, 128, 64, true, false);   // Sb^T MN-major, w K-major
+    constexpr uint32_t kIdP = tc::idesc(tc::kBF16, 128, 128, true, false);  // kg^T MN-major, v_new K-major
+    const uint32_t sb = smem_u32(sSb), vn = smem_u32(sVn);
+    for (int it = 0; it < nchunks; ++it) {
+      const int st = it % Cfg::kStages;
+      const uint32_t ph = it & 1;
+      const uint32_t w = st_w(st), kg = st_kg(st);
+      wait(st, (it / Cfg::kStages) & 1);
+      wait(5, ph);
+      tc::fence_after();
+      if (tc::elect_one()) {
 #pragma unroll
-          for (int ks = 0; ks < D / 16; ++ks)
-            tc::mma_bf16(tX(hc), tc::desc_kmajor(w + (ks >> 2) * (kTile * 128), (ks & 3) * 32),
-                         tc::desc_mnmajor(sb + hc * Cfg::kBytesTile, Cfg::kBytesTile, ks), kIdX, ks > 0);
-          tc::commit(B(3 + hc));
-        }
-        // every reader of the stage that chunk it - 1 used has arrived on barrier 8 above
+        for (int ks = 0; ks < D / 16; ++ks)
+          tc::mma_bf16(tX, tc::desc_mnmajor(sb, Cfg::kBytesTile, ks),
+                       tc::desc_kmajor(w + (ks >> 2) * (kTile * 128), (ks & 3) * 32), kIdX, ks > 0);
+        tc::commit(B(3));
+        // every reader of the stage that chunk it - 1 used has arrived on barrier 5 above
         if (it + Cfg::kStages - 1 < nchunks)
           prefetch(c0 + it + Cfg::kStages - 1, (it + Cfg::kStages - 1) % Cfg::kStages);
-        for (int hc = 0; hc < 2; ++hc) {  // P_h = kg^T . v_new_h
-          wait(9 + hc, ph);
-          tc::fence_after();
-#pragma unroll
-          for (int ks = 0; ks < kTile / 16; ++ks)
-            tc::mma_bf16(tP(hc), tc::desc_mnmajor(kg, kTile * 128, ks),
-                         tc::desc_mnmajor(vn + hc * (Cfg::kBytesTile / 2), Cfg::kBytesTile / 2, ks), kIdP,
-                         ks > 0);
-          tc::commit(B(5 + hc));
-        }
       }
+      __syncwarp();
+      wait(6, ph);
+      tc::fence_after();
+      if (tc::elect_one()) {
+#pragma unroll
+        for (int ks = 0; ks < kTile / 16; ++ks)
+          tc::mma_bf16(tP, tc::desc_mnmajor(kg, kTile * 128, ks), tc::desc_kmajor(vn, ks * 32), kIdP, ks > 0);
+        tc::commit(B(4));
+      }
+      __syncwarp();
     }
   } else {
-    // ---------------- workers ----------------
+    // ---------------- worker warps ----------------
 #pragma unroll
-    for (int hc = 0; hc < 2; ++hc)
-#pragma unroll
-      for (int j = 0; j < 32; j += 4) {
-        const float4 v = *reinterpret_cast<const float4*>(p.h0 + state_off + 64 * hc + j);
-        S[hc][j] = v.x;
-        S[hc][j + 1] = v.y;
-        S[hc][j + 2] = v.z;
-        S[hc][j + 3] = v.w;
-      }
+    for (int j = 0; j < 64; j += 4) {
+      const float4 v = *reinterpret_cast<const float4*>(p.h0 + state_off + j);
+      S[j] = v.x;
+      S[j + 1] = v.y;
+      S[j + 2] = v.z;
+      S[j + 3] = v.w;
+    }
     float el = 1.f;  // 2^G_last of the previous chunk for this key row
-    auto update_state = [&](int hc) {  // S_h = 2^G_last S_h + P_h
-      __syncwarp();
+    auto update_state = [&]() {  // S = 2^G_last S + P
       tc::fence_after();
-      float P[32];
-      tc::ld32(tc::lane_addr(tP(hc), 32 * quarter, 32 * half), P);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) S[hc][j] = fmaf(el, S[hc][j], P[j]);
+      for (int j0 = 0; j0 < 64; j0 += 32) {
+        float P[32];
+        tc::ld32(tc::lane_addr(tP, 32 * quarter, 64 * half + j0), P);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) S[j0 + j] = fmaf(el, S[j0 + j], P[j]);
+      }
+    };
+    auto hand_over = [&](int b) {  // operand tile written: make it visible to the tensor cores
+      tc::fence_smem_async();
+      tc::fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(B(b));
     };
     for (int it = 0; it < nchunks; ++it) {
       const int st = it % Cfg::kStages;
       const uint32_t ph = it & 1;
-#pragma unroll
-      for (int hc = 0; hc < 2; ++hc) {
-        // ---- previous chunk's P_h into the state; bf16(S_h) -> MN-major [key][64] operand ----
-        if (it > 0) {
-          wait(5 + hc, ph ^ 1);
-          update_state(hc);
-        }
-        unsigned char* row = sSb + hc * Cfg::kBytesTile + (key >> 3) * 1024 + (key & 7) * 128;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint4 pk;
-          pk.x = pack_bf16x2(S[hc][8 * c], S[hc][8 * c + 1]);
-          pk.y = pack_bf16x2(S[hc][8 * c + 2], S[hc][8 * c + 3]);
-          pk.z = pack_bf16x2(S[hc][8 * c + 4], S[hc][8 * c + 5]);
-          pk.w = pack_bf16x2(S[hc][8 * c + 6], S[hc][8 * c + 7]);
-          *reinterpret_cast<uint4*>(row + (((4 * half + c) ^ (key & 7)) << 4)) = pk;
-        }
-        tc::fence_smem_async();
-        tc::fence_before();
-        mbar_arrive(B(7 + hc));
+      // ---- previous chunk's P into the state; bf16(S) -> Sb^T (MN-major, panel = value half) ----
+      if (it > 0) {
+        wait(4, ph ^ 1);
+        update_state();
       }
+      {
+        unsigned char* row = sSb + half * Cfg::kBytesTile + (key >> 3) * 1024 + (key & 7) * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint4 pk;
+          pk.x = pack_bf16x2(S[8 * c], S[8 * c + 1]);
+          pk.y = pack_bf16x2(S[8 * c + 2], S[8 * c + 3]);
+          pk.z = pack_bf16x2(S[8 * c + 4], S[8 * c + 5]);
+          pk.w = pack_bf16x2(S[8 * c + 6], S[8 * c + 7]);
+          *reinterpret_cast<uint4*>(row + ((c ^ (key & 7)) << 4)) = pk;
+        }
+      }
+      hand_over(5);
+      // ---- v_new = bf16(u - X) -> K-major operand [value row][64 tokens] ----
       wait(st, (it / Cfg::kStages) & 1);
       el = st_el(st)[key];
-#pragma unroll
-      for (int hc = 0; hc < 2; ++hc) {
-        // ---- v_new_h = bf16(u - X_h) -> MN-major [token][64] operand (lanes 0-15) ----
-        wait(3 + hc, ph);
-        __syncwarp();
-        tc::fence_after();
+      wait(3, ph);
+      tc::fence_after();
+      {
         float X[32];
-        tc::ld32(tc::lane_addr(tX(hc), 32 * quarter, 32 * half), X);
-        if (lane < 16) {
-          const unsigned char* urow = st_u(st) + hc * (kTile * 128) + tok * 128;
-          unsigned char* vrow = sVn + hc * (Cfg::kBytesTile / 2) + (tok >> 3) * 1024 + (tok & 7) * 128;
+        tc::ld32(tc::lane_addr(tX, 32 * quarter, 32 * half), X);  // value `key`, tokens 32 half ..
+        const unsigned char* u = st_u(st) + (key >> 6) * (kTile * 128);  // value panel of u
+        const int vc = (key & 63) >> 3, vb = (key & 7) * 2;
+        unsigned char* vrow = sVn + (key >> 3) * 1024 + (key & 7) * 128;
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const int pc = ((4 * half + c) ^ (tok & 7)) << 4;
-            const uint4 uv = *reinterpret_cast<const uint4*>(urow + pc);
-            const uint32_t* uw = reinterpret_cast<const uint32_t*>(&uv);
-            uint4 pk;
-            uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
+        for (int c = 0; c < 4; ++c) {
+          float vn[8];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 u2 = unpack_bf16x2(uw[e]);
-              pw[e] = pack_bf16x2(u2.x - X[8 * c + 2 * e], u2.y - X[8 * c + 2 * e + 1]);
-            }
-            *reinterpret_cast<uint4*>(vrow + pc) = pk;
+          for (int e = 0; e < 8; ++e) {
+            const int t = 32 * half + 8 * c + e;
+            const __nv_bfloat16 uv = *reinterpret_cast<const __nv_bfloat16*>(u + t * 128 + ((vc ^ (t & 7)) << 4) + vb);
+            vn[e] = __bfloat162float(uv) - X[8 * c + e];
           }
+          uint4 pk;
+          pk.x = pack_bf16x2(vn[0], vn[1]);
+          pk.y = pack_bf16x2(vn[2], vn[3]);
+          pk.z = pack_bf16x2(vn[4], vn[5]);
+          pk.w = pack_bf16x2(vn[6], vn[7]);
+          *reinterpret_cast<uint4*>(vrow + (((4 * half + c) ^ (key & 7)) << 4)) = pk;
         }
-        tc::fence_smem_async();
-        tc::fence_before();
-        mbar_arrive(B(9 + hc));
       }
+      hand_over(6);
     }
     if (nchunks > 0) {
-#pragma unroll
-      for (int hc = 0; hc < 2; ++hc) {
-        wait(5 + hc, (nchunks - 1) & 1);
-        update_state(hc);
-      }
+      wait(4, (nchunks - 1) & 1);
+      update_state();
     }
   }
   // a wait that ran out anywhere in the CTA: leave the final state untouched
   const bool ok = __syncthreads_and(alive) != 0;
-  if (ok && warp < 8) {
+  if (ok && warp < Cfg::kWorkerWarps) {
 #pragma unroll
-    for (int hc = 0; hc < 2; ++hc)
-#pragma unroll
-      for (int j = 0; j < 32; j += 4)
-        *reinterpret_cast<float4*>(p.ht + state_off + 64 * hc + j) =
-            make_float4(S[hc][j], S[hc][j + 1], S[hc][j + 2], S[hc][j + 3]);
+    for (int j = 0; j < 64; j += 4)
+      *reinterpret_cast<float4*>(p.ht + state_off + j) = make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
   }
   tc::fence_before();
   __syncthreads();
-  if (warp == 8) tc::dealloc(tmem, Cfg::kTmemCols);
+  if (warp == Cfg::kWorkerWarps) tc::dealloc(tmem, Cfg::kTmemCols);
 }
 
 }  // namespace memt

@@ -100,6 +100,15 @@ __device__ __forceinline__ void ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// one lane of a converged warp (the lowest active one)
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n .reg .pred P;\n elect.sync _|P, 0xffffffff;\n selp.b32 %0, 1, 0, P;\n}\n"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 __device__ __forceinline__ uint32_t lane_addr(uint32_t base, int lane0, int col) {
   return base + (static_cast<uint32_t>(lane0) << 16) + static_cast<uint32_t>(col);
 }
