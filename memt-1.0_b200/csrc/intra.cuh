@@ -198,6 +198,7 @@ struct IntraKernel {
   float* sPre;  // [2][128]: per-token scalars of the current / next unit (fetch_scalars)
   int pre;      // which half of sPre belongs to the current unit
   float* sSeg;
+  float* sFac;  // [2][kSmall]: factors of the current / next unit (per-head decay)
   float* sScr;  // 4 fp32 16x16 scratch blocks of the blocked solve
 
   int tid, lane, warp, len, tok0, h;
@@ -266,13 +267,20 @@ struct IntraKernel {
     }
   }
 
-  // ---- decay, per-head layout: one warp computes every factor the chunk needs ----
-  __device__ void head_factors(const IntraParams& p) {
-    if (warp != 0) return;
+  // ---- decay, per-head layout: one warp computes every factor a chunk needs ----
+  // From the unit's per-token log-decays gbuf[0, 64) (zero past ln) into the factor buffer
+  // fac (layout of use_factors). Executed by one whole warp.
+  __device__ void head_factors(const float* gbuf, float* fac, int ln) {
+    float* fG = fac;
+    float* fLf = fac + kTile;
+    float* fEh = fac + 2 * kTile;
+    float* fKgf = fac + 3 * kTile;
+    float* fRf = fac + 4 * kTile;
+    float* fSeg = fac + 9 * kTile;
     // G_t = (sum_{s<=t} g_s) / ln2 over the 64 tokens; lane owns tokens 2*lane, 2*lane+1
     const int t0 = 2 * lane, t1 = 2 * lane + 1;
-    const float g0 = sPre[pre * 2 * kTile + t0];  // zero beyond the chunk
-    const float g1 = sPre[pre * 2 * kTile + t1];
+    const float g0 = gbuf[t0];
+    const float g1 = gbuf[t1];
     float s = g0 + g1;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -280,24 +288,38 @@ struct IntraKernel {
       if (lane >= o) s += y;
     }
     const float excl = s - (g0 + g1);
-    sG[t0] = (excl + g0) * kRcpLn2;
-    sG[t1] = (excl + g0 + g1) * kRcpLn2;
-    __syncwarp();
-    const int last = len - 1;
-    const float Gl = sG[last];
+    const float G0 = (excl + g0) * kRcpLn2, G1 = (excl + g0 + g1) * kRcpLn2;
+    fG[t0] = G0;
+    fG[t1] = G1;
+    // G at the last token and at the sub-chunk starts 16r, by shuffles
+    const int last = ln - 1;
+    const float Gl = __shfl_sync(0xffffffffu, (last & 1) ? G1 : G0, last >> 1);
+    float Gn[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) Gn[r] = __shfl_sync(0xffffffffu, G0, 8 * r);
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
       const int i = 2 * lane + q;
-      const float Gi = sG[i];
-      const float Gn = sG[i & ~15];
-      sLf[i] = fast_exp2(Gi - Gn);                   // left factor 2^(G_i - G_n(i))
-      sEh[i] = fast_exp2(Gi);                        // 2^G_i
-      sKgf[i] = i < len ? fast_exp2(Gl - Gi) : 0.f;  // 2^(G_last - G_i)
+      const float Gi = q ? G1 : G0;
+      const float Gs = Gn[i >> 4];
+      fLf[i] = fast_exp2(Gi - Gs);                  // left factor 2^(G_i - G_n(i))
+      fEh[i] = fast_exp2(Gi);                       // 2^G_i
+      fKgf[i] = i < ln ? fast_exp2(Gl - Gi) : 0.f;  // 2^(G_last - G_i)
 #pragma unroll
-      for (int r = 1; r < 4; ++r)                    // right factors 2^(G_n(r) - G_j), j < 16r
-        sRf[r * kTile + i] = i < 16 * r ? fast_exp2(sG[16 * r] - Gi) : 0.f;
+      for (int r = 1; r < 4; ++r)                   // right factors 2^(G_n(r) - G_j), j < 16r
+        fRf[r * kTile + i] = i < 16 * r ? fast_exp2(Gn[r] - Gi) : 0.f;
     }
-    if (lane == 0) sSeg[0] = fast_exp2(Gl);          // 2^G_last
+    if (lane == 0) fSeg[0] = fast_exp2(Gl);         // 2^G_last
+  }
+  // point the factor arrays at buffer b of sFac
+  __device__ __forceinline__ void use_factors(int b) {
+    float* f = sFac + b * Cfg::kSmall;
+    sG = f;
+    sLf = f + kTile;
+    sEh = f + 2 * kTile;
+    sKgf = f + 3 * kTile;
+    sRf = f + 4 * kTile;  // [4][64], rows 1..3 used
+    sSeg = f + 9 * kTile;
   }
 
   // ---- decay, per-channel layout: cumulative sum and factor tables of one panel ----
@@ -527,34 +549,38 @@ struct IntraKernel {
   // upper slot (s, r)); every finished block is also written as bf16 into sAi (rows >= len zero).
   __device__ void solve() {
     constexpr int LD = Cfg::kLdA, LDI = Cfg::kLdAi;
-    {
-      const int r = warp;
+    if (warp < 2) {
+      // Diagonal blocks by forward substitution in fp32: warp w inverts blocks 2w (lanes 0-15)
+      // and 2w + 1 (lanes 16-31); lane c holds column c of X = (I + L)^-1 - I:
+      //   X[i][c] = -(L[i][c] + sum_{c < j < i} L[i][j] X[j][c])   (X[j][c] = 0 for j <= c)
+      // Row i of L is read by 128-bit broadcast loads, the sum split over four accumulators.
+      const int r = 2 * warp + (lane >> 4);
       const int c = lane & 15;
       float* blk = sA + (16 * r) * LD + 16 * r;
       float x[16];
+      x[0] = 0.f;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) x[j] = (c < j) ? -blk[j * LD + c] : 0.f;
+      for (int i = 1; i < 16; ++i) {
+        float l[16];
 #pragma unroll
-      for (int i = 2; i < 16; ++i) {
-        const float a = (c < i) ? -blk[i * LD + c] : 0.f;
-        float s0 = a, s1 = 0.f;
-#pragma unroll
-        for (int j = 0; j < 16; j += 2) {
-          const float aj0 = __shfl_sync(0xffffffffu, a, j);
-          const float aj1 = __shfl_sync(0xffffffffu, a, j + 1);
-          if (j < i) s0 = fmaf(aj0, x[j], s0);
-          if (j + 1 < i) s1 = fmaf(aj1, x[j + 1], s1);
+        for (int q = 0; q < (i + 3) / 4; ++q) {
+          const float4 v = *reinterpret_cast<const float4*>(blk + i * LD + 4 * q);
+          l[4 * q] = v.x;
+          l[4 * q + 1] = v.y;
+          l[4 * q + 2] = v.z;
+          l[4 * q + 3] = v.w;
         }
-        x[i] = s0 + s1;
+        float s[4] = {blk[i * LD + c], 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int j = 1; j < i; ++j) s[j & 3] = fmaf(l[j], x[j], s[j & 3]);
+        x[i] = (c < i) ? -((s[0] + s[1]) + (s[2] + s[3])) : 0.f;
       }
       __syncwarp();
-      if (lane < 16) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const float v = x[j] + (j == c ? 1.f : 0.f);
-          blk[j * LD + c] = v;
-          sAi[(16 * r + j) * LDI + 16 * r + c] = __float2bfloat16_rn((16 * r + j < len) ? v : 0.f);
-        }
+      for (int j = 0; j < 16; ++j) {
+        const float v = x[j] + (j == c ? 1.f : 0.f);
+        blk[j * LD + c] = v;
+        sAi[(16 * r + j) * LDI + 16 * r + c] = __float2bfloat16_rn((16 * r + j < len) ? v : 0.f);
       }
     }
     named_sync(1, 128);
@@ -763,6 +789,9 @@ struct IntraKernel {
       if constexpr (!HEAD) channel_tables();
     };
 
+    // per-head decay with overlap: the staging warps compute the next unit's factors
+    constexpr bool kNextFactors = kOverlap && HEAD;
+    bool first = true;
     set_unit(p, unit);
     load_key_panel(0);
     cp_async_commit();
@@ -780,8 +809,12 @@ struct IntraKernel {
       if constexpr (kOverlap) load_value_panel(0);
       cp_async_commit();
       if constexpr (HEAD) {
-        __syncthreads();  // the unit's scalars (fetched one unit ahead) are visible
-        head_factors(p);
+        use_factors(pre);
+        if (!kNextFactors || first) {
+          __syncthreads();  // the unit's scalars are visible
+          if (warp == 0) head_factors(sPre + pre * 2 * kTile, sFac + pre * Cfg::kSmall, len);
+        }
+        first = false;
       }
 
       float acc[3][4];
@@ -824,6 +857,12 @@ struct IntraKernel {
           stage_u(p, 128, 128);
           named_sync(2, 128);
           stage_w_kg(kcur, gKG, gEl, 0, 128, 128);
+          if constexpr (kNextFactors) {
+            if (has_next && warp == 7) {
+              const ChunkDesc d2 = p.table[static_cast<int>(next / p.H)];
+              head_factors(sPre + (pre ^ 1) * 2 * kTile, sFac + (pre ^ 1) * Cfg::kSmall, d2.len);
+            }
+          }
         }
         __syncthreads();
         wy_product(kcur, sW);  // w = A^-1 . w operand; the w-gate tile is free
@@ -895,17 +934,13 @@ __global__ void __launch_bounds__(256, 2) intra_kernel(IntraParams p) {
   k.sEi = reinterpret_cast<float*>(base + Cfg::offEi);
   k.sA = reinterpret_cast<float*>(base + Cfg::offA);
   k.sAi = reinterpret_cast<__nv_bfloat16*>(base + Cfg::offAi);
-  __shared__ float s_small[Cfg::kSmall];
+  __shared__ float s_fac[2 * Cfg::kSmall];
   __shared__ __align__(16) float s_scr[4 * 256];
   k.sScr = s_scr;
-  k.sG = s_small;
-  k.sLf = s_small + kTile;
-  k.sEh = s_small + 2 * kTile;
-  k.sKgf = s_small + 3 * kTile;
-  k.sRf = s_small + 4 * kTile;  // [4][64], rows 1..3 used
+  k.sFac = s_fac;
+  k.use_factors(0);
   __shared__ float s_pre[4 * kTile];
   k.sPre = s_pre;
-  k.sSeg = s_small + 9 * kTile;
   k.tid = threadIdx.x;
   k.lane = threadIdx.x & 31;
   k.warp = threadIdx.x >> 5;
