@@ -207,17 +207,19 @@ struct IntraKernel {
 
   // async copy of one [64][P] bf16 panel (rows >= len zero-filled) into a swizzled tile
   __device__ __forceinline__ void load_tile(__nv_bfloat16* dst, const __nv_bfloat16* src, int c0) {
-    load_tile_for(dst, src, c0, tok0, len, h, 0, NT);
+    load_tile_for<0, NT>(dst, src, c0, tok0, len, h);
   }
-  // the same for an explicit (token range, head) and the threads [t0, t0 + n)
+  // the same for an explicit (token range, head) and the threads [T0, T0 + NTH)
+  template <int T0, int NTH>
   __device__ __forceinline__ void load_tile_for(__nv_bfloat16* dst, const __nv_bfloat16* src, int c0, int tk0,
-                                                int ln, int hd, int t0, int n) {
+                                                int ln, int hd) {
     const __nv_bfloat16* base = src + (int64_t)tk0 * row_stride + (int64_t)hd * D + c0;
     constexpr int kChunks = kTile * P / 8;
-    const int len = ln;
-    for (int i = tid - t0; i < kChunks; i += n) {
+    static_assert(kChunks % NTH == 0, "chunks per thread");
+#pragma unroll
+    for (int i = tid - T0; i < kChunks; i += NTH) {
       const int row = i / (P / 8), col = (i % (P / 8)) * 8;
-      const bool valid = row < len;
+      const bool valid = row < ln;
       cp_async16_zfill(dst + swz<P>(row, col), valid ? base + (int64_t)row * row_stride + col : src, valid);
     }
   }
@@ -636,11 +638,14 @@ struct IntraKernel {
     }
   }
 
-  // u operand in place: sV = bf16(v * w)   (wy_fast.py:98-100); threads [t0, t0 + n)
-  __device__ void stage_u(const IntraParams& p, int t0, int n) {
+  // u operand in place: sV = bf16(v * w)   (wy_fast.py:98-100); threads [T0, T0 + NTH)
+  template <int T0, int NTH>
+  __device__ void stage_u(const IntraParams& p) {
     if (p.write == nullptr) return;
     constexpr int kChunks = kTile * P / 8;
-    for (int i = tid - t0; i < kChunks; i += n) {
+    static_assert(kChunks % NTH == 0, "chunks per thread");
+#pragma unroll
+    for (int i = tid - T0; i < kChunks; i += NTH) {
       const int row = i / (P / 8), col = (i % (P / 8)) * 8;
       uint4 vv = *reinterpret_cast<const uint4*>(sV + swz<P>(row, col));
       const uint4 ww = *reinterpret_cast<const uint4*>(sW + swz<P>(row, col));
@@ -653,11 +658,14 @@ struct IntraKernel {
   }
 
   // w operand bf16( bf16(k*b) * 2^G ) in place of k (wy_fast.py:110-116), kg = bf16(k 2^(G_last-G))
-  // to global (wy_fast.py:125-139) and 2^G_last; threads [t0, t0 + n)
-  __device__ void stage_w_kg(__nv_bfloat16* kt, __nv_bfloat16* gKG, float* gEl, int c0, int t0, int n) {
+  // to global (wy_fast.py:125-139) and 2^G_last; threads [T0, T0 + NTH)
+  template <int T0, int NTH>
+  __device__ void stage_w_kg(__nv_bfloat16* kt, __nv_bfloat16* gKG, float* gEl, int c0) {
     const int last = len - 1;
     constexpr int kChunks = kTile * P / 8;
-    for (int i = tid - t0; i < kChunks; i += n) {
+    static_assert(kChunks % NTH == 0, "chunks per thread");
+#pragma unroll
+    for (int i = tid - T0; i < kChunks; i += NTH) {
       const int row = i / (P / 8), col = (i % (P / 8)) * 8;
       uint4 kv = *reinterpret_cast<const uint4*>(kt + swz<P>(row, col));
       uint32_t* kw = reinterpret_cast<uint32_t*>(&kv);
@@ -689,7 +697,7 @@ struct IntraKernel {
       *reinterpret_cast<uint4*>(kt + swz<P>(row, col)) = kv;  // w operand replaces k in place
       *reinterpret_cast<uint4*>(gKG + pswz(row, c0 + col)) = kgv;
     }
-    const int j = tid - t0;
+    const int j = tid - T0;
     if (j >= 0 && j < P) {
       if constexpr (HEAD)
         gEl[c0 + j] = sSeg[0];
@@ -851,12 +859,12 @@ struct IntraKernel {
             const int c2 = static_cast<int>(next / p.H), h2 = static_cast<int>(next % p.H);
             const ChunkDesc d2 = p.table[c2];
             fetch_scalars(p, d2.tok0, d2.len, h2, sPre + (pre ^ 1) * 2 * kTile, 128);
-            if constexpr (kPrefetch) load_tile_for(kspare, p.k, 0, d2.tok0, d2.len, h2, 128, 128);
+            if constexpr (kPrefetch) load_tile_for<128, 128>(kspare, p.k, 0, d2.tok0, d2.len, h2);
           }
           if constexpr (kPrefetch) cp_async_commit();
-          stage_u(p, 128, 128);
+          stage_u<128, 128>(p);
           named_sync(2, 128);
-          stage_w_kg(kcur, gKG, gEl, 0, 128, 128);
+          stage_w_kg<128, 128>(kcur, gKG, gEl, 0);
           if constexpr (kNextFactors) {
             if (has_next && warp == 7) {
               const ChunkDesc d2 = p.table[static_cast<int>(next / p.H)];
@@ -881,7 +889,7 @@ struct IntraKernel {
           cp_async_commit();
           cp_async_wait<0>();
           prepare_key_panel(c0);
-          stage_w_kg(kcur, gKG, gEl, c0, 0, NT);
+          stage_w_kg<0, NT>(kcur, gKG, gEl, c0);
           __syncthreads();
           wy_product(kcur, sO);
           __syncthreads();
@@ -894,7 +902,7 @@ struct IntraKernel {
           cp_async_commit();
           cp_async_wait<0>();
           __syncthreads();
-          stage_u(p, 0, NT);
+          stage_u<0, NT>(p);
           __syncthreads();
           wy_product(sV, sO);
           __syncthreads();
