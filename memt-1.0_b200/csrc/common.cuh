@@ -115,7 +115,7 @@ __device__ __forceinline__ void cp_async_wait() {
 }
 
 // ---------------------------------------------------------------------------
-// mbarrier + bulk (TMA, untiled) copies global -> shared. No cluster multicast anywhere.
+// mbarrier + bulk (TMA, untiled) copies global -> shared, each into this CTA only.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(uint32_t mbar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(mbar), "r"(count));
@@ -129,7 +129,9 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t mbar, uint32_t bytes) {
 __device__ __forceinline__ void mbar_arrive(uint32_t mbar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(mbar) : "memory");
 }
-// Bounded wait for the phase with the given parity; false after ~2^24 polls (seconds).
+// Bounded wait for the phase with the given parity; false after 2^24 polls (about a second).
+// Plain polling: a thread suspended by a try_wait time hint resumes measurably later than a
+// polling one, which lengthens the scan's dependent chain.
 __device__ __forceinline__ bool mbar_wait(uint32_t mbar, uint32_t parity) {
   for (int i = 0; i < (1 << 24); ++i) {
     uint32_t ok;
@@ -150,6 +152,19 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
       "l"(src), "r"(bytes), "r"(mbar)
       : "memory");
 }
+
+// Bulk (TMA engine) copy shared -> global; both addresses 16-byte aligned, bytes % 16 == 0.
+__device__ __forceinline__ void bulk_s2g(void* dst, uint32_t src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;\n" ::"l"(dst), "r"(src), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;\n" ::: "memory"); }
+// the shared-memory sources of this thread's committed bulk stores may be overwritten
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory"); }
+// this thread's committed bulk stores have completed
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory"); }
+// make this thread's generic-proxy shared-memory writes visible to the async proxy
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
 
 // XOR-swizzled bf16 tile with RL elements per row (RL % 64 == 0): the low three bits of the
 // 16-byte chunk index are XORed with (row & 7), so ldmatrix over 8 consecutive rows and
@@ -203,7 +218,7 @@ __host__ __device__ inline int64_t max_chunks_bound(int64_t L, int32_t N, int32_
 // kernel parameter blocks
 // ---------------------------------------------------------------------------
 struct IntraParams {
-  const WsHeader* hdr;
+  WsHeader* hdr;
   const ChunkDesc* table;
   int32_t H;
   const __nv_bfloat16* k;

@@ -10,12 +10,14 @@
 // ([chunk][head][D/64][64][64]), all bf16 in the scan's swizzled tile layout, and the chunk's
 // total decay 2^G_last (fp32, [chunk][head][D]).
 //
-// Numerics follow the reference's GPU rounding points: fp32 cumulative log2 decay;
-// exact-fp32 diagonal 16x16 key-key blocks; tf32 off-diagonal blocks built from operands
-// scaled to the first token of the row sub-chunk; fp32 forward substitution on the
-// diagonal blocks and tf32 products for the off-diagonal inverse blocks; A^-1 stored as
-// bf16; u = A^-1 bf16(v*w), w = A^-1 bf16(bf16(k*b) 2^G), kg = bf16(k 2^(G_last-G)), all
-// with fp32 accumulation.
+// Numerics follow the reference's GPU rounding points: fp32 cumulative log2 decay; fp32
+// diagonal 16x16 key-key blocks; off-diagonal blocks from tf32 operands scaled to the first
+// token of the row sub-chunk (per-channel decay); fp32 forward substitution on the diagonal
+// blocks and tf32 products for the off-diagonal inverse blocks; A^-1 stored as bf16;
+// u = A^-1 bf16(v*w), w = A^-1 bf16(bf16(k*b) 2^G), kg = bf16(k 2^(G_last-G)), all with fp32
+// accumulation. With a per-head decay every key-key block, diagonal or not, is the exact
+// bf16 product k'_i . k'_j (fp32 accumulation) times 2^(G_i - G_j) <= 1: more accurate than
+// the reference's tf32 operands for the off-diagonal blocks, and free of their conversions.
 //
 // Operand staging: k, erase, v, write (bf16) and the decay arrive by cp.async into
 // XOR-swizzled shared tiles. The tf32 score products take their fragments straight from
@@ -29,9 +31,9 @@
 // write kg (named barriers keep the two groups independent).
 //
 // Gate layouts:
-//   per head (one decay per token): every factor is a row or column scalar. The diagonal
+//   per head (one decay per token): every factor is a row or column scalar, so all key-key
 //     blocks are exact bf16 products (fp32 accumulation) times the per-pair 2^(G_i-G_j),
-//     which is the reference's fp32 sum; no factor can overflow.
+//     applied after the sum (exponents <= 0: no overflow).
 //   per channel: 2^G and 2^-G are tabulated once when every exponent of the panel lies in
 //     [-60, 60] and factors are products of table entries (diagonal blocks in 3xTF32);
 //     otherwise factors are exp2 of differences and the diagonal blocks are evaluated pair
@@ -220,7 +222,7 @@ struct IntraKernel {
     for (int i = tid - T0; i < kChunks; i += NTH) {
       const int row = i / (P / 8), col = (i % (P / 8)) * 8;
       const bool valid = row < ln;
-      cp_async16_zfill(dst + swz<P>(row, col), valid ? base + (int64_t)row * row_stride + col : src, valid);
+      cp_async16_zfill(dst + pswz(row, col), valid ? base + (int64_t)row * row_stride + col : src, valid);
     }
   }
 
@@ -245,7 +247,7 @@ struct IntraKernel {
     for (int i = tid; i < kChunks; i += NT) {
       const int row = i / (P / 8), col = (i % (P / 8)) * 8;
       if (row >= len) continue;
-      uint4* ptr = reinterpret_cast<uint4*>(sK + swz<P>(row, col));
+      uint4* ptr = reinterpret_cast<uint4*>(sK + pswz(row, col));
       uint4 kv = *ptr;
       float sb[8];
       if (p.beta_layout == 1) {
@@ -380,7 +382,51 @@ struct IntraKernel {
   }
 
   // ---- key-key scores of this panel, accumulated into acc[piece] ----
+  // Per-head decay: every piece is the exact product k'_i . k'_j (bf16 operands, fp32
+  // accumulation; with an erase factor the fp32 product k'*b is split into bf16 hi + lo parts,
+  // so the two bf16 products sum to the exact value); store_scores applies the per-pair decay
+  // 2^(G_i - G_j) <= 1 in fp32.
+  __device__ void scores_panel_head(float (&acc)[3][4], const __nv_bfloat16* sK) {
+    int r, nts[3];
+    score_pieces(warp, r, nts);
+    if (16 * r >= len) return;  // whole row block beyond the chunk (chunk_intra.py:242-278)
+    const int n_ref = 16 * r;
+#pragma unroll 4
+    for (int kk = 0; kk < P / 16; ++kk) {
+      uint32_t a[4], bq[3][2];
+      ldsm_x4(a, smem_u32(sK + pswz(n_ref + (lane & 15), 16 * kk + 8 * (lane >> 4))));
+#pragma unroll
+      for (int s = 0; s < 3; ++s)
+        if (nts[s] >= 0)
+          ldsm_x2(bq[s], smem_u32(sK + pswz(8 * nts[s] + (lane & 7), 16 * kk + 8 * ((lane >> 3) & 1))));
+      if constexpr (ERASE) {
+        uint32_t eb[4], hi[4], lo[4];
+        ldsm_x4(eb, smem_u32(sB + pswz(n_ref + (lane & 15), 16 * kk + 8 * (lane >> 4))));
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float p0 = bf_lo(a[q]) * bf_lo(eb[q]), p1 = bf_hi(a[q]) * bf_hi(eb[q]);
+          hi[q] = pack_bf16x2(p0, p1);
+          lo[q] = pack_bf16x2(p0 - bf_lo(hi[q]), p1 - bf_hi(hi[q]));
+        }
+#pragma unroll
+        for (int s = 0; s < 3; ++s)
+          if (nts[s] >= 0) {
+            mma_bf16_16816(acc[s], hi, bq[s]);
+            mma_bf16_16816(acc[s], lo, bq[s]);
+          }
+      } else {
+#pragma unroll
+        for (int s = 0; s < 3; ++s)
+          if (nts[s] >= 0) mma_bf16_16816(acc[s], a, bq[s]);
+      }
+    }
+  }
+
   __device__ void scores_panel(float (&acc)[3][4], const __nv_bfloat16* sK) {
+    if constexpr (HEAD) {
+      scores_panel_head(acc, sK);
+      return;
+    }
     int r, nts[3];
     score_pieces(warp, r, nts);
     if (16 * r >= len) return;  // whole row block beyond the chunk (chunk_intra.py:242-278)
@@ -402,13 +448,13 @@ struct IntraKernel {
     for (int kk = 0; kk < P / 16; ++kk) {
       // all fragment loads of the k-step first
       uint32_t a[4], eb[4] = {0u, 0u, 0u, 0u}, bq[3][2];
-      ldsm_x4(a, smem_u32(sK + swz<P>(n_ref + (lane & 15), 16 * kk + 8 * (lane >> 4))));
+      ldsm_x4(a, smem_u32(sK + pswz(n_ref + (lane & 15), 16 * kk + 8 * (lane >> 4))));
       if constexpr (ERASE)
-        ldsm_x4(eb, smem_u32(sB + swz<P>(n_ref + (lane & 15), 16 * kk + 8 * (lane >> 4))));
+        ldsm_x4(eb, smem_u32(sB + pswz(n_ref + (lane & 15), 16 * kk + 8 * (lane >> 4))));
 #pragma unroll
       for (int s = 0; s < 3; ++s)
         if (nts[s] >= 0)
-          ldsm_x2(bq[s], smem_u32(sK + swz<P>(8 * nts[s] + (lane & 7), 16 * kk + 8 * ((lane >> 3) & 1))));
+          ldsm_x2(bq[s], smem_u32(sK + pswz(8 * nts[s] + (lane & 7), 16 * kk + 8 * ((lane >> 3) & 1))));
       // left operand (tf32, two k8 slices) when the warp owns an off-diagonal piece, or per
       // channel (the diagonal pieces then use 3xTF32 as well)
       const int cA = 16 * kk + 2 * t;  // channel of the lo element of a[0]/a[1]
@@ -425,11 +471,12 @@ struct IntraKernel {
             x2 *= bf_lo(eb[2 * sl + 1]);
             x3 *= bf_hi(eb[2 * sl + 1]);
           }
+          // (row g, k-slot t), (row g+8, k-slot t), (row g, k-slot t+4), (row g+8, k-slot t+4)
           if constexpr (HEAD) {
-            lv[sl][0] = x0 * lf0;  // (row g,   k-slot t)
-            lv[sl][1] = x2 * lf1;  // (row g+8, k-slot t)
-            lv[sl][2] = x1 * lf0;  // (row g,   k-slot t+4)
-            lv[sl][3] = x3 * lf1;  // (row g+8, k-slot t+4)
+            lv[sl][0] = x0 * lf0;
+            lv[sl][1] = x2 * lf1;
+            lv[sl][2] = x1 * lf0;
+            lv[sl][3] = x3 * lf1;
           } else {
             const int c = cA + 8 * sl;
             const float2 f0 = p2d2(i0, n_ref, c), f1 = p2d2(i1, n_ref, c);
@@ -510,9 +557,9 @@ struct IntraKernel {
             float sum = 0.f;
             if (i < len && j < i) {
               for (int c = 0; c < P; ++c) {
-                float kb = __bfloat162float(sK[swz<P>(i, c)]);
-                if constexpr (ERASE) kb *= __bfloat162float(sB[swz<P>(i, c)]);
-                sum += kb * __bfloat162float(sK[swz<P>(j, c)]) *
+                float kb = __bfloat162float(sK[pswz(i, c)]);
+                if constexpr (ERASE) kb *= __bfloat162float(sB[pswz(i, c)]);
+                sum += kb * __bfloat162float(sK[pswz(j, c)]) *
                        fast_exp2(sE[i * Cfg::kLdE + c] - sE[j * Cfg::kLdE + c]);
               }
             }
@@ -531,15 +578,12 @@ struct IntraKernel {
 #pragma unroll
     for (int s = 0; s < 3; ++s) {
       if (nts[s] < 0) continue;
-      const bool diag = (nts[s] >> 1) == r;
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const int i = 16 * r + g + ((q & 2) ? 8 : 0);
         const int j = 8 * nts[s] + 2 * t + (q & 1);
         float x = acc[s][q];
-        if constexpr (HEAD) {
-          if (diag) x = (j < i && i < len) ? x * fast_exp2(sG[i] - sG[j]) : 0.f;
-        }
+        if constexpr (HEAD) x = (j < i && i < len) ? x * fast_exp2(sG[i] - sG[j]) : 0.f;
         if (j >= i || i >= len) x = 0.f;
         sA[i * Cfg::kLdA + j] = x;
       }
@@ -647,13 +691,13 @@ struct IntraKernel {
 #pragma unroll
     for (int i = tid - T0; i < kChunks; i += NTH) {
       const int row = i / (P / 8), col = (i % (P / 8)) * 8;
-      uint4 vv = *reinterpret_cast<const uint4*>(sV + swz<P>(row, col));
-      const uint4 ww = *reinterpret_cast<const uint4*>(sW + swz<P>(row, col));
+      uint4 vv = *reinterpret_cast<const uint4*>(sV + pswz(row, col));
+      const uint4 ww = *reinterpret_cast<const uint4*>(sW + pswz(row, col));
       uint32_t* vw = reinterpret_cast<uint32_t*>(&vv);
       const uint32_t* wg = reinterpret_cast<const uint32_t*>(&ww);
 #pragma unroll
       for (int e = 0; e < 4; ++e) vw[e] = pack_bf16x2(bf_lo(vw[e]) * bf_lo(wg[e]), bf_hi(vw[e]) * bf_hi(wg[e]));
-      *reinterpret_cast<uint4*>(sV + swz<P>(row, col)) = vv;
+      *reinterpret_cast<uint4*>(sV + pswz(row, col)) = vv;
     }
   }
 
@@ -667,12 +711,12 @@ struct IntraKernel {
 #pragma unroll
     for (int i = tid - T0; i < kChunks; i += NTH) {
       const int row = i / (P / 8), col = (i % (P / 8)) * 8;
-      uint4 kv = *reinterpret_cast<const uint4*>(kt + swz<P>(row, col));
+      uint4 kv = *reinterpret_cast<const uint4*>(kt + pswz(row, col));
       uint32_t* kw = reinterpret_cast<uint32_t*>(&kv);
       uint4 kgv;
       uint32_t* kgw = reinterpret_cast<uint32_t*>(&kgv);
       uint4 bv = make_uint4(0, 0, 0, 0);
-      if constexpr (ERASE) bv = *reinterpret_cast<const uint4*>(sB + swz<P>(row, col));
+      if constexpr (ERASE) bv = *reinterpret_cast<const uint4*>(sB + pswz(row, col));
       const uint32_t* bw = reinterpret_cast<const uint32_t*>(&bv);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -694,7 +738,7 @@ struct IntraKernel {
         else
           kw[e] = pack_bf16x2(k0 * e0, k1 * e1);
       }
-      *reinterpret_cast<uint4*>(kt + swz<P>(row, col)) = kv;  // w operand replaces k in place
+      *reinterpret_cast<uint4*>(kt + pswz(row, col)) = kv;  // w operand replaces k in place
       *reinterpret_cast<uint4*>(gKG + pswz(row, c0 + col)) = kgv;
     }
     const int j = tid - T0;
@@ -706,47 +750,52 @@ struct IntraKernel {
     }
   }
 
-  // sO (swizzled [64][P]) = A^-1 (lower) . src (swizzled [64][P]); warp w: row block w/2,
-  // column half w&1, k-steps 0..r only.
+  // dst ([64][P], pswz) = A^-1 (lower) . src ([64][P], pswz). Row block r needs k-steps 0..r,
+  // so warp w takes column quarter w % 4 of two row blocks with r + 1 summing to 5: blocks
+  // 3 and 0 (warps 0-3) or 2 and 1 (warps 4-7) -- the same work on every warp.
   __device__ void wy_product(const __nv_bfloat16* src, __nv_bfloat16* dst) {
-    const int r = warp >> 1, half = warp & 1;
-    constexpr int NTW = P / 16;
-    float acc[NTW][4];
-#pragma unroll
-    for (int i = 0; i < NTW; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-    const int n_base = half * (P / 2);
-    for (int ks = 0; ks <= r; ++ks) {
-      uint32_t a[4], b[NTW / 2][4];
-      ldsm_x4(a, smem_u32(sAi + (16 * r + (lane & 15)) * Cfg::kLdAi + 16 * ks + 8 * (lane >> 4)));
-#pragma unroll
-      for (int np = 0; np < NTW; np += 2)
-        ldsm_x4_t(b[np / 2], smem_u32(src + swz<P>(16 * ks + (lane & 15), n_base + 8 * np + 8 * (lane >> 4))));
-#pragma unroll
-      for (int np = 0; np < NTW; np += 2) {
-        uint32_t b0[2] = {b[np / 2][0], b[np / 2][1]}, b1[2] = {b[np / 2][2], b[np / 2][3]};
-        mma_bf16_16816(acc[np], a, b0);
-        mma_bf16_16816(acc[np + 1], a, b1);
-      }
-    }
+    constexpr int CW = P / 4;     // columns of a quarter
+    constexpr int NTW = CW / 8;   // 8-column tiles of a quarter
+    const int n_base = (warp & 3) * CW;
     const int g = lane >> 2, t = lane & 3;
 #pragma unroll
-    for (int nt = 0; nt < NTW; ++nt) {
-      const int col = n_base + 8 * nt + 2 * t;
-      const int i0 = 16 * r + g;
-      *reinterpret_cast<uint32_t*>(dst + swz<P>(i0, col)) = pack_bf16x2(acc[nt][0], acc[nt][1]);
-      *reinterpret_cast<uint32_t*>(dst + swz<P>(i0 + 8, col)) = pack_bf16x2(acc[nt][2], acc[nt][3]);
+    for (int half = 0; half < 2; ++half) {
+      const int r = (warp < 4) ? (half ? 0 : 3) : (half ? 1 : 2);
+      float acc[NTW][4];
+#pragma unroll
+      for (int i = 0; i < NTW; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+      for (int ks = 0; ks <= r; ++ks) {
+        uint32_t a[4], b[NTW / 2][4];
+        ldsm_x4(a, smem_u32(sAi + (16 * r + (lane & 15)) * Cfg::kLdAi + 16 * ks + 8 * (lane >> 4)));
+#pragma unroll
+        for (int np = 0; np < NTW; np += 2)
+          ldsm_x4_t(b[np / 2], smem_u32(src + pswz(16 * ks + (lane & 15), n_base + 8 * np + 8 * (lane >> 4))));
+#pragma unroll
+        for (int np = 0; np < NTW; np += 2) {
+          uint32_t b0[2] = {b[np / 2][0], b[np / 2][1]}, b1[2] = {b[np / 2][2], b[np / 2][3]};
+          mma_bf16_16816(acc[np], a, b0);
+          mma_bf16_16816(acc[np + 1], a, b1);
+        }
+      }
+#pragma unroll
+      for (int nt = 0; nt < NTW; ++nt) {
+        const int col = n_base + 8 * nt + 2 * t;
+        const int i0 = 16 * r + g;
+        *reinterpret_cast<uint32_t*>(dst + pswz(i0, col)) = pack_bf16x2(acc[nt][0], acc[nt][1]);
+        *reinterpret_cast<uint32_t*>(dst + pswz(i0 + 8, col)) = pack_bf16x2(acc[nt][2], acc[nt][3]);
+      }
     }
   }
 
-  // shared [64][P] tile (swz<P>) -> global [64][D] tile in the panel layout the scan reads
-  // (pswz: 64-column panels, each swz<64>, the canonical 128-byte-swizzled operand layout of
-  // the tensor-core descriptors); 16-byte stores
-  __device__ void store_panels(__nv_bfloat16* out, int c0, const __nv_bfloat16* src) {
-    constexpr int kChunks = kTile * P / 8;
-#pragma unroll
-    for (int i = tid; i < kChunks; i += NT) {
-      const int row = i / (P / 8), col = (i % (P / 8)) * 8;
-      *reinterpret_cast<uint4*>(out + pswz(row, c0 + col)) = *reinterpret_cast<const uint4*>(src + swz<P>(row, col));
+  // shared [64][P] tile (pswz) -> global [64][D] tile at column c0: shared tiles use the panel
+  // layout of the global tiles (64-column panels of 128-byte swizzled rows), so the tile is the
+  // same bytes at panel c0 / 64 and moves with one bulk copy, issued by thread 0 after the
+  // writers fenced their stores to the async proxy and a barrier. Thread 0 waits for the read
+  // (bulk_wait_read) before the shared tile is overwritten.
+  __device__ __forceinline__ void store_tile_async(__nv_bfloat16* out, int c0, const __nv_bfloat16* src) {
+    if (tid == 0) {
+      bulk_s2g(out + (c0 >> 6) * (kTile * 64), smem_u32(src), static_cast<uint32_t>(Cfg::kTileB));
+      bulk_commit();
     }
   }
 
@@ -874,11 +923,14 @@ struct IntraKernel {
         }
         __syncthreads();
         wy_product(kcur, sW);  // w = A^-1 . w operand; the w-gate tile is free
+        fence_proxy_async_smem();
         __syncthreads();
-        store_panels(gW, 0, sW);
+        store_tile_async(gW, 0, sW);
         wy_product(sV, kcur);  // u = A^-1 . bf16(v*w); the w operand is consumed
+        fence_proxy_async_smem();
         __syncthreads();
-        store_panels(gU, 0, kcur);
+        store_tile_async(gU, 0, kcur);
+        if (tid == 0) bulk_wait_read();  // before the next unit reloads sW and kcur
       } else {
         // ---- D = 256: panels one after the other ----
         if (warp < 4) solve();
@@ -892,8 +944,10 @@ struct IntraKernel {
           stage_w_kg<0, NT>(kcur, gKG, gEl, c0);
           __syncthreads();
           wy_product(kcur, sO);
+          fence_proxy_async_smem();
           __syncthreads();
-          store_panels(gW, c0, sO);
+          store_tile_async(gW, c0, sO);
+          if (tid == 0) bulk_wait_read();
           __syncthreads();
         }
         for (int pn = 0; pn < Cfg::kPanels; ++pn) {
@@ -905,11 +959,16 @@ struct IntraKernel {
           stage_u<0, NT>(p);
           __syncthreads();
           wy_product(sV, sO);
+          fence_proxy_async_smem();
           __syncthreads();
-          store_panels(gU, c0, sO);
+          store_tile_async(gU, c0, sO);
+          if (tid == 0) bulk_wait_read();
         }
       }
-      if (!has_next) break;
+      if (!has_next) {
+        if (tid == 0) bulk_wait_all();
+        break;
+      }
       unit = next;
       set_unit(p, unit);
       __syncthreads();  // the last tile stores read shared memory the next unit overwrites

@@ -45,6 +45,8 @@ static int launch_read_tc(const ReadParams& p, int64_t maxlen, cudaStream_t s) {
   P.p = p;
   const uint64_t row = static_cast<uint64_t>(p.H) * ReadTcCfg::D;
   cudaError_t e = make_tmap_bf16_2d(&P.q_map, p.q, row, static_cast<uint64_t>(p.L), row * 2, 64, ReadTcCfg::kTok);
+  if (e == cudaSuccess && p.out_bf16)
+    e = make_tmap_bf16_2d(&P.o_map, p.out, row, static_cast<uint64_t>(p.L), row * 2, 64, ReadTcCfg::kTok);
   if (e == cudaSuccess) e = ensure_smem(read_tc_kernel, ReadTcCfg::kSmem);
   if (e != cudaSuccess) return cuda_status(e);
   const int64_t per = int64_t(kReadTcTiles) * ReadTcCfg::kTok;

@@ -25,6 +25,15 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(mbar)
       : "memory");
 }
+// Store the shared-memory box at smem address src to (x, y) of the tensor (bulk group of this
+// thread; rows outside the tensor are not written). x * 2 bytes must be a multiple of 16.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int x, int y, uint32_t src) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];\n" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(x), "r"(y), "r"(src)
+      : "memory");
+}
 #endif
 
 }  // namespace memt
