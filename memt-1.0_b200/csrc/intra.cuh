@@ -242,21 +242,25 @@ struct IntraKernel {
   }
 
   // Fold sqrt(beta) into k in place: k' = bf16( bf16(sqrt(beta)) * k ) (models/qwen/layer.py:81-96)
-  __device__ void fold_beta(const IntraParams& p, __nv_bfloat16* sK, int c0) {
+  // for the unit (tk0, ln, hd) whose per-head scalars are in sPre half `ph`; threads [T0, T0 + NTH)
+  template <int T0, int NTH>
+  __device__ void fold_beta_for(const IntraParams& p, __nv_bfloat16* kbuf, int c0, int tk0, int ln, int hd, int ph) {
     constexpr int kChunks = kTile * P / 8;
-    for (int i = tid; i < kChunks; i += NT) {
+    static_assert(kChunks % NTH == 0, "chunks per thread");
+#pragma unroll
+    for (int i = tid - T0; i < kChunks; i += NTH) {
       const int row = i / (P / 8), col = (i % (P / 8)) * 8;
-      if (row >= len) continue;
-      uint4* ptr = reinterpret_cast<uint4*>(sK + pswz(row, col));
+      if (row >= ln) continue;
+      uint4* ptr = reinterpret_cast<uint4*>(kbuf + pswz(row, col));
       uint4 kv = *ptr;
       float sb[8];
       if (p.beta_layout == 1) {
-        const float s = sPre[pre * 2 * kTile + kTile + row];
+        const float s = sPre[ph * 2 * kTile + kTile + row];
 #pragma unroll
         for (int e = 0; e < 8; ++e) sb[e] = s;
       } else {
-        const uint4 be = *reinterpret_cast<const uint4*>(p.beta + (int64_t)(tok0 + row) * row_stride +
-                                                         (int64_t)h * D + c0 + col);
+        const uint4 be = *reinterpret_cast<const uint4*>(p.beta + (int64_t)(tk0 + row) * row_stride +
+                                                         (int64_t)hd * D + c0 + col);
         const uint32_t* bw = reinterpret_cast<const uint32_t*>(&be);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -269,6 +273,9 @@ struct IntraKernel {
       for (int e = 0; e < 4; ++e) kw[e] = pack_bf16x2(bf_lo(kw[e]) * sb[2 * e], bf_hi(kw[e]) * sb[2 * e + 1]);
       *ptr = kv;
     }
+  }
+  __device__ void fold_beta(const IntraParams& p, __nv_bfloat16* kbuf, int c0) {
+    fold_beta_for<0, NT>(p, kbuf, c0, tok0, len, h, pre);
   }
 
   // ---- decay, per-head layout: one warp computes every factor a chunk needs ----
@@ -920,6 +927,7 @@ struct IntraKernel {
               head_factors(sPre + (pre ^ 1) * 2 * kTile, sFac + (pre ^ 1) * Cfg::kSmall, d2.len);
             }
           }
+
         }
         __syncthreads();
         wy_product(kcur, sW);  // w = A^-1 . w operand; the w-gate tile is free

@@ -28,6 +28,9 @@ cudaError_t ensure_smem(Kernel kernel, size_t bytes) {
   auto key = std::make_pair(reinterpret_cast<const void*>(kernel), dev);
   if (done.count(key)) return cudaSuccess;
   e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+  // the whole unified L1 as shared memory, so that two large-tile CTAs fit on one SM
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
   if (e == cudaSuccess) done.insert(key);
   return e;
 }

@@ -10,9 +10,12 @@
 //   * a control warp issues the 128x128x128 MMA of each tile into one of two tensor-memory
 //     accumulators and refills the query stage once the MMA has consumed it;
 //   * eight worker warps drain the other accumulator: warp w reads tokens 32 (w % 4).. and
-//     columns 64 (w / 4).., scales, rounds and stores 128 contiguous bytes per token.
-// Rows past the block end (the tile straddles into the next block or past L) are computed
-// from whatever the TMA brought (zeros past L) and not stored. Every wait is bounded.
+//     columns 64 (w / 4).., scales and rounds; a bf16 output tile goes back into the query
+//     stage it came from (the MMA has consumed it) in the TMA box layout and leaves with two
+//     TMA stores, after which the stage takes the query tile two ahead.
+// The last tile of a block may straddle into the next block (or past L): its rows are
+// computed from whatever the TMA brought (zeros past L) and stored row by row up to the block
+// end instead. Every wait is bounded.
 #pragma once
 
 #include "common.cuh"
@@ -26,22 +29,23 @@ constexpr int kReadTcTiles = 8;  // 128-token tiles per CTA
 
 struct ReadTcParams {
   CUtensorMap q_map;  // bf16 [L, H*D], boxes of 64 x 128
+  CUtensorMap o_map;  // bf16 output, same geometry (used when out_bf16)
   ReadParams p;
 };
 
 struct ReadTcCfg {
   static constexpr int D = 128, kTok = 128;
-  static constexpr int kWorkers = 256;
-  static constexpr int kThreads = kWorkers + 32;
+  static constexpr int kWorkerWarps = 8;
+  static constexpr int kThreads = (kWorkerWarps + 1) * 32;
   static constexpr uint32_t kBytesS = D * D * 2;          // 32 KB
-  static constexpr uint32_t kBytesQ = kTok * D * 2;       // 32 KB per stage
+  static constexpr uint32_t kBytesQ = kTok * D * 2;       // 32 KB per stage (query tile, then output tile)
   static constexpr uint32_t kOffQ = kBytesS;
   static constexpr uint32_t kOffBar = kOffQ + 2 * kBytesQ;
   static constexpr size_t kSmem = kOffBar + 128 + 1024;
   static constexpr uint32_t kTmemCols = 256;
 };
 
-__global__ void __launch_bounds__(ReadTcCfg::kThreads, 1) read_tc_kernel(const __grid_constant__ ReadTcParams P) {
+__global__ void __launch_bounds__(ReadTcCfg::kThreads, 2) read_tc_kernel(const __grid_constant__ ReadTcParams P) {
   using Cfg = ReadTcCfg;
   constexpr int D = Cfg::D;
   const ReadParams& p = P.p;
@@ -56,21 +60,24 @@ __global__ void __launch_bounds__(ReadTcCfg::kThreads, 1) read_tc_kernel(const _
   if (first >= eos) return;
   int ntiles = (int)((eos - first + Cfg::kTok - 1) / Cfg::kTok);
   if (ntiles > kReadTcTiles) ntiles = kReadTcTiles;
+  const bool tma_out = p.out_bf16 != 0;
+  auto full_tile = [&](int i) { return first + (int64_t)(i + 1) * Cfg::kTok <= eos; };
 
-  // barriers: 0/1 query stage full (TMA), 2/3 accumulator full (commit),
-  // 4/5 accumulator drained (workers), 6 snapshot operand written (workers)
+  // barriers: 0/1 stage holds the query tile (TMA), 2/3 accumulator full (commit),
+  // 4/5 accumulator drained, 6 snapshot operand written, 7/8 output tile written to the stage
+  // (4-8: one arrival per worker warp)
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + Cfg::kOffBar);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + Cfg::kOffBar + 64);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + Cfg::kOffBar + 96);
   auto B = [&](int i) { return smem_u32(&bar[i]); };
   unsigned char* sS = sm;
   const uint32_t sQ = smem_u32(sm + Cfg::kOffQ);
 
   if (tid == 0) {
     for (int i = 0; i < 4; ++i) mbar_init(B(i), 1);
-    for (int i = 4; i < 7; ++i) mbar_init(B(i), Cfg::kWorkers);
+    for (int i = 4; i < 9; ++i) mbar_init(B(i), Cfg::kWorkerWarps);
     mbar_fence_init();
   }
-  if (warp == 8) tc::alloc(smem_u32(tmem_slot), Cfg::kTmemCols);
+  if (warp == Cfg::kWorkerWarps) tc::alloc(smem_u32(tmem_slot), Cfg::kTmemCols);
   tc::fence_before();
   __syncthreads();
   tc::fence_after();
@@ -81,14 +88,28 @@ __global__ void __launch_bounds__(ReadTcCfg::kThreads, 1) read_tc_kernel(const _
     if (alive && !mbar_wait(B(b), parity)) alive = false;
   };
 
-  if (warp == 8) {
+  if (warp == Cfg::kWorkerWarps) {
     if (lane == 0) {
+      // Stage s cycles: query tile i (TMA load) -> MMA(i) -> output tile i (workers) ->
+      // TMA store -> query tile i + 2.
       auto load_q = [&](int i) {
         const int s = i & 1;
         const int y = static_cast<int>(first + (int64_t)i * Cfg::kTok);
         mbar_expect_tx(B(s), Cfg::kBytesQ);
         tma_load_2d(sQ + s * Cfg::kBytesQ, &P.q_map, h * D, y, B(s));
         tma_load_2d(sQ + s * Cfg::kBytesQ + Cfg::kBytesQ / 2, &P.q_map, h * D + 64, y, B(s));
+      };
+      auto store_out = [&](int i) {  // output tile i has been written to its stage
+        const int s = i & 1;
+        wait(7 + s, (i >> 1) & 1);
+        if (tma_out && full_tile(i)) {
+          fence_proxy_async_smem();
+          const int y = static_cast<int>(first + (int64_t)i * Cfg::kTok);
+          tma_store_2d(&P.o_map, h * D, y, sQ + s * Cfg::kBytesQ);
+          tma_store_2d(&P.o_map, h * D + 64, y, sQ + s * Cfg::kBytesQ + Cfg::kBytesQ / 2);
+          bulk_commit();
+          bulk_wait_read();
+        }
       };
       load_q(0);
       if (ntiles > 1) load_q(1);
@@ -106,11 +127,13 @@ __global__ void __launch_bounds__(ReadTcCfg::kThreads, 1) read_tc_kernel(const _
           tc::mma_bf16(tmem + 128 * s, tc::desc_kmajor(q + (ks >> 2) * (Cfg::kBytesQ / 2), (ks & 3) * 32),
                        tc::desc_mnmajor(ss, Cfg::kBytesS / 2, ks), kId, ks > 0);
         tc::commit(B(2 + s));
-        if (i + 2 < ntiles) {  // the stage is free once this MMA has read it
-          wait(2 + s, (i >> 1) & 1);
-          load_q(i + 2);
+        if (i >= 1) {
+          store_out(i - 1);
+          if (i + 1 < ntiles) load_q(i + 1);
         }
       }
+      store_out(ntiles - 1);
+      bulk_wait_all();
     }
   } else {
     // snapshot -> bf16 MN-major operand: thread t converts row t / 2, values 64 (t % 2) ..
@@ -130,22 +153,37 @@ __global__ void __launch_bounds__(ReadTcCfg::kThreads, 1) read_tc_kernel(const _
         *reinterpret_cast<uint4*>(dst + ((c ^ (row & 7)) << 4)) = pk;
       }
       tc::fence_smem_async();
-      mbar_arrive(B(6));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(B(6));
     }
     const int quarter = warp & 3, half = warp >> 2;
     const int64_t qrow = (int64_t)p.H * D;
+    const int r = 32 * quarter + lane;  // token row of the tile
     for (int i = 0; i < ntiles; ++i) {
       const int s = i & 1;
-      wait(2 + s, (i >> 1) & 1);
+      wait(2 + s, (i >> 1) & 1);  // MMA(i) done: its query stage is free for the output
       __syncwarp();
       tc::fence_after();
       float o[2][32];
       tc::ld32(tc::lane_addr(tmem + 128 * s, 32 * quarter, 64 * half), o[0]);
       tc::ld32(tc::lane_addr(tmem + 128 * s, 32 * quarter, 64 * half + 32), o[1]);
       tc::fence_before();
-      mbar_arrive(B(4 + s));  // the accumulator may be overwritten
-      const int64_t tok = first + (int64_t)i * Cfg::kTok + 32 * quarter + lane;
-      if (tok < eos) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(B(4 + s));  // the accumulator may be overwritten
+      const int64_t tok = first + (int64_t)i * Cfg::kTok + r;
+      if (tma_out && full_tile(i)) {
+        // output tile in the box layout of the TMA store: value panel `half`, row r
+        unsigned char* row = sm + Cfg::kOffQ + s * Cfg::kBytesQ + half * (Cfg::kBytesQ / 2) + (r >> 3) * 1024 +
+                             (r & 7) * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const float* v = &o[c >> 2][(c & 3) * 8];
+          *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) << 4)) =
+              make_uint4(pack_bf16x2(v[0] * p.scale, v[1] * p.scale), pack_bf16x2(v[2] * p.scale, v[3] * p.scale),
+                         pack_bf16x2(v[4] * p.scale, v[5] * p.scale), pack_bf16x2(v[6] * p.scale, v[7] * p.scale));
+        }
+        fence_proxy_async_smem();
+      } else if (tok < eos) {
         const int64_t off = tok * qrow + (int64_t)h * D + 64 * half;
         if (p.out_bf16) {
           uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + off);
@@ -164,11 +202,13 @@ __global__ void __launch_bounds__(ReadTcCfg::kThreads, 1) read_tc_kernel(const _
           }
         }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(B(7 + s));  // output tile i is in the stage (or stored)
     }
   }
   tc::fence_before();
   __syncthreads();
-  if (warp == 8) tc::dealloc(tmem, Cfg::kTmemCols);
+  if (warp == Cfg::kWorkerWarps) tc::dealloc(tmem, Cfg::kTmemCols);
 }
 
 }  // namespace memt

@@ -141,11 +141,13 @@ def _gather_chunks(x, chunks, tile=TILE):
     return out.transpose(0, 2, 1, 3)
 
 
-def intra(k, g, v, chunks, *, b=None, w=None, mode="exact"):
+def intra(k, g, v, chunks, *, b=None, w=None, mode="exact", exact_scores=False):
     """Per-chunk WY operands. Returns dict with G, Ainv, u, w_wy, kg, g_last (all [NC,H,...]).
 
     Follows the reference's GPU algorithm; ``mode`` selects exact float64 or the
-    GPU rounding points (see module docstring).
+    GPU rounding points (see module docstring). ``exact_scores`` drops the tf32 rounding of
+    the off-diagonal score operands (the sm_100a kernel's evaluation for a per-head decay:
+    exact products scaled by 2^(G_i - G_j)); the default is the reference's.
     """
     emu = mode == "bf16"
     rb = bf16 if emu else _id
@@ -182,9 +184,10 @@ def intra(k, g, v, chunks, *, b=None, w=None, mode="exact"):
         # off-diagonal blocks: reference point = first token of the row sub-chunk
         # (chunk_intra.py:251-253, 267-271, 287-297)
         gn = G[:, :, r * SUB, :][:, :, None, :]  # [NC,H,1,K]
-        left = rt(kb[:, :, rows] * np.exp2(G[:, :, rows] - gn)) * vmask[:, :, rows]
+        rs = _id if exact_scores else rt
+        left = rs(kb[:, :, rows] * np.exp2(G[:, :, rows] - gn)) * vmask[:, :, rows]
         cols = slice(0, r * SUB)
-        right = rt(kc[:, :, cols] * np.exp2(gn - G[:, :, cols]))
+        right = rs(kc[:, :, cols] * np.exp2(gn - G[:, :, cols]))
         A[:, :, rows, cols] = rf(np.einsum("nhic,nhjc->nhij", left, right))
     # rows of sub-chunks that start beyond the chunk length are skipped by the kernel
     A *= valid[:, None, :, None]
@@ -271,10 +274,11 @@ def read(q, states, cu_seqlens, scale, *, mode="exact"):
     return o
 
 
-def chunked(q, k, v, g, h0, r0, cu_seqlens, scale, *, b=None, w=None, chunk_tokens=2048, mode="exact"):
+def chunked(q, k, v, g, h0, r0, cu_seqlens, scale, *, b=None, w=None, chunk_tokens=2048, mode="exact",
+            exact_scores=False):
     """token_memory_packed: (read of the incoming snapshot r0, final state from h0)."""
     chunks = plan_chunks(cu_seqlens, chunk_tokens)
-    ops = intra(k, g, v, chunks, b=b, w=w, mode=mode)
+    ops = intra(k, g, v, chunks, b=b, w=w, mode=mode, exact_scores=exact_scores)
     final = scan(ops, chunks, h0, mode=mode)
     o = read(q, r0, cu_seqlens, scale, mode=mode)
     return o, final
