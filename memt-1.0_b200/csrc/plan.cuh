@@ -68,23 +68,8 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ 
     if (n < N) {
       int64_t room = max_chunks - off;
       if (room < 0) room = 0;
-      if (cnt > room) {
-        atomicOr(&s_status, 2);
-        cnt = static_cast<int32_t>(room);
-      }
+      if (cnt > room) atomicOr(&s_status, 2);
       sample_off[n] = static_cast<int32_t>(off < max_chunks ? off : max_chunks);
-      int32_t c = 0;
-      for (int64_t e0 = bos; e0 < eos && c < cnt; e0 += chunk_tokens) {
-        const int64_t e1 = (e0 + chunk_tokens < eos) ? e0 + chunk_tokens : eos;
-        for (int64_t t0 = e0; t0 < e1 && c < cnt; t0 += kTile, ++c) {
-          ChunkDesc d;
-          d.sample = n;
-          d.tok0 = static_cast<int32_t>(t0);
-          d.len = static_cast<int32_t>((e1 - t0) < kTile ? (e1 - t0) : kTile);
-          d.pad = 0;
-          table[off + c] = d;
-        }
-      }
     }
     __syncthreads();
     if (tid == 0) {
@@ -93,8 +78,35 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ 
     }
     __syncthreads();
   }
+  if (tid == 0) sample_off[N] = s_base;
+  __syncthreads();
+  // Table entries, one chunk per thread: the sample owning chunk c is the last n with
+  // sample_off[n] <= c (binary search; empty samples share their offset with the next one);
+  // inside a sample, chunk j is tile j % per_event of write event j / per_event.
+  const int32_t total = s_base;
+  const int32_t per_event = (chunk_tokens + kTile - 1) / kTile;
+  for (int32_t c = tid; c < total; c += blockDim.x) {
+    int32_t lo = 0, hi = N - 1;
+    while (lo < hi) {
+      const int32_t mid = (lo + hi + 1) >> 1;
+      if (sample_off[mid] <= c) lo = mid; else hi = mid - 1;
+    }
+    const int32_t n = lo;
+    int64_t a = cu_seqlens[n], b = cu_seqlens[n + 1];
+    const int64_t bos = a < 0 ? 0 : (a > L ? L : a);
+    const int64_t eos = b < bos ? bos : (b > L ? L : b);
+    const int32_t j = c - sample_off[n];
+    const int64_t e0 = bos + static_cast<int64_t>(j / per_event) * chunk_tokens;
+    const int64_t e1 = (e0 + chunk_tokens < eos) ? e0 + chunk_tokens : eos;
+    const int64_t t0 = e0 + static_cast<int64_t>(j % per_event) * kTile;
+    ChunkDesc d;
+    d.sample = n;
+    d.tok0 = static_cast<int32_t>(t0);
+    d.len = static_cast<int32_t>((e1 - t0) < kTile ? (e1 - t0) : kTile);
+    d.pad = 0;
+    table[c] = d;
+  }
   if (tid == 0) {
-    sample_off[N] = s_base;
     hdr->num_chunks = s_base;
     hdr->status = s_status;
   }
