@@ -165,8 +165,8 @@ __global__ void __launch_bounds__(ReadTcCfg::kThreads, 2) read_tc_kernel(const _
       __syncwarp();
       tc::fence_after();
       float o[2][32];
-      tc::ld32(tc::lane_addr(tmem + 128 * s, 32 * quarter, 64 * half), o[0]);
-      tc::ld32(tc::lane_addr(tmem + 128 * s, 32 * quarter, 64 * half + 32), o[1]);
+      tc::ld32x2(tc::lane_addr(tmem + 128 * s, 32 * quarter, 64 * half),
+                 tc::lane_addr(tmem + 128 * s, 32 * quarter, 64 * half + 32), o[0], o[1]);
       tc::fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(B(4 + s));  // the accumulator may be overwritten

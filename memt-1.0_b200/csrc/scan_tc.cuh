@@ -148,12 +148,12 @@ __global__ void __launch_bounds__(ScanTcCfg::kThreads, 1) scan_tc_kernel(ScanPar
     float el = 1.f;  // 2^G_last of the previous chunk for this key row
     auto update_state = [&]() {  // S = 2^G_last S + P
       tc::fence_after();
+      float P0[32], P1[32];
+      tc::ld32x2(tc::lane_addr(tP, 32 * quarter, 64 * half), tc::lane_addr(tP, 32 * quarter, 64 * half + 32), P0, P1);
 #pragma unroll
-      for (int j0 = 0; j0 < 64; j0 += 32) {
-        float P[32];
-        tc::ld32(tc::lane_addr(tP, 32 * quarter, 64 * half + j0), P);
-#pragma unroll
-        for (int j = 0; j < 32; ++j) S[j0 + j] = fmaf(el, S[j0 + j], P[j]);
+      for (int j = 0; j < 32; ++j) {
+        S[j] = fmaf(el, S[j], P0[j]);
+        S[32 + j] = fmaf(el, S[32 + j], P1[j]);
       }
     };
     auto hand_over = [&](int b) {  // operand tile written: make it visible to the tensor cores
