@@ -228,21 +228,27 @@ def run_ours(args, rank, world, local_rank):
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     gpu_uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
-    _lib.profiler_reset()
     barrier()
     torch.cuda.synchronize()
     with ClockSampler(gpu_uuid) as clocks:
-        _lib.profiler_enable(True)
         for i in range(args.steps):
             flush.zero_()
             starts[i].record(stream)
             step()
             ends[i].record(stream)
         torch.cuda.synchronize()
-        _lib.profiler_enable(False)
     barrier()
     torch.cuda.synchronize()
     ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / args.steps
+    # per-kernel device times from the library's event profiler, in a separate pass of the same
+    # steps (its events between launches are kept out of the timed region above)
+    _lib.profiler_reset()
+    _lib.profiler_enable(True)
+    for i in range(args.steps):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    _lib.profiler_enable(False)
     prof = _lib.profiler_read()
     _lib.profiler_reset()
     launches = sum(n for _, n in prof.values())

@@ -153,6 +153,14 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
       : "memory");
 }
 
+// Programmatic dependent launch: a kernel launched with programmatic stream serialization
+// may start while the previous kernel of the stream is still running. It must call
+// griddep_wait() before touching global memory that any earlier work produces (it returns
+// once the previous grid has completed and its writes are visible; a no-op otherwise);
+// griddep_launch_dependents() lets the next such kernel start its own prologue early.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;\n" :::); }
+
 // Bulk (TMA engine) copy shared -> global; both addresses 16-byte aligned, bytes % 16 == 0.
 __device__ __forceinline__ void bulk_s2g(void* dst, uint32_t src, uint32_t bytes) {
   asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;\n" ::"l"(dst), "r"(src), "r"(bytes)

@@ -17,8 +17,7 @@ static int launch_intra_t(const IntraParams& p, int64_t max_chunks, cudaStream_t
   const int64_t units = max_chunks * p.H;
   const unsigned grid = static_cast<unsigned>(units < slots ? units : slots);
   ProfScope prof(kProfIntra, s);
-  kernel<<<grid, Cfg::kThreads, Cfg::kSmem, s>>>(p);
-  return cuda_status(cudaGetLastError());
+  return cuda_status(launch_pdl(kernel, dim3(grid), dim3(Cfg::kThreads), Cfg::kSmem, s, p));
 }
 
 template <int D>

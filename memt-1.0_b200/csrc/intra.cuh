@@ -816,6 +816,8 @@ struct IntraKernel {
   }
 
   __device__ void run(const IntraParams& p) {
+    griddep_wait();               // the chunk table and every input are complete
+    griddep_launch_dependents();  // the scan may set up while the last units run
     const int64_t units = (int64_t)p.hdr->num_chunks * p.H;
     int64_t unit = blockIdx.x;
     if (unit >= units) return;

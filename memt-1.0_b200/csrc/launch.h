@@ -72,6 +72,24 @@ cudaError_t resident_slots(Kernel kernel, int threads, size_t smem, int* slots) 
   return cudaSuccess;
 }
 
+// Launch with programmatic stream serialization (the kernel calls griddep_wait() before it
+// reads anything earlier work produces).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 int launch_plan(const int32_t* cu, int32_t N, int64_t L, int32_t chunk_tokens, int32_t max_chunks,
                 WsHeader* hdr, ChunkDesc* table, int32_t* sample_off, cudaStream_t s);
 int launch_intra(int D, bool erase, const IntraParams& p, int64_t max_chunks, cudaStream_t s);

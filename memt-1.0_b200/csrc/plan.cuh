@@ -24,6 +24,7 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ 
   __shared__ int32_t s_status;
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
+  griddep_launch_dependents();  // the intra kernel waits for this grid before it reads the table
   if (tid == 0) {
     s_base = 0;
     s_status = 0;

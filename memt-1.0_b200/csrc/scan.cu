@@ -12,8 +12,7 @@ static int launch_scan_t(const ScanParams& p, cudaStream_t s) {
   if (e != cudaSuccess) return cuda_status(e);
   const unsigned grid = static_cast<unsigned>(p.N) * p.H * (D / Cfg::BV);
   ProfScope prof(kProfScan, s);
-  scan_kernel<D><<<grid, Cfg::kThreads, Cfg::kSmem, s>>>(p);
-  return cuda_status(cudaGetLastError());
+  return cuda_status(launch_pdl(scan_kernel<D>, dim3(grid), dim3(Cfg::kThreads), Cfg::kSmem, s, p));
 }
 
 // d = 128: tcgen05 kernel, one CTA per (sample, head)
@@ -22,8 +21,7 @@ static int launch_scan_tc(const ScanParams& p, cudaStream_t s) {
   if (e != cudaSuccess) return cuda_status(e);
   const unsigned grid = static_cast<unsigned>(p.N) * p.H;
   ProfScope prof(kProfScan, s);
-  scan_tc_kernel<<<grid, ScanTcCfg::kThreads, ScanTcCfg::kSmem, s>>>(p);
-  return cuda_status(cudaGetLastError());
+  return cuda_status(launch_pdl(scan_tc_kernel, dim3(grid), dim3(ScanTcCfg::kThreads), ScanTcCfg::kSmem, s, p));
 }
 
 int launch_scan(int D, const ScanParams& p, cudaStream_t s) {

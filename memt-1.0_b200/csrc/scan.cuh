@@ -66,6 +66,8 @@ __global__ void __launch_bounds__(ScanCfg<D>::kThreads) scan_kernel(ScanParams p
     bulk_g2s(smem_u32(sEl(st)), p.Elast + ch * D, Cfg::kBytesEl, mb);
   };
 
+  griddep_wait();
+  griddep_launch_dependents();
   const int c0 = p.sample_off[n], c1 = p.sample_off[n + 1];
   if (tid == 0) {
     mbar_init(smem_u32(&mbar[0]), 1);

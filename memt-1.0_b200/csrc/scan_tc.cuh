@@ -61,9 +61,6 @@ __global__ void __launch_bounds__(ScanTcCfg::kThreads, 1) scan_tc_kernel(ScanPar
   unsigned char* sSb = sm + Cfg::kOffSb;  // Sb^T: 2 value panels of [128 key rows][64 values]
   unsigned char* sVn = sm + Cfg::kOffVn;  // v_new: [128 value rows][64 tokens]
 
-  const int c0 = p.sample_off[n], c1 = p.sample_off[n + 1];
-  const int nchunks = c1 - c0;
-
   if (tid == 0) {
     for (int i = 0; i < 5; ++i) mbar_init(B(i), 1);
     mbar_init(B(5), Cfg::kWorkerWarps);
@@ -76,6 +73,10 @@ __global__ void __launch_bounds__(ScanTcCfg::kThreads, 1) scan_tc_kernel(ScanPar
   tc::fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t tP = tmem, tX = tmem + 128;
+  griddep_wait();  // the intra kernel's tiles and the chunk offsets are complete
+  griddep_launch_dependents();
+  const int c0 = p.sample_off[n], c1 = p.sample_off[n + 1];
+  const int nchunks = c1 - c0;
 
   bool alive = true;
   auto wait = [&](int b, uint32_t parity) {
