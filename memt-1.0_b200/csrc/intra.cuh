@@ -230,15 +230,26 @@ struct IntraKernel {
   // bf16(sqrt(beta)) of a per-head beta. Threads [t0, t0 + 64); issued one unit ahead so the
   // global-load latency hides behind the previous unit's solve.
   __device__ void fetch_scalars(const IntraParams& p, int tk0, int ln, int hd, float* buf, int t0) {
+    float gv, bv;
+    load_scalars(p, tk0, ln, hd, t0, gv, bv);
+    store_scalars(buf, t0, gv, bv);
+  }
+  // the two halves of fetch_scalars: issue the loads early, store once other work is done
+  __device__ __forceinline__ void load_scalars(const IntraParams& p, int tk0, int ln, int hd, int t0, float& gv,
+                                               float& bv) const {
+    const int i = tid - t0;
+    gv = 0.f;
+    bv = 0.f;
+    if (i >= 0 && i < ln && i < kTile) {
+      if constexpr (HEAD) gv = p.g[(int64_t)(tk0 + i) * p.H + hd];
+      if (p.beta_layout == 1) bv = __bfloat162float(p.beta[(int64_t)(tk0 + i) * p.H + hd]);
+    }
+  }
+  __device__ __forceinline__ void store_scalars(float* buf, int t0, float gv, float bv) const {
     const int i = tid - t0;
     if (i < 0 || i >= kTile) return;
-    float gv = 0.f, bv = 0.f;
-    if (i < ln) {
-      if constexpr (HEAD) gv = p.g[(int64_t)(tk0 + i) * p.H + hd];
-      if (p.beta_layout == 1) bv = bf16_round(sqrtf(__bfloat162float(p.beta[(int64_t)(tk0 + i) * p.H + hd])));
-    }
     buf[i] = gv;
-    buf[kTile + i] = bv;
+    buf[kTile + i] = bv > 0.f ? bf16_round(sqrtf(bv)) : 0.f;
   }
 
   // Fold sqrt(beta) into k in place: k' = bf16( bf16(sqrt(beta)) * k ) (models/qwen/layer.py:81-96)
@@ -846,6 +857,13 @@ struct IntraKernel {
       load_tile(sV, p.v, c0);
       if (p.write != nullptr) load_tile(sW, p.write, c0);
     };
+    // with the solve / staging split only the staging warps use v and w: they load them alone
+    auto load_value_panel_staging = [&]() {
+      if (warp >= 4) {
+        load_tile_for<128, 128>(sV, p.v, 0, tok0, len, h);
+        if (p.write != nullptr) load_tile_for<128, 128>(sW, p.write, 0, tok0, len, h);
+      }
+    };
     auto prepare_key_panel = [&](int c0) {  // after the key panel landed
       __syncthreads();
       if (p.beta_layout != 0) {
@@ -872,7 +890,7 @@ struct IntraKernel {
       __nv_bfloat16* gKG = p.KG + chunk_head * kTile * D;
       float* gEl = p.Elast + chunk_head * D;
 
-      if constexpr (kOverlap) load_value_panel(0);
+      if constexpr (kOverlap) load_value_panel_staging();
       cp_async_commit();
       if constexpr (HEAD) {
         use_factors(pre);
@@ -897,14 +915,18 @@ struct IntraKernel {
           cp_async_commit();
           cp_async_wait<0>();
         } else {
-          cp_async_wait<1>();  // the key group (older than the value group) landed
+          // the key group landed (warps 4-7 also have the younger value group in flight)
+          if (kOverlap && warp < 4)
+            cp_async_wait<0>();
+          else
+            cp_async_wait<1>();
         }
         prepare_key_panel(pn * P);
         scores_panel(acc, kcur);
       }
       __syncthreads();
       store_scores(acc);
-      cp_async_wait<0>();  // every thread's copies of v and w are complete
+      if constexpr (!kOverlap) cp_async_wait<0>();  // every thread's copies of v and w are complete
       __syncthreads();
 
       if constexpr (kOverlap) {
@@ -913,14 +935,18 @@ struct IntraKernel {
         if (warp < 4) {
           solve();
         } else {
+          cp_async_wait<0>();  // this thread's copies of v and w
+          named_sync(2, 128);  // ... and every staging thread's
+          float ng = 0.f, nb = 0.f;  // next unit's scalars, loaded now, stored after stage_u
           if (has_next) {
             const int c2 = static_cast<int>(next / p.H), h2 = static_cast<int>(next % p.H);
             const ChunkDesc d2 = p.table[c2];
-            fetch_scalars(p, d2.tok0, d2.len, h2, sPre + (pre ^ 1) * 2 * kTile, 128);
+            load_scalars(p, d2.tok0, d2.len, h2, 128, ng, nb);
             if constexpr (kPrefetch) load_tile_for<128, 128>(kspare, p.k, 0, d2.tok0, d2.len, h2);
           }
           if constexpr (kPrefetch) cp_async_commit();
           stage_u<128, 128>(p);
+          if (has_next) store_scalars(sPre + (pre ^ 1) * 2 * kTile, 128, ng, nb);
           named_sync(2, 128);
           stage_w_kg<128, 128>(kcur, gKG, gEl, 0);
           if constexpr (kNextFactors) {
