@@ -924,8 +924,7 @@ struct IntraKernel {
         prepare_key_panel(pn * P);
         scores_panel(acc, kcur);
       }
-      __syncthreads();
-      store_scores(acc);
+      store_scores(acc);  // nothing reads the score buffer while the scores are formed
       if constexpr (!kOverlap) cp_async_wait<0>();  // every thread's copies of v and w are complete
       __syncthreads();
 
