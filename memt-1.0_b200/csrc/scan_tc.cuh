@@ -185,30 +185,32 @@ __global__ void __launch_bounds__(ScanTcCfg::kThreads, 1) scan_tc_kernel(ScanPar
       }
       hand_over(5);
       // ---- v_new = bf16(u - X) -> K-major operand [value row][64 tokens] ----
+      // u of this thread's value column is read while X^T is still being computed
       wait(st, (it / Cfg::kStages) & 1);
       el = st_el(st)[key];
+      float uv[32];
+      {
+        const unsigned char* u = st_u(st) + (key >> 6) * (kTile * 128);  // value panel of u
+        const int vc = (key & 63) >> 3, vb = (key & 7) * 2;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int t = 32 * half + e;
+          uv[e] = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(u + t * 128 + ((vc ^ (t & 7)) << 4) + vb));
+        }
+      }
       wait(3, ph);
       tc::fence_after();
       {
         float X[32];
         tc::ld32(tc::lane_addr(tX, 32 * quarter, 32 * half), X);  // value `key`, tokens 32 half ..
-        const unsigned char* u = st_u(st) + (key >> 6) * (kTile * 128);  // value panel of u
-        const int vc = (key & 63) >> 3, vb = (key & 7) * 2;
         unsigned char* vrow = sVn + (key >> 3) * 1024 + (key & 7) * 128;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          float vn[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const int t = 32 * half + 8 * c + e;
-            const __nv_bfloat16 uv = *reinterpret_cast<const __nv_bfloat16*>(u + t * 128 + ((vc ^ (t & 7)) << 4) + vb);
-            vn[e] = __bfloat162float(uv) - X[8 * c + e];
-          }
           uint4 pk;
-          pk.x = pack_bf16x2(vn[0], vn[1]);
-          pk.y = pack_bf16x2(vn[2], vn[3]);
-          pk.z = pack_bf16x2(vn[4], vn[5]);
-          pk.w = pack_bf16x2(vn[6], vn[7]);
+          pk.x = pack_bf16x2(uv[8 * c] - X[8 * c], uv[8 * c + 1] - X[8 * c + 1]);
+          pk.y = pack_bf16x2(uv[8 * c + 2] - X[8 * c + 2], uv[8 * c + 3] - X[8 * c + 3]);
+          pk.z = pack_bf16x2(uv[8 * c + 4] - X[8 * c + 4], uv[8 * c + 5] - X[8 * c + 5]);
+          pk.w = pack_bf16x2(uv[8 * c + 6] - X[8 * c + 6], uv[8 * c + 7] - X[8 * c + 7]);
           *reinterpret_cast<uint4*>(vrow + (((4 * half + c) ^ (key & 7)) << 4)) = pk;
         }
       }
