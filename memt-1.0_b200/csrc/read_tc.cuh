@@ -6,7 +6,8 @@
 //   * the block's fp32 snapshot is read once, rounded to bf16 (read.py:64) and written as the
 //     MN-major B operand [128 key rows][2 x 64 values] in shared memory;
 //   * 64-token query tiles arrive by TMA (2-D tensor map over the [L, H*D] query rows, two
-//     64-key boxes with the 128-byte swizzle = the K-major A operand) into a four-deep ring;
+//     64-key boxes with the 128-byte swizzle = the K-major A operand) into a four-deep ring
+//     (two CTAs per SM);
 //   * a control warp issues the M = 64, N = 128, K = 128 MMA of each tile into one of two
 //     tensor-memory accumulators;
 //   * eight worker warps drain the other accumulator (token r in lane 32 (r / 16) + r % 16),
@@ -38,18 +39,19 @@ struct ReadTcCfg {
   static constexpr int kWorkerWarps = 8;
   static constexpr int kThreads = (kWorkerWarps + 1) * 32;
   static constexpr int kStages = 4;                       // query / output tile ring
+  static constexpr int kAcc = 2;                          // tensor-memory accumulators
   static constexpr uint32_t kBytesS = D * D * 2;          // 32 KB
   static constexpr uint32_t kBytesQ = kTok * D * 2;       // 16 KB per stage (query tile, then output tile)
   static constexpr uint32_t kBytesBox = kBytesQ / 2;      // one 64-wide panel of a tile
   static constexpr uint32_t kOffQ = kBytesS;
   static constexpr uint32_t kOffBar = kOffQ + kStages * kBytesQ;
   static constexpr size_t kSmem = kOffBar + 256 + 1024;
-  static constexpr uint32_t kTmemCols = 256;              // two M = 64 accumulators of 128 columns
+  static constexpr uint32_t kTmemCols = 256;              // kAcc M = 64 accumulators of 128 columns
 };
 
 __global__ void __launch_bounds__(ReadTcCfg::kThreads, 2) read_tc_kernel(const __grid_constant__ ReadTcParams P) {
   using Cfg = ReadTcCfg;
-  constexpr int D = Cfg::D, NS = Cfg::kStages;
+  constexpr int D = Cfg::D, NS = Cfg::kStages, NA = Cfg::kAcc;
   const ReadParams& p = P.p;
   extern __shared__ __align__(1024) unsigned char smem_read_tc[];
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_read_tc) + 1023) &
@@ -65,18 +67,19 @@ __global__ void __launch_bounds__(ReadTcCfg::kThreads, 2) read_tc_kernel(const _
   const bool tma_out = p.out_bf16 != 0;
   auto full_tile = [&](int i) { return first + (int64_t)(i + 1) * Cfg::kTok <= eos; };
 
-  // barriers: [0, 4) stage holds the query tile (TMA); 4/5 accumulator full (commit);
-  // 6/7 accumulator drained; 8 snapshot operand written; [9, 13) output tile written to the
-  // stage (6-12: one arrival per worker warp)
+  // barriers: [0, NS) stage holds the query tile (TMA); [QF, QF + NA) accumulator full
+  // (commit); [AE, AE + NA) accumulator drained; SR snapshot operand written; [OR, OR + NS)
+  // output tile written to the stage (AE.. and SR.. : one arrival per worker warp)
+  constexpr int AF = NS, AE = NS + NA, SR = NS + 2 * NA, OR = SR + 1, NBAR = OR + NS;
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + Cfg::kOffBar);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + Cfg::kOffBar + 128);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + Cfg::kOffBar + 8 * NBAR);
   auto B = [&](int i) { return smem_u32(&bar[i]); };
   unsigned char* sS = sm;
   const uint32_t sQ = smem_u32(sm + Cfg::kOffQ);
 
   if (tid == 0) {
-    for (int i = 0; i < 6; ++i) mbar_init(B(i), 1);
-    for (int i = 6; i < 13; ++i) mbar_init(B(i), Cfg::kWorkerWarps);
+    for (int i = 0; i < AE; ++i) mbar_init(B(i), 1);
+    for (int i = AE; i < NBAR; ++i) mbar_init(B(i), Cfg::kWorkerWarps);
     mbar_fence_init();
   }
   if (warp == Cfg::kWorkerWarps) tc::alloc(smem_u32(tmem_slot), Cfg::kTmemCols);
@@ -93,7 +96,8 @@ __global__ void __launch_bounds__(ReadTcCfg::kThreads, 2) read_tc_kernel(const _
   if (warp == Cfg::kWorkerWarps) {
     if (lane == 0) {
       // Stage s cycles: query tile i (TMA load) -> MMA(i) -> output tile i (workers) ->
-      // TMA store -> query tile i + 4. Up to three query tiles are in flight at any time.
+      // TMA store -> query tile i + NS, loaded R iterations after the store was issued so that
+      // the control thread never waits for a store's read of shared memory.
       auto load_q = [&](int i) {
         const int s = i % NS;
         const int y = static_cast<int>(first + (int64_t)i * Cfg::kTok);
@@ -101,36 +105,40 @@ __global__ void __launch_bounds__(ReadTcCfg::kThreads, 2) read_tc_kernel(const _
         tma_load_2d(sQ + s * Cfg::kBytesQ, &P.q_map, h * D, y, B(s));
         tma_load_2d(sQ + s * Cfg::kBytesQ + Cfg::kBytesBox, &P.q_map, h * D + 64, y, B(s));
       };
+      // one bulk group per tile (empty when the tile is stored row by row), so that the read
+      // of tile j's output is complete once at most R - 1 younger groups are pending
+      constexpr int R = 2;
       auto store_out = [&](int i) {  // output tile i has been written to its stage
         const int s = i % NS;
-        wait(9 + s, (i / NS) & 1);
+        wait(OR + s, (i / NS) & 1);
         if (tma_out && full_tile(i)) {
           fence_proxy_async_smem();
           const int y = static_cast<int>(first + (int64_t)i * Cfg::kTok);
           tma_store_2d(&P.o_map, h * D, y, sQ + s * Cfg::kBytesQ);
           tma_store_2d(&P.o_map, h * D + 64, y, sQ + s * Cfg::kBytesQ + Cfg::kBytesBox);
-          bulk_commit();
-          bulk_wait_read();
         }
+        bulk_commit();
       };
       for (int i = 0; i < NS && i < ntiles; ++i) load_q(i);
-      wait(8, 0);
+      wait(SR, 0);
       constexpr uint32_t kId = tc::idesc(tc::kBF16, 64, 128, false, true);  // q K-major, S MN-major
       const uint32_t ss = smem_u32(sS);
       for (int i = 0; i < ntiles; ++i) {
-        const int s = i % NS, a = i & 1;
+        const int s = i % NS, a = i % NA;
         wait(s, (i / NS) & 1);
-        if (i >= 2) wait(6 + a, ((i >> 1) - 1) & 1);
+        if (i >= NA) wait(AE + a, ((i / NA) - 1) & 1);
         tc::fence_after();
         const uint32_t q = sQ + s * Cfg::kBytesQ;
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks)
           tc::mma_bf16(tmem + 128 * a, tc::desc_kmajor(q + (ks >> 2) * Cfg::kBytesBox, (ks & 3) * 32),
                        tc::desc_mnmajor(ss, Cfg::kBytesS / 2, ks), kId, ks > 0);
-        tc::commit(B(4 + a));
-        if (i >= 1) {
-          store_out(i - 1);
-          if (i - 1 + NS < ntiles) load_q(i - 1 + NS);
+        tc::commit(B(AF + a));
+        if (i >= 1) store_out(i - 1);
+        // refill the stage of tile i - R, whose output store was committed R - 1 groups ago
+        if (i >= R && i - R + NS < ntiles) {
+          asm volatile("cp.async.bulk.wait_group.read %0;\n" ::"n"(R - 1) : "memory");
+          load_q(i - R + NS);
         }
       }
       store_out(ntiles - 1);
@@ -155,7 +163,7 @@ __global__ void __launch_bounds__(ReadTcCfg::kThreads, 2) read_tc_kernel(const _
       }
       tc::fence_smem_async();
       __syncwarp();
-      if (lane == 0) mbar_arrive(B(8));
+      if (lane == 0) mbar_arrive(B(SR));
     }
     // M = 64 accumulator: token r of the tile sits in lane 32 (r / 16) + r % 16, so warp w uses
     // lanes 0-15 for tokens 16 (w % 4) .. and columns 64 (w / 4) .. + 63
@@ -163,8 +171,8 @@ __global__ void __launch_bounds__(ReadTcCfg::kThreads, 2) read_tc_kernel(const _
     const int64_t qrow = (int64_t)p.H * D;
     const int r = 16 * quarter + lane;  // token row of the tile (lanes 0-15)
     for (int i = 0; i < ntiles; ++i) {
-      const int s = i % NS, a = i & 1;
-      wait(4 + a, (i >> 1) & 1);  // MMA(i) done: its query stage is free for the output
+      const int s = i % NS, a = i % NA;
+      wait(AF + a, (i / NA) & 1);  // MMA(i) done: its query stage is free for the output
       __syncwarp();
       tc::fence_after();
       float o[2][32];
@@ -172,7 +180,7 @@ __global__ void __launch_bounds__(ReadTcCfg::kThreads, 2) read_tc_kernel(const _
                  tc::lane_addr(tmem + 128 * a, 32 * quarter, 64 * half + 32), o[0], o[1]);
       tc::fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(B(6 + a));  // the accumulator may be overwritten
+      if (lane == 0) mbar_arrive(B(AE + a));  // the accumulator may be overwritten
       const int64_t tok = first + (int64_t)i * Cfg::kTok + r;
       if (lane < 16) {
         if (tma_out && full_tile(i)) {
@@ -208,7 +216,7 @@ __global__ void __launch_bounds__(ReadTcCfg::kThreads, 2) read_tc_kernel(const _
         }
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(B(9 + s));  // output tile i is in the stage (or stored)
+      if (lane == 0) mbar_arrive(B(OR + s));  // output tile i is in the stage (or stored)
     }
   }
   tc::fence_before();
