@@ -5,6 +5,7 @@
 // bf16 / tf32 cast points.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -204,7 +205,7 @@ struct ChunkDesc {
 // Workspace header (first 256 bytes of every update workspace).
 struct WsHeader {
   int32_t num_chunks;  // chunks written by the plan kernel
-  int32_t status;      // bit 0: clamped offsets, bit 1: chunk table overflow
+  int32_t status;      // bit 0: clamped offsets, bit 1: chunk table overflow, bit 2: copy wait timed out
   int32_t reserved[62];
 };
 
@@ -228,6 +229,7 @@ __host__ __device__ inline int64_t max_chunks_bound(int64_t L, int32_t N, int32_
 struct IntraParams {
   WsHeader* hdr;
   const ChunkDesc* table;
+  int64_t L;  // packed tokens
   int32_t H;
   const __nv_bfloat16* k;
   const __nv_bfloat16* v;
@@ -241,6 +243,9 @@ struct IntraParams {
   __nv_bfloat16* U;
   __nv_bfloat16* KG;
   float* Elast;
+  // TMA maps over k, v and write ([L][H*D] bf16, boxes of 64 channels x 64 tokens, 128-byte
+  // swizzle); encoded by the launcher for the kernels that load their tiles by TMA
+  CUtensorMap k_map, v_map, w_map;
 };
 
 struct ScanParams {

@@ -6,10 +6,19 @@
 namespace memt {
 
 template <int D, bool HEAD, bool ERASE>
-static int launch_intra_t(const IntraParams& p, int64_t max_chunks, cudaStream_t s) {
+static int launch_intra_t(const IntraParams& p0, int64_t max_chunks, cudaStream_t s) {
   using Cfg = IntraCfg<D, HEAD, ERASE>;
   auto kernel = intra_kernel<D, HEAD, ERASE>;
-  cudaError_t e = ensure_smem(kernel, Cfg::kSmem);
+  IntraParams p = p0;
+  cudaError_t e = cudaSuccess;
+  if constexpr (Cfg::kTma) {  // [L][H*D] bf16 rows, boxes of 64 channels x 64 tokens
+    const uint64_t row = static_cast<uint64_t>(p.H) * D, rows = static_cast<uint64_t>(p.L);
+    e = make_tmap_bf16_2d(&p.k_map, p.k, row, rows, row * 2, 64, kTile);
+    if (e == cudaSuccess) e = make_tmap_bf16_2d(&p.v_map, p.v, row, rows, row * 2, 64, kTile);
+    if (e == cudaSuccess && p.write != nullptr) e = make_tmap_bf16_2d(&p.w_map, p.write, row, rows, row * 2, 64, kTile);
+    if (e != cudaSuccess) return cuda_status(e);
+  }
+  e = ensure_smem(kernel, Cfg::kSmem);
   if (e != cudaSuccess) return cuda_status(e);
   int slots = 0;
   e = resident_slots(kernel, Cfg::kThreads, Cfg::kSmem, &slots);

@@ -41,6 +41,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "tma.h"
 
 namespace memt {
 
@@ -66,7 +67,10 @@ struct IntraCfg {
   static constexpr size_t offEi = offE + kBytesE;
   static constexpr size_t offA = offEi + kBytesE;
   static constexpr size_t offAi = offA + kBytesA;
-  static constexpr size_t kSmem = offAi + kBytesAi;
+  // per-head decay without erase, D <= 128: k, v and write tiles arrive by TMA (the tiles need
+  // the 1024-byte aligned base of the 128-byte swizzle: slack for aligning the dynamic base)
+  static constexpr bool kTma = HEAD && !ERASE && kPanels == 1;
+  static constexpr size_t kSmem = offAi + kBytesAi + (kTma ? 1024 : 0);
   static constexpr int kSmall = 9 * kTile + kThreads;  // static per-head factors + scan totals
 };
 
@@ -191,6 +195,8 @@ struct IntraKernel {
   static constexpr int P = Cfg::kPanel;
   static constexpr int NT = Cfg::kThreads;
   static constexpr bool kOverlap = Cfg::kPanels == 1;  // solve || staging (D <= 128)
+  static constexpr bool kTma = Cfg::kTma;
+  static constexpr uint32_t kTileBytes = static_cast<uint32_t>(Cfg::kTileB);
 
   __nv_bfloat16 *sK, *sB, *sV, *sW, *sO, *sAi;
   float *sE, *sEi, *sA;
@@ -202,6 +208,7 @@ struct IntraKernel {
   float* sSeg;
   float* sFac;  // [2][kSmall]: factors of the current / next unit (per-head decay)
   float* sScr;  // 4 fp32 16x16 scratch blocks of the blocked solve
+  uint32_t sMb;  // TMA path: mbarriers [k buffer 0, k buffer 1, v + write] (8 bytes each)
 
   int tid, lane, warp, len, tok0, h;
   int64_t row_stride;
@@ -261,8 +268,11 @@ struct IntraKernel {
 #pragma unroll
     for (int i = tid - T0; i < kChunks; i += NTH) {
       const int row = i / (P / 8), col = (i % (P / 8)) * 8;
-      if (row >= ln) continue;
       uint4* ptr = reinterpret_cast<uint4*>(kbuf + pswz(row, col));
+      if (row >= ln) {
+        if constexpr (kTma) *ptr = make_uint4(0, 0, 0, 0);
+        continue;
+      }
       uint4 kv = *ptr;
       float sb[8];
       if (p.beta_layout == 1) {
@@ -700,16 +710,31 @@ struct IntraKernel {
     }
   }
 
-  // u operand in place: sV = bf16(v * w)   (wy_fast.py:98-100); threads [T0, T0 + NTH)
+  // zero rows [len, 64) of a [64][P] tile; threads [T0, T0 + NTH)
+  template <int T0, int NTH>
+  __device__ void zero_rows(__nv_bfloat16* t) {
+    constexpr int kChunks = kTile * P / 8;
+    for (int i = tid - T0 + len * (P / 8); i < kChunks; i += NTH)
+      *reinterpret_cast<uint4*>(t + pswz(i / (P / 8), (i % (P / 8)) * 8)) = make_uint4(0, 0, 0, 0);
+  }
+
+  // u operand in place: sV = bf16(v * w)   (wy_fast.py:98-100); threads [T0, T0 + NTH); in the
+  // TMA path rows past the chunk become zero
   template <int T0, int NTH>
   __device__ void stage_u(const IntraParams& p) {
-    if (p.write == nullptr) return;
     constexpr int kChunks = kTile * P / 8;
     static_assert(kChunks % NTH == 0, "chunks per thread");
+    if (p.write == nullptr) {
+      if constexpr (kTma) {  // rows past the chunk hold the next sample's tokens: zero them
+        if (len < kTile) zero_rows<T0, NTH>(sV);
+      }
+      return;
+    }
 #pragma unroll
     for (int i = tid - T0; i < kChunks; i += NTH) {
       const int row = i / (P / 8), col = (i % (P / 8)) * 8;
-      uint4 vv = *reinterpret_cast<const uint4*>(sV + pswz(row, col));
+      uint4 vv = make_uint4(0, 0, 0, 0);
+      if (!kTma || row < len) vv = *reinterpret_cast<const uint4*>(sV + pswz(row, col));
       const uint4 ww = *reinterpret_cast<const uint4*>(sW + pswz(row, col));
       uint32_t* vw = reinterpret_cast<uint32_t*>(&vv);
       const uint32_t* wg = reinterpret_cast<const uint32_t*>(&ww);
@@ -833,10 +858,7 @@ struct IntraKernel {
     int64_t unit = blockIdx.x;
     if (unit >= units) return;
     row_stride = (int64_t)p.H * D;
-    // next unit's k streams into the spare tile during the solve (per-head decay, no erase)
-    constexpr bool kPrefetch = kOverlap && HEAD && !ERASE;
     __nv_bfloat16* kcur = sK;
-    __nv_bfloat16* kspare = sO;
 
     auto load_decay = [&](int c0) {
       const float* base = p.g + (int64_t)tok0 * row_stride + (int64_t)h * D + c0;
@@ -941,9 +963,7 @@ struct IntraKernel {
             const int c2 = static_cast<int>(next / p.H), h2 = static_cast<int>(next % p.H);
             const ChunkDesc d2 = p.table[c2];
             load_scalars(p, d2.tok0, d2.len, h2, 128, ng, nb);
-            if constexpr (kPrefetch) load_tile_for<128, 128>(kspare, p.k, 0, d2.tok0, d2.len, h2);
           }
-          if constexpr (kPrefetch) cp_async_commit();
           stage_u<128, 128>(p);
           if (has_next) store_scalars(sPre + (pre ^ 1) * 2 * kTile, 128, ng, nb);
           named_sync(2, 128);
@@ -1009,24 +1029,150 @@ struct IntraKernel {
       __syncthreads();  // the last tile stores read shared memory the next unit overwrites
       if constexpr (!kOverlap) fetch_scalars(p, tok0, len, h, sPre + (pre ^ 1) * 2 * kTile, 0);
       pre ^= 1;
-      if constexpr (kPrefetch) {
-        __nv_bfloat16* tmp = kcur;
-        kcur = kspare;
-        kspare = tmp;
-      } else {
-        load_key_panel(0);
-        cp_async_commit();
-      }
+      load_key_panel(0);
+      cp_async_commit();
     }
+  }
+
+  // ---- the persistent loop of the TMA configuration (per-head decay, no erase, D <= 128) ----
+  // Thread 0 issues every tile load: at the top of a unit the unit's v and write tiles and the
+  // next unit's k tile (into the spare k buffer), each completing on an mbarrier that the
+  // consuming threads wait on. The chunk table entry of the unit after next and the next unit's
+  // per-token scalars are loaded into registers at the top as well and consumed one phase or
+  // one unit later, so no global-load latency sits on the unit's chain.
+  __device__ void run_tma(const IntraParams& p) {
+    griddep_wait();               // the chunk table and every input are complete
+    griddep_launch_dependents();  // the scan may set up while the last units run
+    const int64_t units = (int64_t)p.hdr->num_chunks * p.H;
+    int64_t unit = blockIdx.x;
+    if (unit >= units) return;
+    row_stride = (int64_t)p.H * D;
+    auto mb = [&](int i) { return sMb + 8u * i; };
+    auto tma_tile = [&](__nv_bfloat16* dst, const CUtensorMap* map, int tk0, int hd, uint32_t bar) {
+#pragma unroll
+      for (int b = 0; b < P / 64; ++b) tma_load_2d(smem_u32(dst) + b * 8192u, map, hd * D + 64 * b, tk0, bar);
+    };
+    if (tid == 0) {
+      mbar_init(mb(0), 1);
+      mbar_init(mb(1), 1);
+      mbar_init(mb(2), 1);
+      mbar_fence_init();
+    }
+    __syncthreads();
+    __nv_bfloat16* kcur = sK;
+    __nv_bfloat16* kspare = sO;
+    int kb = 0;         // mbarrier of kcur
+    uint32_t kph = 0;   // bit b: phase parity of k buffer b's next completion
+    uint32_t vph = 0;   // phase parity of the v + write barrier
+    bool ok = true;     // every copy wait of this thread completed
+    set_unit(p, unit);
+    ChunkDesc nd{};     // table entry of the next unit
+    if (unit + gridDim.x < units) nd = p.table[(unit + gridDim.x) / p.H];
+    if (tid == 0) {
+      mbar_expect_tx(mb(0), kTileBytes);
+      tma_tile(kcur, &p.k_map, tok0, h, mb(0));
+    }
+    pre = 0;
+    fetch_scalars(p, tok0, len, h, sPre, 0);
+    bool first = true;
+    for (;;) {
+      const int64_t next = unit + gridDim.x;
+      const bool has_next = next < units;
+      const int hn = static_cast<int>(next % p.H);
+      ChunkDesc nn{};  // the unit after next: needed one unit from now
+      if (next + gridDim.x < units) nn = p.table[(next + gridDim.x) / p.H];
+      __nv_bfloat16* gW = p.W + unit * kTile * D;
+      __nv_bfloat16* gU = p.U + unit * kTile * D;
+      __nv_bfloat16* gKG = p.KG + unit * kTile * D;
+      float* gEl = p.Elast + unit * D;
+
+      if (tid == 0) {
+        fence_proxy_async_smem();  // the previous unit's accesses to sV, sW and kspare come first
+        mbar_expect_tx(mb(2), p.write != nullptr ? 2 * kTileBytes : kTileBytes);
+        tma_tile(sV, &p.v_map, tok0, h, mb(2));
+        if (p.write != nullptr) tma_tile(sW, &p.w_map, tok0, h, mb(2));
+        if (has_next) {
+          mbar_expect_tx(mb(kb ^ 1), kTileBytes);
+          tma_tile(kspare, &p.k_map, nd.tok0, hn, mb(kb ^ 1));
+        }
+      }
+      float ng = 0.f, nb = 0.f;  // next unit's scalars (threads 128..191), stored in the staging
+      if (has_next) load_scalars(p, nd.tok0, nd.len, hn, 128, ng, nb);
+      use_factors(pre);
+      if (first) {
+        __syncthreads();  // the unit's scalars are visible
+        if (warp == 0) head_factors(sPre, sFac, len);
+        first = false;
+      }
+
+      float acc[3][4];
+#pragma unroll
+      for (int i = 0; i < 3; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+      // ---- key-key scores: k landed; fold sqrt(beta) (zeroing rows past the chunk) ----
+      ok &= mbar_wait(mb(kb), (kph >> kb) & 1u);
+      kph ^= 1u << kb;
+      if (p.beta_layout != 0)
+        fold_beta(p, kcur, 0);
+      else if (len < kTile)
+        zero_rows<0, NT>(kcur);
+      __syncthreads();
+      scores_panel(acc, kcur);
+      store_scores(acc);
+      __syncthreads();
+
+      // warps 0-3: blocked solve; warps 4-7: u operand (v * w in place), the next unit's
+      // scalars, then w operand (in place of k), kg and the next unit's decay factors
+      if (warp < 4) {
+        solve();
+      } else {
+        ok &= mbar_wait(mb(2), vph);
+        stage_u<128, 128>(p);
+        if (has_next) store_scalars(sPre + (pre ^ 1) * 2 * kTile, 128, ng, nb);
+        named_sync(2, 128);
+        stage_w_kg<128, 128>(kcur, gKG, gEl, 0);
+        if (has_next && warp == 7)
+          head_factors(sPre + (pre ^ 1) * 2 * kTile, sFac + (pre ^ 1) * Cfg::kSmall, nd.len);
+      }
+      vph ^= 1u;
+      __syncthreads();
+      wy_product(kcur, sW);  // w = A^-1 . w operand; the w-gate tile is free
+      fence_proxy_async_smem();
+      __syncthreads();
+      store_tile_async(gW, 0, sW);
+      wy_product(sV, kcur);  // u = A^-1 . bf16(v*w); the w operand is consumed
+      fence_proxy_async_smem();
+      __syncthreads();
+      store_tile_async(gU, 0, kcur);
+      if (tid == 0) bulk_wait_read();  // before the next unit reloads sV, sW and kcur
+      if (!has_next) {
+        if (tid == 0) bulk_wait_all();
+        break;
+      }
+      unit = next;
+      h = hn;
+      tok0 = nd.tok0;
+      len = nd.len;
+      nd = nn;
+      __syncthreads();  // the last tile stores read shared memory the next unit overwrites
+      pre ^= 1;
+      __nv_bfloat16* tmp = kcur;
+      kcur = kspare;
+      kspare = tmp;
+      kb ^= 1;
+    }
+    if (!ok) atomicOr(&p.hdr->status, 4);  // a tile never arrived: results are not valid
   }
 };
 
 template <int D, bool HEAD, bool ERASE>
-__global__ void __launch_bounds__(256, 2) intra_kernel(IntraParams p) {
-  extern __shared__ __align__(128) unsigned char smem_intra[];
+__global__ void __launch_bounds__(256, 2) intra_kernel(const __grid_constant__ IntraParams p) {
+  extern __shared__ __align__(1024) unsigned char smem_intra[];
   using Cfg = IntraCfg<D, HEAD, ERASE>;
   IntraKernel<D, HEAD, ERASE> k;
   unsigned char* base = smem_intra;
+  if constexpr (Cfg::kTma) base += (1024u - (smem_u32(smem_intra) & 1023u)) & 1023u;
   k.sK = reinterpret_cast<__nv_bfloat16*>(base + Cfg::offK);
   k.sB = reinterpret_cast<__nv_bfloat16*>(base + Cfg::offB);
   k.sV = reinterpret_cast<__nv_bfloat16*>(base + Cfg::offV);
@@ -1047,7 +1193,13 @@ __global__ void __launch_bounds__(256, 2) intra_kernel(IntraParams p) {
   k.lane = threadIdx.x & 31;
   k.warp = threadIdx.x >> 5;
   k.fast = true;
-  k.run(p);
+  if constexpr (Cfg::kTma) {
+    __shared__ __align__(8) uint64_t s_mbar[3];
+    k.sMb = smem_u32(s_mbar);
+    k.run_tma(p);
+  } else {
+    k.run(p);
+  }
 }
 
 }  // namespace memt

@@ -95,6 +95,7 @@ int update_bf16(const memt_gdn2_update_args* a, void* ws, cudaStream_t s) {
   IntraParams ip{};
   ip.hdr = hdr;
   ip.table = table;
+  ip.L = a->total_tokens;
   ip.H = a->num_heads;
   ip.k = static_cast<const __nv_bfloat16*>(a->k);
   ip.v = static_cast<const __nv_bfloat16*>(a->v);
