@@ -237,24 +237,28 @@ struct IntraKernel {
   // bf16(sqrt(beta)) of a per-head beta. Threads [t0, t0 + 64); issued one unit ahead so the
   // global-load latency hides behind the previous unit's solve.
   __device__ void fetch_scalars(const IntraParams& p, int tk0, int ln, int hd, float* buf, int t0) {
-    float gv, bv;
+    float gv;
+    uint32_t bv;
     load_scalars(p, tk0, ln, hd, t0, gv, bv);
     store_scalars(buf, t0, gv, bv);
   }
   // the two halves of fetch_scalars: issue the loads early, store once other work is done
+  // (beta stays as raw bf16 bits until the store: nothing waits on the loads before then)
   __device__ __forceinline__ void load_scalars(const IntraParams& p, int tk0, int ln, int hd, int t0, float& gv,
-                                               float& bv) const {
+                                               uint32_t& bv) const {
     const int i = tid - t0;
     gv = 0.f;
-    bv = 0.f;
+    bv = 0u;
     if (i >= 0 && i < ln && i < kTile) {
       if constexpr (HEAD) gv = p.g[(int64_t)(tk0 + i) * p.H + hd];
-      if (p.beta_layout == 1) bv = __bfloat162float(p.beta[(int64_t)(tk0 + i) * p.H + hd]);
+      if (p.beta_layout == 1)
+        bv = *reinterpret_cast<const unsigned short*>(p.beta + (int64_t)(tk0 + i) * p.H + hd);
     }
   }
-  __device__ __forceinline__ void store_scalars(float* buf, int t0, float gv, float bv) const {
+  __device__ __forceinline__ void store_scalars(float* buf, int t0, float gv, uint32_t bits) const {
     const int i = tid - t0;
     if (i < 0 || i >= kTile) return;
+    const float bv = __uint_as_float(bits << 16);
     buf[i] = gv;
     buf[kTile + i] = bv > 0.f ? bf16_round(sqrtf(bv)) : 0.f;
   }
@@ -734,12 +738,14 @@ struct IntraKernel {
     for (int i = tid - T0; i < kChunks; i += NTH) {
       const int row = i / (P / 8), col = (i % (P / 8)) * 8;
       uint4 vv = make_uint4(0, 0, 0, 0);
-      if (!kTma || row < len) vv = *reinterpret_cast<const uint4*>(sV + pswz(row, col));
-      const uint4 ww = *reinterpret_cast<const uint4*>(sW + pswz(row, col));
-      uint32_t* vw = reinterpret_cast<uint32_t*>(&vv);
-      const uint32_t* wg = reinterpret_cast<const uint32_t*>(&ww);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) vw[e] = pack_bf16x2(bf_lo(vw[e]) * bf_lo(wg[e]), bf_hi(vw[e]) * bf_hi(wg[e]));
+      if (!kTma || row < len) {
+        vv = *reinterpret_cast<const uint4*>(sV + pswz(row, col));
+        const uint4 ww = *reinterpret_cast<const uint4*>(sW + pswz(row, col));
+        vv.x = mul_bf16x2(vv.x, ww.x);
+        vv.y = mul_bf16x2(vv.y, ww.y);
+        vv.z = mul_bf16x2(vv.z, ww.z);
+        vv.w = mul_bf16x2(vv.w, ww.w);
+      }
       *reinterpret_cast<uint4*>(sV + pswz(row, col)) = vv;
     }
   }
@@ -827,6 +833,62 @@ struct IntraKernel {
         *reinterpret_cast<uint32_t*>(dst + pswz(i0, col)) = pack_bf16x2(acc[nt][0], acc[nt][1]);
         *reinterpret_cast<uint32_t*>(dst + pswz(i0 + 8, col)) = pack_bf16x2(acc[nt][2], acc[nt][3]);
       }
+    }
+  }
+
+  // Both WY products in one pass (TMA loop): w = A^-1 . (w operand in kt) -> dw and
+  // u = A^-1 . (u operand in sV) -> du, all [64][P] pswz tiles; the A^-1 fragment of a k-step
+  // feeds both. Row block r needs k-steps 0..r: warps 0-3 take row blocks 3 and 0, warps 4-7
+  // blocks 2 and 1, each in column quarter warp % 4 -- the same work on every warp. The sources
+  // are only read and the destinations are other tiles: no barrier between reads and writes.
+  template <int R>
+  __device__ __forceinline__ void wy_block(const __nv_bfloat16* kt, __nv_bfloat16* dw, __nv_bfloat16* du) {
+    constexpr int CW = P / 4;    // columns of a quarter
+    constexpr int NTW = CW / 8;  // 8-column tiles of a quarter
+    const int n_base = (warp & 3) * CW;
+    float aw[NTW][4], au[NTW][4];
+#pragma unroll
+    for (int i = 0; i < NTW; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) aw[i][j] = au[i][j] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks <= R; ++ks) {
+      uint32_t a[4], bw[NTW / 2][4], bu[NTW / 2][4];
+      ldsm_x4(a, smem_u32(sAi + (16 * R + (lane & 15)) * Cfg::kLdAi + 16 * ks + 8 * (lane >> 4)));
+#pragma unroll
+      for (int np = 0; np < NTW; np += 2) {
+        const int off = pswz(16 * ks + (lane & 15), n_base + 8 * np + 8 * (lane >> 4));
+        ldsm_x4_t(bw[np / 2], smem_u32(kt + off));
+        ldsm_x4_t(bu[np / 2], smem_u32(sV + off));
+      }
+#pragma unroll
+      for (int np = 0; np < NTW; np += 2) {
+        const uint32_t w0[2] = {bw[np / 2][0], bw[np / 2][1]}, w1[2] = {bw[np / 2][2], bw[np / 2][3]};
+        const uint32_t u0[2] = {bu[np / 2][0], bu[np / 2][1]}, u1[2] = {bu[np / 2][2], bu[np / 2][3]};
+        mma_bf16_16816(aw[np], a, w0);
+        mma_bf16_16816(aw[np + 1], a, w1);
+        mma_bf16_16816(au[np], a, u0);
+        mma_bf16_16816(au[np + 1], a, u1);
+      }
+    }
+    const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+    for (int nt = 0; nt < NTW; ++nt) {
+      const int col = n_base + 8 * nt + 2 * t;
+      const int i0 = 16 * R + g;
+      *reinterpret_cast<uint32_t*>(dw + pswz(i0, col)) = pack_bf16x2(aw[nt][0], aw[nt][1]);
+      *reinterpret_cast<uint32_t*>(dw + pswz(i0 + 8, col)) = pack_bf16x2(aw[nt][2], aw[nt][3]);
+      *reinterpret_cast<uint32_t*>(du + pswz(i0, col)) = pack_bf16x2(au[nt][0], au[nt][1]);
+      *reinterpret_cast<uint32_t*>(du + pswz(i0 + 8, col)) = pack_bf16x2(au[nt][2], au[nt][3]);
+    }
+  }
+  __device__ void wy_products(const __nv_bfloat16* kt, __nv_bfloat16* dw, __nv_bfloat16* du) {
+    if (warp < 4) {
+      wy_block<3>(kt, dw, du);
+      wy_block<0>(kt, dw, du);
+    } else {
+      wy_block<2>(kt, dw, du);
+      wy_block<1>(kt, dw, du);
     }
   }
 
@@ -958,7 +1020,8 @@ struct IntraKernel {
         } else {
           cp_async_wait<0>();  // this thread's copies of v and w
           named_sync(2, 128);  // ... and every staging thread's
-          float ng = 0.f, nb = 0.f;  // next unit's scalars, loaded now, stored after stage_u
+          float ng = 0.f;  // next unit's scalars, loaded now, stored after stage_u
+          uint32_t nb = 0u;
           if (has_next) {
             const int c2 = static_cast<int>(next / p.H), h2 = static_cast<int>(next % p.H);
             const ChunkDesc d2 = p.table[c2];
@@ -1035,11 +1098,12 @@ struct IntraKernel {
   }
 
   // ---- the persistent loop of the TMA configuration (per-head decay, no erase, D <= 128) ----
-  // Thread 0 issues every tile load: at the top of a unit the unit's v and write tiles and the
+  // Thread 0 issues every tile copy: at the top of a unit the unit's v and write tiles and the
   // next unit's k tile (into the spare k buffer), each completing on an mbarrier that the
-  // consuming threads wait on. The chunk table entry of the unit after next and the next unit's
-  // per-token scalars are loaded into registers at the top as well and consumed one phase or
-  // one unit later, so no global-load latency sits on the unit's chain.
+  // consuming threads wait on; at the end the w and u tiles as bulk stores that are waited for
+  // only where their buffers are loaded again. The chunk table entry of the unit after next and
+  // the next unit's per-token scalars are loaded into registers at the top as well and consumed
+  // one phase or one unit later, so no global-load latency sits on the unit's chain.
   __device__ void run_tma(const IntraParams& p) {
     griddep_wait();               // the chunk table and every input are complete
     griddep_launch_dependents();  // the scan may set up while the last units run
@@ -1090,13 +1154,17 @@ struct IntraKernel {
         fence_proxy_async_smem();  // the previous unit's accesses to sV, sW and kspare come first
         mbar_expect_tx(mb(2), p.write != nullptr ? 2 * kTileBytes : kTileBytes);
         tma_tile(sV, &p.v_map, tok0, h, mb(2));
-        if (p.write != nullptr) tma_tile(sW, &p.w_map, tok0, h, mb(2));
         if (has_next) {
           mbar_expect_tx(mb(kb ^ 1), kTileBytes);
           tma_tile(kspare, &p.k_map, nd.tok0, hn, mb(kb ^ 1));
         }
+        if (p.write != nullptr) {
+          bulk_wait_read_but1();  // the previous unit's w has left the write-gate tile
+          tma_tile(sW, &p.w_map, tok0, h, mb(2));
+        }
       }
-      float ng = 0.f, nb = 0.f;  // next unit's scalars (threads 128..191), stored in the staging
+      float ng = 0.f;  // next unit's scalars (threads 128..191), stored in the staging
+      uint32_t nb = 0u;
       if (has_next) load_scalars(p, nd.tok0, nd.len, hn, 128, ng, nb);
       use_factors(pre);
       if (first) {
@@ -1117,6 +1185,7 @@ struct IntraKernel {
         fold_beta(p, kcur, 0);
       else if (len < kTile)
         zero_rows<0, NT>(kcur);
+      if (tid == 0) bulk_wait_read();  // the previous unit's u has left the score buffer
       __syncthreads();
       scores_panel(acc, kcur);
       store_scores(acc);
@@ -1137,15 +1206,18 @@ struct IntraKernel {
       }
       vph ^= 1u;
       __syncthreads();
-      wy_product(kcur, sW);  // w = A^-1 . w operand; the w-gate tile is free
+      // w into the write-gate tile (consumed by the u operand), u into the score buffer (free
+      // once the solve is done); both leave by bulk copies that nothing waits for until their
+      // buffers are loaded again (the write gate at the next unit's top, the scores after its fold)
+      wy_products(kcur, sW, reinterpret_cast<__nv_bfloat16*>(sA));
       fence_proxy_async_smem();
-      __syncthreads();
-      store_tile_async(gW, 0, sW);
-      wy_product(sV, kcur);  // u = A^-1 . bf16(v*w); the w operand is consumed
-      fence_proxy_async_smem();
-      __syncthreads();
-      store_tile_async(gU, 0, kcur);
-      if (tid == 0) bulk_wait_read();  // before the next unit reloads sV, sW and kcur
+      __syncthreads();  // every product written, every source tile read
+      if (tid == 0) {
+        bulk_s2g(gW, smem_u32(sW), kTileBytes);
+        bulk_commit();
+        bulk_s2g(gU, smem_u32(sA), kTileBytes);
+        bulk_commit();
+      }
       if (!has_next) {
         if (tid == 0) bulk_wait_all();
         break;
@@ -1155,7 +1227,6 @@ struct IntraKernel {
       tok0 = nd.tok0;
       len = nd.len;
       nd = nn;
-      __syncthreads();  // the last tile stores read shared memory the next unit overwrites
       pre ^= 1;
       __nv_bfloat16* tmp = kcur;
       kcur = kspare;
