@@ -1107,10 +1107,22 @@ struct IntraKernel {
   __device__ void run_tma(const IntraParams& p) {
     griddep_wait();               // the chunk table and every input are complete
     griddep_launch_dependents();  // the scan may set up while the last units run
-    const int64_t units = (int64_t)p.hdr->num_chunks * p.H;
-    int64_t unit = blockIdx.x;
-    if (unit >= units) return;
-    row_stride = (int64_t)p.H * D;
+    // units advance by the grid size as (chunk, head) pairs, without divisions
+    const int nch = p.hdr->num_chunks;
+    const int H = p.H;
+    int c = static_cast<int>(blockIdx.x / H);
+    h = static_cast<int>(blockIdx.x % H);
+    if (c >= nch) return;
+    const int dc = static_cast<int>(gridDim.x / H), dh = static_cast<int>(gridDim.x % H);
+    auto advance = [&](int& cc, int& hh) {
+      hh += dh;
+      cc += dc;
+      if (hh >= H) {
+        hh -= H;
+        cc += 1;
+      }
+    };
+    row_stride = (int64_t)H * D;
     auto mb = [&](int i) { return sMb + 8u * i; };
     auto tma_tile = [&](__nv_bfloat16* dst, const CUtensorMap* map, int tk0, int hd, uint32_t bar) {
 #pragma unroll
@@ -1129,9 +1141,15 @@ struct IntraKernel {
     uint32_t kph = 0;   // bit b: phase parity of k buffer b's next completion
     uint32_t vph = 0;   // phase parity of the v + write barrier
     bool ok = true;     // every copy wait of this thread completed
-    set_unit(p, unit);
-    ChunkDesc nd{};     // table entry of the next unit
-    if (unit + gridDim.x < units) nd = p.table[(unit + gridDim.x) / p.H];
+    {
+      const ChunkDesc d0 = p.table[c];
+      tok0 = d0.tok0;
+      len = d0.len;
+    }
+    int nc = c, nh = h;  // the next unit
+    advance(nc, nh);
+    ChunkDesc nd{};      // table entry of the next unit
+    if (nc < nch) nd = p.table[nc];
     if (tid == 0) {
       mbar_expect_tx(mb(0), kTileBytes);
       tma_tile(kcur, &p.k_map, tok0, h, mb(0));
@@ -1140,11 +1158,13 @@ struct IntraKernel {
     fetch_scalars(p, tok0, len, h, sPre, 0);
     bool first = true;
     for (;;) {
-      const int64_t next = unit + gridDim.x;
-      const bool has_next = next < units;
-      const int hn = static_cast<int>(next % p.H);
-      ChunkDesc nn{};  // the unit after next: needed one unit from now
-      if (next + gridDim.x < units) nn = p.table[(next + gridDim.x) / p.H];
+      const bool has_next = nc < nch;
+      const int hn = nh;
+      int n2c = nc, n2h = nh;  // the unit after next: its table entry is needed one unit from now
+      advance(n2c, n2h);
+      ChunkDesc nn{};
+      if (n2c < nch) nn = p.table[n2c];
+      const int64_t unit = (int64_t)c * H + h;
       __nv_bfloat16* gW = p.W + unit * kTile * D;
       __nv_bfloat16* gU = p.U + unit * kTile * D;
       __nv_bfloat16* gKG = p.KG + unit * kTile * D;
@@ -1222,10 +1242,12 @@ struct IntraKernel {
         if (tid == 0) bulk_wait_all();
         break;
       }
-      unit = next;
-      h = hn;
+      c = nc;
+      h = nh;
       tok0 = nd.tok0;
       len = nd.len;
+      nc = n2c;
+      nh = n2h;
       nd = nn;
       pre ^= 1;
       __nv_bfloat16* tmp = kcur;
