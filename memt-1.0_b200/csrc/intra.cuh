@@ -233,6 +233,26 @@ struct IntraKernel {
     }
   }
 
+  // Chunk walk of a [64][P] pswz tile by threads [T0, T0 + NTH): thread t = tid - T0 visits the
+  // 16-byte chunks t, t + NTH, ..., i.e. chunk column t % (P/8) in rows t / (P/8) + j * kRows.
+  // kRows is a multiple of 8, so the swizzle key (row & 7), and with it the chunk's position in
+  // its row, is the same on every visit: visit j lies j * kStride bytes after the first.
+  template <int NTH>
+  struct Walk {
+    static constexpr int kRows = NTH / (P / 8);
+    static constexpr int kSteps = kTile / kRows;
+    static constexpr uint32_t kStride = kRows * 128u;
+    static_assert(kRows % 8 == 0 && kTile % kRows == 0, "swizzle key fixed along the walk");
+  };
+  // first visit of thread tid: its row and column, and the chunk's byte offset in the tile
+  template <int T0>
+  __device__ __forceinline__ uint32_t walk_start(int& row0, int& col) const {
+    const int t = tid - T0;
+    row0 = t / (P / 8);
+    col = (t % (P / 8)) * 8;
+    return 2u * static_cast<uint32_t>(pswz(row0, col));
+  }
+
   // Per-token scalars of a unit into buf: [0, 64) the per-head log-decay, [64, 128)
   // bf16(sqrt(beta)) of a per-head beta. Threads [t0, t0 + 64); issued one unit ahead so the
   // global-load latency hides behind the previous unit's solve.
@@ -267,12 +287,14 @@ struct IntraKernel {
   // for the unit (tk0, ln, hd) whose per-head scalars are in sPre half `ph`; threads [T0, T0 + NTH)
   template <int T0, int NTH>
   __device__ void fold_beta_for(const IntraParams& p, __nv_bfloat16* kbuf, int c0, int tk0, int ln, int hd, int ph) {
-    constexpr int kChunks = kTile * P / 8;
-    static_assert(kChunks % NTH == 0, "chunks per thread");
+    using Wk = Walk<NTH>;
+    int row0, col;
+    unsigned char* kb = reinterpret_cast<unsigned char*>(kbuf) + walk_start<T0>(row0, col);
+    const __nv_bfloat16* bsrc = p.beta + (int64_t)(tk0 + row0) * row_stride + (int64_t)hd * D + c0 + col;
 #pragma unroll
-    for (int i = tid - T0; i < kChunks; i += NTH) {
-      const int row = i / (P / 8), col = (i % (P / 8)) * 8;
-      uint4* ptr = reinterpret_cast<uint4*>(kbuf + pswz(row, col));
+    for (int j = 0; j < Wk::kSteps; ++j) {
+      const int row = row0 + j * Wk::kRows;
+      uint4* ptr = reinterpret_cast<uint4*>(kb + j * Wk::kStride);
       if (row >= ln) {
         if constexpr (kTma) *ptr = make_uint4(0, 0, 0, 0);
         continue;
@@ -284,8 +306,7 @@ struct IntraKernel {
 #pragma unroll
         for (int e = 0; e < 8; ++e) sb[e] = s;
       } else {
-        const uint4 be = *reinterpret_cast<const uint4*>(p.beta + (int64_t)(tk0 + row) * row_stride +
-                                                         (int64_t)hd * D + c0 + col);
+        const uint4 be = *reinterpret_cast<const uint4*>(bsrc + (int64_t)j * Wk::kRows * row_stride);
         const uint32_t* bw = reinterpret_cast<const uint32_t*>(&be);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -422,6 +443,44 @@ struct IntraKernel {
     int r, nts[3];
     score_pieces(warp, r, nts);
     if (16 * r >= len) return;  // whole row block beyond the chunk (chunk_intra.py:242-278)
+    if constexpr (ERASE) {
+      scores_head_erase(acc, sK, r, nts);
+    } else {
+      if (nts[2] >= 0)
+        scores_head_np<3>(acc, sK, r, nts);
+      else
+        scores_head_np<2>(acc, sK, r, nts);
+    }
+  }
+  // Exact bf16 products of NP pieces. Every ldmatrix row of a k-step starts at a multiple of 8
+  // rows, so its swizzle key is lane & 7 for the whole loop: a fragment address is a per-thread
+  // base plus (k-step chunk XOR a per-thread key), the k-step parts being constants.
+  template <int NP>
+  __device__ __forceinline__ void scores_head_np(float (&acc)[3][4], const __nv_bfloat16* sK, int r,
+                                                 const int (&nts)[3]) {
+    const uint32_t key = lane & 7;
+    const uint32_t base = smem_u32(sK);
+    const uint32_t a_row = base + (16 * r + (lane & 15)) * 128;      // A: rows 16r + (lane & 15)
+    const uint32_t a_x = ((uint32_t(lane >> 4)) ^ key) << 4;         //    k chunk 2kk + (lane >> 4)
+    const uint32_t b_x = ((uint32_t(lane >> 3) & 1u) ^ key) << 4;    // B: k chunk 2kk + ((lane >> 3) & 1)
+    uint32_t b_row[NP];
+#pragma unroll
+    for (int s = 0; s < NP; ++s) b_row[s] = base + (8 * nts[s] + (lane & 7)) * 128;
+#pragma unroll
+    for (int kk = 0; kk < P / 16; ++kk) {
+      const uint32_t pan = (kk >> 2) * 8192u;           // 64-column panel of the k-step
+      const uint32_t cx = uint32_t((2 * kk) & 7) << 4;  // its first 16-byte chunk in the panel
+      uint32_t a[4], bq[NP][2];
+      ldsm_x4(a, a_row + pan + (cx ^ a_x));
+#pragma unroll
+      for (int s = 0; s < NP; ++s) ldsm_x2(bq[s], b_row[s] + pan + (cx ^ b_x));
+#pragma unroll
+      for (int s = 0; s < NP; ++s) mma_bf16_16816(acc[s], a, bq[s]);
+    }
+  }
+  // with an erase factor: the fp32 product k'*b split into bf16 hi + lo parts
+  __device__ __forceinline__ void scores_head_erase(float (&acc)[3][4], const __nv_bfloat16* sK, int r,
+                                                    const int (&nts)[3]) {
     const int n_ref = 16 * r;
 #pragma unroll 4
     for (int kk = 0; kk < P / 16; ++kk) {
@@ -431,26 +490,20 @@ struct IntraKernel {
       for (int s = 0; s < 3; ++s)
         if (nts[s] >= 0)
           ldsm_x2(bq[s], smem_u32(sK + pswz(8 * nts[s] + (lane & 7), 16 * kk + 8 * ((lane >> 3) & 1))));
-      if constexpr (ERASE) {
-        uint32_t eb[4], hi[4], lo[4];
-        ldsm_x4(eb, smem_u32(sB + pswz(n_ref + (lane & 15), 16 * kk + 8 * (lane >> 4))));
+      uint32_t eb[4], hi[4], lo[4];
+      ldsm_x4(eb, smem_u32(sB + pswz(n_ref + (lane & 15), 16 * kk + 8 * (lane >> 4))));
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float p0 = bf_lo(a[q]) * bf_lo(eb[q]), p1 = bf_hi(a[q]) * bf_hi(eb[q]);
-          hi[q] = pack_bf16x2(p0, p1);
-          lo[q] = pack_bf16x2(p0 - bf_lo(hi[q]), p1 - bf_hi(hi[q]));
-        }
-#pragma unroll
-        for (int s = 0; s < 3; ++s)
-          if (nts[s] >= 0) {
-            mma_bf16_16816(acc[s], hi, bq[s]);
-            mma_bf16_16816(acc[s], lo, bq[s]);
-          }
-      } else {
-#pragma unroll
-        for (int s = 0; s < 3; ++s)
-          if (nts[s] >= 0) mma_bf16_16816(acc[s], a, bq[s]);
+      for (int q = 0; q < 4; ++q) {
+        const float p0 = bf_lo(a[q]) * bf_lo(eb[q]), p1 = bf_hi(a[q]) * bf_hi(eb[q]);
+        hi[q] = pack_bf16x2(p0, p1);
+        lo[q] = pack_bf16x2(p0 - bf_lo(hi[q]), p1 - bf_hi(hi[q]));
       }
+#pragma unroll
+      for (int s = 0; s < 3; ++s)
+        if (nts[s] >= 0) {
+          mma_bf16_16816(acc[s], hi, bq[s]);
+          mma_bf16_16816(acc[s], lo, bq[s]);
+        }
     }
   }
 
@@ -734,19 +787,23 @@ struct IntraKernel {
       }
       return;
     }
+    using Wk = Walk<NTH>;
+    int row0, col;
+    const uint32_t off = walk_start<T0>(row0, col);
+    unsigned char* vb = reinterpret_cast<unsigned char*>(sV) + off;
+    const unsigned char* wb = reinterpret_cast<const unsigned char*>(sW) + off;
 #pragma unroll
-    for (int i = tid - T0; i < kChunks; i += NTH) {
-      const int row = i / (P / 8), col = (i % (P / 8)) * 8;
+    for (int j = 0; j < Wk::kSteps; ++j) {
       uint4 vv = make_uint4(0, 0, 0, 0);
-      if (!kTma || row < len) {
-        vv = *reinterpret_cast<const uint4*>(sV + pswz(row, col));
-        const uint4 ww = *reinterpret_cast<const uint4*>(sW + pswz(row, col));
+      if (!kTma || row0 + j * Wk::kRows < len) {
+        vv = *reinterpret_cast<const uint4*>(vb + j * Wk::kStride);
+        const uint4 ww = *reinterpret_cast<const uint4*>(wb + j * Wk::kStride);
         vv.x = mul_bf16x2(vv.x, ww.x);
         vv.y = mul_bf16x2(vv.y, ww.y);
         vv.z = mul_bf16x2(vv.z, ww.z);
         vv.w = mul_bf16x2(vv.w, ww.w);
       }
-      *reinterpret_cast<uint4*>(sV + pswz(row, col)) = vv;
+      *reinterpret_cast<uint4*>(vb + j * Wk::kStride) = vv;
     }
   }
 
@@ -755,17 +812,21 @@ struct IntraKernel {
   template <int T0, int NTH>
   __device__ void stage_w_kg(__nv_bfloat16* kt, __nv_bfloat16* gKG, float* gEl, int c0) {
     const int last = len - 1;
-    constexpr int kChunks = kTile * P / 8;
-    static_assert(kChunks % NTH == 0, "chunks per thread");
+    using Wk = Walk<NTH>;
+    int row0, col;
+    const uint32_t off = walk_start<T0>(row0, col);
+    unsigned char* kb = reinterpret_cast<unsigned char*>(kt) + off;
+    unsigned char* gb = reinterpret_cast<unsigned char*>(gKG) + (c0 >> 6) * 8192 + off;  // same layout
+    const unsigned char* bb = reinterpret_cast<const unsigned char*>(sB) + off;
 #pragma unroll
-    for (int i = tid - T0; i < kChunks; i += NTH) {
-      const int row = i / (P / 8), col = (i % (P / 8)) * 8;
-      uint4 kv = *reinterpret_cast<const uint4*>(kt + pswz(row, col));
+    for (int j = 0; j < Wk::kSteps; ++j) {
+      const int row = row0 + j * Wk::kRows;
+      uint4 kv = *reinterpret_cast<const uint4*>(kb + j * Wk::kStride);
       uint32_t* kw = reinterpret_cast<uint32_t*>(&kv);
       uint4 kgv;
       uint32_t* kgw = reinterpret_cast<uint32_t*>(&kgv);
       uint4 bv = make_uint4(0, 0, 0, 0);
-      if constexpr (ERASE) bv = *reinterpret_cast<const uint4*>(sB + pswz(row, col));
+      if constexpr (ERASE) bv = *reinterpret_cast<const uint4*>(bb + j * Wk::kStride);
       const uint32_t* bw = reinterpret_cast<const uint32_t*>(&bv);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -787,8 +848,8 @@ struct IntraKernel {
         else
           kw[e] = pack_bf16x2(k0 * e0, k1 * e1);
       }
-      *reinterpret_cast<uint4*>(kt + pswz(row, col)) = kv;  // w operand replaces k in place
-      *reinterpret_cast<uint4*>(gKG + pswz(row, c0 + col)) = kgv;
+      *reinterpret_cast<uint4*>(kb + j * Wk::kStride) = kv;  // w operand replaces k in place
+      *reinterpret_cast<uint4*>(gb + j * Wk::kStride) = kgv;
     }
     const int j = tid - T0;
     if (j >= 0 && j < P) {
@@ -845,7 +906,16 @@ struct IntraKernel {
   __device__ __forceinline__ void wy_block(const __nv_bfloat16* kt, __nv_bfloat16* dw, __nv_bfloat16* du) {
     constexpr int CW = P / 4;    // columns of a quarter
     constexpr int NTW = CW / 8;  // 8-column tiles of a quarter
-    const int n_base = (warp & 3) * CW;
+    // The quarter starts at 16-byte chunk cq of a row; the swizzle key of every fragment row is
+    // lane & 7 (fragment rows start at multiples of 8), and the chunk offsets within a 64-column
+    // panel (cq & 7, the tile np, the lane's half) occupy disjoint bits, so each fragment
+    // address is a per-thread base plus (constant XOR a per-thread key).
+    const int cq = (warp & 3) * (CW / 8);
+    const uint32_t key = lane & 7;
+    const uint32_t b_off = (cq >> 3) * 8192u + (lane & 15) * 128u;
+    const uint32_t b_x = ((uint32_t(cq & 7) + uint32_t(lane >> 4)) ^ key) << 4;
+    const uint32_t kt_b = smem_u32(kt) + b_off, v_b = smem_u32(sV) + b_off;
+    const uint32_t a_b = smem_u32(sAi + (16 * R + (lane & 15)) * Cfg::kLdAi + 8 * (lane >> 4));
     float aw[NTW][4], au[NTW][4];
 #pragma unroll
     for (int i = 0; i < NTW; ++i)
@@ -854,12 +924,12 @@ struct IntraKernel {
 #pragma unroll
     for (int ks = 0; ks <= R; ++ks) {
       uint32_t a[4], bw[NTW / 2][4], bu[NTW / 2][4];
-      ldsm_x4(a, smem_u32(sAi + (16 * R + (lane & 15)) * Cfg::kLdAi + 16 * ks + 8 * (lane >> 4)));
+      ldsm_x4(a, a_b + ks * 32u);
 #pragma unroll
       for (int np = 0; np < NTW; np += 2) {
-        const int off = pswz(16 * ks + (lane & 15), n_base + 8 * np + 8 * (lane >> 4));
-        ldsm_x4_t(bw[np / 2], smem_u32(kt + off));
-        ldsm_x4_t(bu[np / 2], smem_u32(sV + off));
+        const uint32_t o = ks * 2048u + ((uint32_t(np) << 4) ^ b_x);
+        ldsm_x4_t(bw[np / 2], kt_b + o);
+        ldsm_x4_t(bu[np / 2], v_b + o);
       }
 #pragma unroll
       for (int np = 0; np < NTW; np += 2) {
@@ -871,15 +941,19 @@ struct IntraKernel {
         mma_bf16_16816(au[np + 1], a, u1);
       }
     }
+    // accumulator rows 16R + g and 16R + g + 8 (swizzle key g), columns 2t, 2t + 1 of tile nt
     const int g = lane >> 2, t = lane & 3;
+    const uint32_t o_x = (uint32_t(cq & 7) ^ uint32_t(g)) << 4;
+    const uint32_t o_b = (cq >> 3) * 8192u + (16 * R + g) * 128u + 4u * t;
+    unsigned char* dwb = reinterpret_cast<unsigned char*>(dw) + o_b;
+    unsigned char* dub = reinterpret_cast<unsigned char*>(du) + o_b;
 #pragma unroll
     for (int nt = 0; nt < NTW; ++nt) {
-      const int col = n_base + 8 * nt + 2 * t;
-      const int i0 = 16 * R + g;
-      *reinterpret_cast<uint32_t*>(dw + pswz(i0, col)) = pack_bf16x2(aw[nt][0], aw[nt][1]);
-      *reinterpret_cast<uint32_t*>(dw + pswz(i0 + 8, col)) = pack_bf16x2(aw[nt][2], aw[nt][3]);
-      *reinterpret_cast<uint32_t*>(du + pswz(i0, col)) = pack_bf16x2(au[nt][0], au[nt][1]);
-      *reinterpret_cast<uint32_t*>(du + pswz(i0 + 8, col)) = pack_bf16x2(au[nt][2], au[nt][3]);
+      const uint32_t o = (uint32_t(nt) << 4) ^ o_x;
+      *reinterpret_cast<uint32_t*>(dwb + o) = pack_bf16x2(aw[nt][0], aw[nt][1]);
+      *reinterpret_cast<uint32_t*>(dwb + o + 1024) = pack_bf16x2(aw[nt][2], aw[nt][3]);
+      *reinterpret_cast<uint32_t*>(dub + o) = pack_bf16x2(au[nt][0], au[nt][1]);
+      *reinterpret_cast<uint32_t*>(dub + o + 1024) = pack_bf16x2(au[nt][2], au[nt][3]);
     }
   }
   __device__ void wy_products(const __nv_bfloat16* kt, __nv_bfloat16* dw, __nv_bfloat16* du) {
