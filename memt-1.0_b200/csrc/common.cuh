@@ -35,6 +35,32 @@ __device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
   asm("mul.rn.bf16x2 %0, %1, %2;\n" : "=r"(d) : "r"(a), "r"(b));
   return d;
 }
+// Two fp32 values in one 64-bit register pair (low word first) and the packed fp32 product,
+// rounded to nearest per lane like two separate multiplies.
+__device__ __forceinline__ uint64_t bf16x2_to_f32x2(uint32_t u) {  // exact widening
+  return (static_cast<uint64_t>(u & 0xffff0000u) << 32) | static_cast<uint64_t>(u << 16);
+}
+__device__ __forceinline__ uint64_t f32x2_splat(float x) {
+  return (static_cast<uint64_t>(__float_as_uint(x)) << 32) | __float_as_uint(x);
+}
+__device__ __forceinline__ uint64_t f32x2_pack(float lo, float hi) {
+  return (static_cast<uint64_t>(__float_as_uint(hi)) << 32) | __float_as_uint(lo);
+}
+__device__ __forceinline__ uint64_t mul_f32x2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;\n" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t f32x2_to_bf16x2(uint64_t v) {
+  return pack_bf16x2(__uint_as_float(static_cast<uint32_t>(v)), __uint_as_float(static_cast<uint32_t>(v >> 32)));
+}
+// four 8x8 bf16 matrices from mma accumulator fragments into shared memory; lane l gives the
+// address of row l % 8 of matrix l / 8
+__device__ __forceinline__ void stsm_x4(uint32_t addr, uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1, %2, %3, %4};\n" ::"r"(addr), "r"(r0), "r"(r1),
+               "r"(r2), "r"(r3)
+               : "memory");
+}
 __device__ __forceinline__ float2 unpack_bf16x2(uint32_t u) {
   __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162*>(&u);
   return __bfloat1622float2(v);

@@ -294,29 +294,25 @@ struct IntraKernel {
 #pragma unroll
     for (int j = 0; j < Wk::kSteps; ++j) {
       const int row = row0 + j * Wk::kRows;
+      const bool in = row < ln;  // rows past the chunk become zero
       uint4* ptr = reinterpret_cast<uint4*>(kb + j * Wk::kStride);
-      if (row >= ln) {
-        if constexpr (kTma) *ptr = make_uint4(0, 0, 0, 0);
-        continue;
-      }
       uint4 kv = *ptr;
-      float sb[8];
+      // both factors are bf16, so bf16(k * s) is one packed bf16 multiply
+      uint32_t sw[4];
       if (p.beta_layout == 1) {
-        const float s = sPre[ph * 2 * kTile + kTile + row];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) sb[e] = s;
+        const uint32_t s = __float_as_uint(sPre[ph * 2 * kTile + kTile + row]);  // bf16-exact
+        sw[0] = sw[1] = sw[2] = sw[3] = (s >> 16) | (s & 0xffff0000u);
       } else {
-        const uint4 be = *reinterpret_cast<const uint4*>(bsrc + (int64_t)j * Wk::kRows * row_stride);
+        uint4 be = make_uint4(0, 0, 0, 0);
+        if (in) be = *reinterpret_cast<const uint4*>(bsrc + (int64_t)j * Wk::kRows * row_stride);
         const uint32_t* bw = reinterpret_cast<const uint32_t*>(&be);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          sb[2 * e] = bf16_round(sqrtf(bf_lo(bw[e])));
-          sb[2 * e + 1] = bf16_round(sqrtf(bf_hi(bw[e])));
-        }
+        for (int e = 0; e < 4; ++e) sw[e] = pack_bf16x2(sqrtf(bf_lo(bw[e])), sqrtf(bf_hi(bw[e])));
       }
-      uint32_t* kw = reinterpret_cast<uint32_t*>(&kv);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) kw[e] = pack_bf16x2(bf_lo(kw[e]) * sb[2 * e], bf_hi(kw[e]) * sb[2 * e + 1]);
+      kv.x = in ? mul_bf16x2(kv.x, sw[0]) : 0u;
+      kv.y = in ? mul_bf16x2(kv.y, sw[1]) : 0u;
+      kv.z = in ? mul_bf16x2(kv.z, sw[2]) : 0u;
+      kv.w = in ? mul_bf16x2(kv.w, sw[3]) : 0u;
       *ptr = kv;
     }
   }
@@ -828,25 +824,30 @@ struct IntraKernel {
       uint4 bv = make_uint4(0, 0, 0, 0);
       if constexpr (ERASE) bv = *reinterpret_cast<const uint4*>(bb + j * Wk::kStride);
       const uint32_t* bw = reinterpret_cast<const uint32_t*>(&bv);
+      uint64_t eh = 0, qh = 0;
+      if constexpr (HEAD) {
+        eh = f32x2_splat(sEh[row]);
+        qh = f32x2_splat(sKgf[row]);
+      }
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float k0 = bf_lo(kw[e]), k1 = bf_hi(kw[e]);
-        float e0, e1, q0, q1;
+        const uint64_t k2 = bf16x2_to_f32x2(kw[e]);
+        uint64_t e2, q2;
         if constexpr (HEAD) {
-          e0 = e1 = sEh[row];
-          q0 = q1 = sKgf[row];
+          e2 = eh;
+          q2 = qh;
         } else {
           const float2 ev = p22(row, col + 2 * e), qv = p2d2(last, row, col + 2 * e);
-          e0 = ev.x;
-          e1 = ev.y;
-          q0 = row < len ? qv.x : 0.f;
-          q1 = row < len ? qv.y : 0.f;
+          e2 = f32x2_pack(ev.x, ev.y);
+          q2 = f32x2_pack(row < len ? qv.x : 0.f, row < len ? qv.y : 0.f);
         }
-        kgw[e] = pack_bf16x2(k0 * q0, k1 * q1);
-        if constexpr (ERASE)
-          kw[e] = pack_bf16x2(bf16_round(k0 * bf_lo(bw[e])) * e0, bf16_round(k1 * bf_hi(bw[e])) * e1);
-        else
-          kw[e] = pack_bf16x2(k0 * e0, k1 * e1);
+        kgw[e] = f32x2_to_bf16x2(mul_f32x2(k2, q2));
+        if constexpr (ERASE) {
+          const float k0 = bf_lo(kw[e]), k1 = bf_hi(kw[e]);
+          kw[e] = f32x2_to_bf16x2(mul_f32x2(f32x2_pack(bf16_round(k0 * bf_lo(bw[e])), bf16_round(k1 * bf_hi(bw[e]))), e2));
+        } else {
+          kw[e] = f32x2_to_bf16x2(mul_f32x2(k2, e2));
+        }
       }
       *reinterpret_cast<uint4*>(kb + j * Wk::kStride) = kv;  // w operand replaces k in place
       *reinterpret_cast<uint4*>(gb + j * Wk::kStride) = kgv;
@@ -941,19 +942,19 @@ struct IntraKernel {
         mma_bf16_16816(au[np + 1], a, u1);
       }
     }
-    // accumulator rows 16R + g and 16R + g + 8 (swizzle key g), columns 2t, 2t + 1 of tile nt
-    const int g = lane >> 2, t = lane & 3;
-    const uint32_t o_x = (uint32_t(cq & 7) ^ uint32_t(g)) << 4;
-    const uint32_t o_b = (cq >> 3) * 8192u + (16 * R + g) * 128u + 4u * t;
-    unsigned char* dwb = reinterpret_cast<unsigned char*>(dw) + o_b;
-    unsigned char* dub = reinterpret_cast<unsigned char*>(du) + o_b;
+    // bf16 accumulators as 8x8 matrices (tile nt, rows 16R + 8 half ..): stmatrix x4 takes tiles
+    // nt, nt + 1 with both halves; lane l addresses row l % 8 of matrix l / 8 = (tile, half)
+    const int mj = lane & 7, mh = (lane >> 3) & 1, mt = lane >> 4;
+    const uint32_t m_off = (cq >> 3) * 8192u + (16 * R + 8 * mh + mj) * 128u +
+                           ((uint32_t((cq & 7) | mt) ^ uint32_t(mj)) << 4);
+    const uint32_t dwa = smem_u32(dw) + m_off, dua = smem_u32(du) + m_off;
 #pragma unroll
-    for (int nt = 0; nt < NTW; ++nt) {
-      const uint32_t o = (uint32_t(nt) << 4) ^ o_x;
-      *reinterpret_cast<uint32_t*>(dwb + o) = pack_bf16x2(aw[nt][0], aw[nt][1]);
-      *reinterpret_cast<uint32_t*>(dwb + o + 1024) = pack_bf16x2(aw[nt][2], aw[nt][3]);
-      *reinterpret_cast<uint32_t*>(dub + o) = pack_bf16x2(au[nt][0], au[nt][1]);
-      *reinterpret_cast<uint32_t*>(dub + o + 1024) = pack_bf16x2(au[nt][2], au[nt][3]);
+    for (int nt = 0; nt < NTW; nt += 2) {
+      const uint32_t o = uint32_t(nt) << 4;  // tiles nt, nt + 1: chunk bit 1 flips
+      stsm_x4(dwa ^ o, pack_bf16x2(aw[nt][0], aw[nt][1]), pack_bf16x2(aw[nt][2], aw[nt][3]),
+              pack_bf16x2(aw[nt + 1][0], aw[nt + 1][1]), pack_bf16x2(aw[nt + 1][2], aw[nt + 1][3]));
+      stsm_x4(dua ^ o, pack_bf16x2(au[nt][0], au[nt][1]), pack_bf16x2(au[nt][2], au[nt][3]),
+              pack_bf16x2(au[nt + 1][0], au[nt + 1][1]), pack_bf16x2(au[nt + 1][2], au[nt + 1][3]));
     }
   }
   __device__ void wy_products(const __nv_bfloat16* kt, __nv_bfloat16* dw, __nv_bfloat16* du) {
