@@ -679,28 +679,34 @@ struct IntraKernel {
     if (warp < 2) {
       // Diagonal blocks by forward substitution in fp32: warp w inverts blocks 2w (lanes 0-15)
       // and 2w + 1 (lanes 16-31); lane c holds column c of X = (I + L)^-1 - I:
-      //   X[i][c] = -(L[i][c] + sum_{c < j < i} L[i][j] X[j][c])   (X[j][c] = 0 for j <= c)
-      // Row i of L is read by 128-bit broadcast loads, the sum split over four accumulators.
+      //   X[j][c] = -(L[j][c] + sum_{c < i < j} L[j][i] X[i][c])   (X[i][c] = 0 for i <= c)
+      // Right-looking: acc[j] collects the sum as soon as each X[i][c] is known, so the
+      // dependent chain per row is one select and one fma. Columns are taken four at a time:
+      // the group's own 4x4 triangle first, then every row below it with one 128-bit broadcast
+      // load of its four entries.
       const int r = 2 * warp + (lane >> 4);
       const int c = lane & 15;
       float* blk = sA + (16 * r) * LD + 16 * r;
-      float x[16];
-      x[0] = 0.f;
+      float acc[16], x[16];
 #pragma unroll
-      for (int i = 1; i < 16; ++i) {
-        float l[16];
+      for (int j = 0; j < 16; ++j) acc[j] = blk[j * LD + c];  // L[j][c]; zero on and above the diagonal
 #pragma unroll
-        for (int q = 0; q < (i + 3) / 4; ++q) {
-          const float4 v = *reinterpret_cast<const float4*>(blk + i * LD + 4 * q);
-          l[4 * q] = v.x;
-          l[4 * q + 1] = v.y;
-          l[4 * q + 2] = v.z;
-          l[4 * q + 3] = v.w;
+      for (int j0 = 0; j0 < 16; j0 += 4) {
+        float4 l[3];
+#pragma unroll
+        for (int q = 0; q < 3; ++q) l[q] = *reinterpret_cast<const float4*>(blk + (j0 + 1 + q) * LD + j0);
+        x[j0] = (c < j0) ? -acc[j0] : 0.f;
+        acc[j0 + 1] = fmaf(l[0].x, x[j0], acc[j0 + 1]);
+        x[j0 + 1] = (c < j0 + 1) ? -acc[j0 + 1] : 0.f;
+        acc[j0 + 2] = fmaf(l[1].y, x[j0 + 1], fmaf(l[1].x, x[j0], acc[j0 + 2]));
+        x[j0 + 2] = (c < j0 + 2) ? -acc[j0 + 2] : 0.f;
+        acc[j0 + 3] = fmaf(l[2].z, x[j0 + 2], fmaf(l[2].y, x[j0 + 1], fmaf(l[2].x, x[j0], acc[j0 + 3])));
+        x[j0 + 3] = (c < j0 + 3) ? -acc[j0 + 3] : 0.f;
+#pragma unroll
+        for (int j = j0 + 4; j < 16; ++j) {
+          const float4 m = *reinterpret_cast<const float4*>(blk + j * LD + j0);
+          acc[j] = fmaf(m.w, x[j0 + 3], fmaf(m.z, x[j0 + 2], fmaf(m.y, x[j0 + 1], fmaf(m.x, x[j0], acc[j]))));
         }
-        float s[4] = {blk[i * LD + c], 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int j = 1; j < i; ++j) s[j & 3] = fmaf(l[j], x[j], s[j & 3]);
-        x[i] = (c < i) ? -((s[0] + s[1]) + (s[2] + s[3])) : 0.f;
       }
       __syncwarp();
 #pragma unroll
