@@ -653,6 +653,10 @@ struct IntraKernel {
 
   // scores -> sA (strictly lower on the diagonal blocks; per-head diagonal scaled by 2^(G_i-G_j))
   __device__ void store_scores(const float (&acc)[3][4]) {
+    if constexpr (HEAD) {
+      store_scores_head(acc);
+      return;
+    }
     int r, nts[3];
     score_pieces(warp, r, nts);
     const int g = lane >> 2, t = lane & 3;
@@ -668,6 +672,42 @@ struct IntraKernel {
         if (j >= i || i >= len) x = 0.f;
         sA[i * Cfg::kLdA + j] = x;
       }
+    }
+  }
+
+  // Per-head decay: a piece left of the diagonal block (columns j < 16r <= rows i) is scaled by
+  // 2^(G_i - G_16r) * 2^(G_16r - G_j), the row and column factors of the unit's factor table
+  // (both <= 1, as G does not increase along the chunk); a piece of the diagonal block by
+  // 2^(G_i - G_j) per pair. Rows past the chunk and entries on or above the diagonal are zero.
+  __device__ void store_scores_head(const float (&acc)[3][4]) {
+    int r, nts[3];
+    score_pieces(warp, r, nts);
+    const int g = lane >> 2, t = lane & 3;
+    const int i0 = 16 * r + g, i1 = i0 + 8;
+    const bool v0 = i0 < len, v1 = i1 < len;
+    const float G0 = sG[i0], G1 = sG[i1], L0 = sLf[i0], L1 = sLf[i1];
+    float* row0 = sA + i0 * Cfg::kLdA;
+    float* row1 = sA + i1 * Cfg::kLdA;
+#pragma unroll
+    for (int s = 0; s < 3; ++s) {
+      if (nts[s] < 0) continue;
+      const int j = 8 * nts[s] + 2 * t;
+      float f00, f01, f10, f11;  // rows i0, i1 x columns j, j + 1
+      if (nts[s] < 2 * r) {
+        const float2 R = *reinterpret_cast<const float2*>(sRf + r * kTile + j);
+        f00 = L0 * R.x;
+        f01 = L0 * R.y;
+        f10 = L1 * R.x;
+        f11 = L1 * R.y;
+      } else {
+        const float2 Gj = *reinterpret_cast<const float2*>(sG + j);
+        f00 = j < i0 ? fast_exp2(G0 - Gj.x) : 0.f;
+        f01 = j + 1 < i0 ? fast_exp2(G0 - Gj.y) : 0.f;
+        f10 = j < i1 ? fast_exp2(G1 - Gj.x) : 0.f;
+        f11 = j + 1 < i1 ? fast_exp2(G1 - Gj.y) : 0.f;
+      }
+      *reinterpret_cast<float2*>(row0 + j) = v0 ? make_float2(acc[s][0] * f00, acc[s][1] * f01) : make_float2(0.f, 0.f);
+      *reinterpret_cast<float2*>(row1 + j) = v1 ? make_float2(acc[s][2] * f10, acc[s][3] * f11) : make_float2(0.f, 0.f);
     }
   }
 
@@ -1356,12 +1396,12 @@ __global__ void __launch_bounds__(256, 2) intra_kernel(const __grid_constant__ I
   k.sEi = reinterpret_cast<float*>(base + Cfg::offEi);
   k.sA = reinterpret_cast<float*>(base + Cfg::offA);
   k.sAi = reinterpret_cast<__nv_bfloat16*>(base + Cfg::offAi);
-  __shared__ float s_fac[2 * Cfg::kSmall];
+  __shared__ __align__(16) float s_fac[2 * Cfg::kSmall];
   __shared__ __align__(16) float s_scr[4 * 256];
   k.sScr = s_scr;
   k.sFac = s_fac;
   k.use_factors(0);
-  __shared__ float s_pre[4 * kTile];
+  __shared__ __align__(16) float s_pre[4 * kTile];
   k.sPre = s_pre;
   k.tid = threadIdx.x;
   k.lane = threadIdx.x & 31;
