@@ -158,6 +158,11 @@ CASES = [
     ([150, 64], 2, 256, "channel", "head", True, True, 2048),
     ([257], 1, 256, "head", None, False, True, 2048),
     ([33, 97, 64, 1], 4, 64, "channel", "channel", True, False, 64),
+    # per-head decay without erase (the TMA-fed intra path): ragged chunks whose tile rows past
+    # the sample hold the next sample's tokens, no beta, per-channel beta, d = 64
+    ([100, 37, 64, 200], 2, 128, "head", "head", False, True, 2048),
+    ([70, 5], 2, 128, "head", None, False, True, 2048),
+    ([90, 40], 2, 64, "head", "channel", False, True, 64),
 ]
 
 
@@ -184,6 +189,23 @@ def test_update_fp32_exact(cuda, case):
     torch.cuda.synchronize()
     ref = oracle_update(x, ct, "exact")
     assert O.rel_fro(out.cpu().numpy(), ref) <= TOL_F32
+
+
+def test_update_partial_chunk_ignores_next_sample(cuda):
+    """The last chunk of a sample is a 64-row tile whose rows past the sample are the next
+    sample's tokens (the tile loads do not stop at the sample end). Non-finite values there
+    must not reach the sample's result."""
+    x = to_bf16(make_inputs(11, [100, 60], 2, 128, gate="head", beta="head", erase=False, write=True))
+    first = {k_: (v_[:100] if k_ in ("q", "k", "v", "g", "beta", "w") and v_ is not None else v_) for k_, v_ in x.items()}
+    first.update(lengths=[100], cu=np.array([0, 100], np.int32), h0=x["h0"][:1])
+    for key in ("k", "v", "w", "beta"):
+        x[key] = x[key].copy()
+        x[key][100:] = np.nan
+    out = gpu_update(x, cuda, torch.bfloat16, 2048)
+    torch.cuda.synchronize()
+    got = out[0:1].cpu().numpy()
+    assert np.isfinite(got).all()
+    assert O.rel_fro(got, oracle_update(first, 2048, "bf16")) <= TOL_BF16
 
 
 def test_update_extreme_decay_slow_path(cuda):
