@@ -259,28 +259,56 @@ def run_ours(args, rank, world, local_rank):
         # ---- end to end through the public API: pinned host inputs -> device -> result -> host ----
         host_in = {name: t.cpu().pin_memory() for name, t in
                    dict(q=q, k=k, v=v, g=g, beta=beta, w=w, h0=h0).items()}
-        dev_in = {name: torch.empty_like(t) for name, t in dict(q=q, k=k, v=v, g=g, beta=beta, w=w, h0=h0).items()}
-        host_out_o = torch.empty(L, H, D, dtype=bf, pin_memory=True)
-        host_out_s = torch.empty(SESSIONS, H, D, D, dtype=torch.float32, pin_memory=True)
+        # two device input sets and two host output sets: step i's inputs go up on the H2D
+        # stream while step i - 1 computes and step i - 2's results come down on the D2H stream
+        # (PCIe is full duplex), as a serving loop would run it
+        dev_in = [{name: torch.empty_like(t, device=dev) for name, t in host_in.items()} for _ in range(2)]
+        host_out = [(torch.empty(L, H, D, dtype=bf, pin_memory=True),
+                     torch.empty(SESSIONS, H, D, D, dtype=torch.float32, pin_memory=True)) for _ in range(2)]
         bytes_in = sum(t.numel() * t.element_size() for t in host_in.values())
-        bytes_out = host_out_o.numel() * 2 + host_out_s.numel() * 4
+        bytes_out = host_out[0][0].numel() * 2 + host_out[0][1].numel() * 4
+        h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        inputs_ready = [torch.cuda.Event() for _ in range(2)]
+        inputs_free = [torch.cuda.Event() for _ in range(2)]
+        outputs_ready = [torch.cuda.Event() for _ in range(2)]
+        outputs_free = [torch.cuda.Event() for _ in range(2)]
+        for ev in inputs_free + outputs_free:
+            ev.record(stream)
 
-        def e2e_step():
-            for name, t in host_in.items():
-                dev_in[name].copy_(t, non_blocking=True)
-            o, s = M.gdn2_chunked(dev_in["q"], dev_in["k"], dev_in["v"], dev_in["g"], dev_in["beta"], dev_in["h0"],
-                                  cu, w=dev_in["w"], max_seqlen=T, chunk_tokens=CHUNK_TOKENS)
-            host_out_o.copy_(o, non_blocking=True)
-            host_out_s.copy_(s, non_blocking=True)
+        def e2e_step(i):
+            b = i % 2
+            with torch.cuda.stream(h2d):
+                h2d.wait_event(inputs_free[b])          # step i - 2 has consumed this input set
+                for name, t in host_in.items():
+                    dev_in[b][name].copy_(t, non_blocking=True)
+                inputs_ready[b].record(h2d)
+            stream.wait_event(inputs_ready[b])
+            stream.wait_event(outputs_free[b])          # step i - 2's results have left the device
+            x = dev_in[b]
+            o, s = M.gdn2_chunked(x["q"], x["k"], x["v"], x["g"], x["beta"], x["h0"],
+                                  cu, w=x["w"], max_seqlen=T, chunk_tokens=CHUNK_TOKENS)
+            inputs_free[b].record(stream)
+            outputs_ready[b].record(stream)
+            with torch.cuda.stream(d2h):
+                d2h.wait_event(outputs_ready[b])
+                host_out[b][0].copy_(o, non_blocking=True)
+                host_out[b][1].copy_(s, non_blocking=True)
+                o.record_stream(d2h)
+                s.record_stream(d2h)
+                outputs_free[b].record(d2h)
 
-        for _ in range(2):
-            e2e_step()
+        for i in range(2):
+            e2e_step(i)
         torch.cuda.synchronize()
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for _ in range(args.steps):
-            e2e_step()
+        started = torch.cuda.Event()
+        started.record(stream)
+        h2d.wait_event(started)         # no copy of the timed steps starts before e0
+        for i in range(args.steps):
+            e2e_step(i)
+        stream.wait_stream(d2h)         # the last results are on the host
         e1.record(stream)
         torch.cuda.synchronize()
         e2e_ms = e0.elapsed_time(e1) / args.steps
