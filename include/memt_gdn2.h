@@ -195,6 +195,20 @@ typedef struct memt_gdn2_read_args {
 
 int memt_gdn2_read(const memt_gdn2_read_args *args, memt_stream_t stream);
 
+/* ---- one memory layer's commit: update and read together ---------------
+ *
+ * Replaces token_memory_packed (models/qwen/ops/packed.py:34-81, models/deepseek/ops/
+ * packed.py:70-108), whose write path and read of the incoming snapshot are independent:
+ * the same work as memt_gdn2_update followed by memt_gdn2_read, with the same arguments,
+ * results and errors, but the read overlaps the update's sequential state scan. After the
+ * update's intra-chunk kernel the scan runs on a library-owned stream of the device's highest
+ * priority while the read runs on the caller's stream; the caller's stream then waits for the
+ * scan, so everything issued to it afterwards sees both results. When the read's states
+ * overlap the update's final_state, or for the fp32 (exact recurrence) update, the two run in
+ * order on the caller's stream instead. */
+int memt_gdn2_update_read(const memt_gdn2_update_args *update, void *workspace, size_t workspace_bytes,
+                          const memt_gdn2_read_args *read, memt_stream_t stream);
+
 /* ---- fused memory readout (decode / query path) -----------------------
  *
  * One pass over the fp32 state for:

@@ -3,6 +3,8 @@
 // replace) in include/memt_gdn2.h.
 #include <cuda_runtime.h>
 
+#include <mutex>
+
 #include "memt_gdn2.h"
 #include "common.cuh"
 #include "launch.h"
@@ -81,7 +83,8 @@ int check_update(const memt_gdn2_update_args* a) {
   return MEMT_OK;
 }
 
-int update_bf16(const memt_gdn2_update_args* a, void* ws, cudaStream_t s) {
+// plan and intra kernels of the bf16 update on stream s; *sp receives the scan's parameters
+int update_bf16_front(const memt_gdn2_update_args* a, void* ws, cudaStream_t s, ScanParams* sp) {
   const int D = a->key_dim;
   const WsLayout w = ws_layout(a->num_samples, a->total_tokens, a->num_heads, D, D, a->chunk_tokens);
   unsigned char* base = static_cast<unsigned char*>(ws);
@@ -113,18 +116,53 @@ int update_bf16(const memt_gdn2_update_args* a, void* ws, cudaStream_t s) {
     st = launch_intra(D, a->erase != nullptr, ip, w.max_chunks, s);
     if (st != MEMT_OK) return st;
   }
-  ScanParams sp{};
-  sp.hdr = hdr;
-  sp.sample_off = sample_off;
-  sp.N = a->num_samples;
-  sp.H = a->num_heads;
-  sp.W = ip.W;
-  sp.U = ip.U;
-  sp.KG = ip.KG;
-  sp.Elast = ip.Elast;
-  sp.h0 = a->initial_state;
-  sp.ht = a->final_state;
-  return launch_scan(D, sp, s);
+  *sp = ScanParams{};
+  sp->hdr = hdr;
+  sp->sample_off = sample_off;
+  sp->N = a->num_samples;
+  sp->H = a->num_heads;
+  sp->W = ip.W;
+  sp->U = ip.U;
+  sp->KG = ip.KG;
+  sp->Elast = ip.Elast;
+  sp->h0 = a->initial_state;
+  sp->ht = a->final_state;
+  return MEMT_OK;
+}
+
+int update_bf16(const memt_gdn2_update_args* a, void* ws, cudaStream_t s) {
+  ScanParams sp;
+  const int st = update_bf16_front(a, ws, s, &sp);
+  if (st != MEMT_OK) return st;
+  return launch_scan(a->key_dim, sp, s);
+}
+
+// A non-blocking stream of the device's highest priority, created once per device, for the
+// state scan of memt_gdn2_update_read.
+int scan_stream(cudaStream_t* out) {
+  static std::mutex m;
+  static cudaStream_t streams[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e);
+  if (dev < 0 || dev >= 64) return MEMT_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(m);
+  if (streams[dev] == nullptr) {
+    int least = 0, greatest = 0;
+    e = cudaDeviceGetStreamPriorityRange(&least, &greatest);
+    if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&streams[dev], cudaStreamNonBlocking, greatest);
+    if (e != cudaSuccess) {
+      streams[dev] = nullptr;
+      return cuda_status(e);
+    }
+  }
+  *out = streams[dev];
+  return MEMT_OK;
+}
+
+bool ranges_overlap(const void* a, size_t na, const void* b, size_t nb) {
+  const uintptr_t x = reinterpret_cast<uintptr_t>(a), y = reinterpret_cast<uintptr_t>(b);
+  return x < y + nb && y < x + na;
 }
 
 int update_f32(const memt_gdn2_update_args* a, cudaStream_t s) {
@@ -144,6 +182,34 @@ int update_f32(const memt_gdn2_update_args* a, cudaStream_t s) {
   p.h0 = a->initial_state;
   p.ht = a->final_state;
   return launch_recurrent(a->key_dim, p, s);
+}
+
+int check_read(const memt_gdn2_read_args* a) {
+  if (a == nullptr || a->num_blocks < 1 || a->num_heads < 1 || a->total_tokens < 0 ||
+      a->cu_seqlens == nullptr || a->q == nullptr || a->states == nullptr || a->out == nullptr)
+    return MEMT_ERR_INVALID_ARGUMENT;
+  if (!dim_ok(a->key_dim) || a->value_dim != a->key_dim) return MEMT_ERR_UNSUPPORTED;
+  if ((a->q_dtype != MEMT_BF16 && a->q_dtype != MEMT_F32) || (a->out_dtype != MEMT_BF16 && a->out_dtype != MEMT_F32))
+    return MEMT_ERR_INVALID_ARGUMENT;
+  if (!aligned16(a->q) || !aligned16(a->states) || !aligned16(a->out)) return MEMT_ERR_MISALIGNED;
+  return MEMT_OK;
+}
+
+// the read's kernels for arguments check_read accepted
+int read_launch(const memt_gdn2_read_args* a, memt_stream_t stream) {
+  if (a->total_tokens == 0) return MEMT_OK;
+  ReadParams p{};
+  p.num_blocks = a->num_blocks;
+  p.H = a->num_heads;
+  p.L = a->total_tokens;
+  p.cu = a->cu_seqlens;
+  p.q = a->q;
+  p.states = a->states;
+  p.scale = a->scale;
+  p.out = a->out;
+  p.out_bf16 = a->out_dtype == MEMT_BF16;
+  const int64_t maxlen = a->max_block_tokens > 0 ? a->max_block_tokens : a->total_tokens;
+  return launch_read(p, a->key_dim, a->q_dtype == MEMT_F32, maxlen, reinterpret_cast<cudaStream_t>(stream));
 }
 
 }  // namespace
@@ -210,26 +276,52 @@ int memt_gdn2_workspace_status(const void* workspace, memt_stream_t stream, int3
 }
 
 int memt_gdn2_read(const memt_gdn2_read_args* a, memt_stream_t stream) {
-  if (a == nullptr || a->num_blocks < 1 || a->num_heads < 1 || a->total_tokens < 0 ||
-      a->cu_seqlens == nullptr || a->q == nullptr || a->states == nullptr || a->out == nullptr)
-    return MEMT_ERR_INVALID_ARGUMENT;
-  if (!dim_ok(a->key_dim) || a->value_dim != a->key_dim) return MEMT_ERR_UNSUPPORTED;
-  if ((a->q_dtype != MEMT_BF16 && a->q_dtype != MEMT_F32) || (a->out_dtype != MEMT_BF16 && a->out_dtype != MEMT_F32))
-    return MEMT_ERR_INVALID_ARGUMENT;
-  if (!aligned16(a->q) || !aligned16(a->states) || !aligned16(a->out)) return MEMT_ERR_MISALIGNED;
-  if (a->total_tokens == 0) return MEMT_OK;
-  ReadParams p{};
-  p.num_blocks = a->num_blocks;
-  p.H = a->num_heads;
-  p.L = a->total_tokens;
-  p.cu = a->cu_seqlens;
-  p.q = a->q;
-  p.states = a->states;
-  p.scale = a->scale;
-  p.out = a->out;
-  p.out_bf16 = a->out_dtype == MEMT_BF16;
-  const int64_t maxlen = a->max_block_tokens > 0 ? a->max_block_tokens : a->total_tokens;
-  return launch_read(p, a->key_dim, a->q_dtype == MEMT_F32, maxlen, reinterpret_cast<cudaStream_t>(stream));
+  const int st = check_read(a);
+  if (st != MEMT_OK) return st;
+  return read_launch(a, stream);
+}
+
+int memt_gdn2_update_read(const memt_gdn2_update_args* u, void* workspace, size_t workspace_bytes,
+                          const memt_gdn2_read_args* r, memt_stream_t stream) {
+  int st = check_update(u);
+  if (st == MEMT_OK) st = check_read(r);
+  if (st != MEMT_OK) return st;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const size_t state_bytes = size_t(u->num_samples) * u->num_heads * u->key_dim * u->value_dim * sizeof(float);
+  const size_t read_state_bytes = size_t(r->num_blocks) * r->num_heads * r->key_dim * r->value_dim * sizeof(float);
+  const bool overlap_ok = u->dtype == MEMT_BF16 && r->total_tokens > 0 &&
+                          !ranges_overlap(r->states, read_state_bytes, u->final_state, state_bytes);
+  if (!overlap_ok) {  // the fp32 recurrence, or a read of the state the update writes: in order
+    st = memt_gdn2_update(u, workspace, workspace_bytes, stream);
+    return st != MEMT_OK ? st : read_launch(r, stream);
+  }
+  const size_t need = memt_gdn2_update_workspace_size(u->num_samples, u->total_tokens, u->num_heads,
+                                                      u->key_dim, u->value_dim, u->chunk_tokens, u->dtype);
+  if (workspace == nullptr || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return MEMT_ERR_WORKSPACE;
+  cudaStream_t side = nullptr;
+  st = scan_stream(&side);
+  if (st != MEMT_OK) return st;
+  ScanParams sp;
+  st = update_bf16_front(u, workspace, s, &sp);
+  if (st != MEMT_OK) return st;
+  // fork after the intra kernel: the scan on the high-priority stream, the read on the caller's
+  cudaEvent_t fork = nullptr, join = nullptr;
+  cudaError_t e = cudaEventCreateWithFlags(&fork, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&join, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventRecord(fork, s);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(side, fork, 0);
+  if (e == cudaSuccess) {
+    st = launch_scan(u->key_dim, sp, side);
+    e = cudaEventRecord(join, side);  // recorded even after a failed launch, so the join below holds
+    const int st_read = read_launch(r, stream);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(s, join, 0);
+    if (st == MEMT_OK) st = st_read;
+  }
+  if (fork != nullptr) cudaEventDestroy(fork);
+  if (join != nullptr) cudaEventDestroy(join);
+  if (e != cudaSuccess) return cuda_status(e);
+  return st;
 }
 
 int memt_memory_readout(const memt_memory_readout_args* a, memt_stream_t stream) {

@@ -131,6 +131,15 @@ def gdn2_update(k, v, g, initial_state, cu_seqlens, *, num_samples, total_tokens
     write gate [L, H, V]. cu_seqlens: int32 device [N+1]. final_state may alias
     initial_state (in-place update).
     """
+    lib, args, ws, out, _keep = _update_args(k, v, g, initial_state, cu_seqlens, num_samples, total_tokens, beta,
+                                             erase, write, chunk_tokens, final_state)
+    _lib.check(lib.memt_gdn2_update(ctypes.byref(args), _ptr(ws), ws.numel(), _stream(out.device)), "memt_gdn2_update")
+    return out
+
+
+def _update_args(k, v, g, initial_state, cu_seqlens, num_samples, total_tokens, beta, erase, write, chunk_tokens,
+                 final_state):
+    """Checked C arguments of an update (plus the tensors they point into)."""
     k = _tokens(k, "k")
     v = _tokens(v, "v")
     L, H, K = k.shape
@@ -175,11 +184,17 @@ def gdn2_update(k, v, g, initial_state, cu_seqlens, *, num_samples, total_tokens
         write=write.data_ptr() if write is not None else None,
         write_layout=_lib.GATE_PER_CHANNEL if write is not None else _lib.GATE_NONE,
         initial_state=h0.data_ptr(), final_state=out.data_ptr())
-    _lib.check(lib.memt_gdn2_update(ctypes.byref(args), _ptr(ws), ws.numel(), _stream(dev)), "memt_gdn2_update")
-    return out
+    return lib, args, ws, out, (k, v, g, beta, erase, write, h0)
 
 
 def _read(q, states, cu, num_blocks, max_block_tokens, scale, out_dtype):
+    lib, args, out, _keep = _read_args(q, states, cu, num_blocks, max_block_tokens, scale, out_dtype)
+    _lib.check(lib.memt_gdn2_read(ctypes.byref(args), _stream(out.device)), "memt_gdn2_read")
+    return out
+
+
+def _read_args(q, states, cu, num_blocks, max_block_tokens, scale, out_dtype):
+    """Checked C arguments of a snapshot read (plus the tensors they point into)."""
     q = _tokens(q, "q")
     L, H, K = q.shape
     if q.dtype not in _DTYPE or out_dtype not in _DTYPE:
@@ -192,8 +207,7 @@ def _read(q, states, cu, num_blocks, max_block_tokens, scale, out_dtype):
         num_blocks=num_blocks, num_heads=H, key_dim=K, value_dim=V, total_tokens=L,
         max_block_tokens=int(max_block_tokens), cu_seqlens=cu.data_ptr(), q=q.data_ptr(), q_dtype=_DTYPE[q.dtype],
         states=states.data_ptr(), scale=float(scale), out=out.data_ptr(), out_dtype=_DTYPE[out_dtype])
-    _lib.check(lib.memt_gdn2_read(ctypes.byref(args), _stream(q.device)), "memt_gdn2_read")
-    return out
+    return lib, args, out, (q, states)
 
 
 def token_memory_packed(q, k, v, log_decay, write, read_states, write_states, *, erase=None, lengths, scale,
@@ -207,9 +221,12 @@ def token_memory_packed(q, k, v, log_decay, write, read_states, write_states, *,
     L = _tokens(q, "q").shape[0]
     _check_lengths(lengths, L)
     cu = _cu_seqlens(lengths, q.device)
-    final = gdn2_update(k, v, log_decay, write_states, cu, num_samples=len(lengths), total_tokens=L,
-                        erase=erase, write=write, chunk_tokens=chunk_tokens)
-    read = _read(q, read_states, cu, len(lengths), max(lengths), scale, v.dtype)
+    lib, uargs, ws, final, _keep_u = _update_args(k, v, log_decay, write_states, cu, len(lengths), L, None, erase,
+                                                  write, chunk_tokens, None)
+    _, rargs, read, _keep_r = _read_args(q, read_states, cu, len(lengths), max(lengths), scale, v.dtype)
+    # one call: the read of the incoming snapshot overlaps the update's state scan
+    _lib.check(lib.memt_gdn2_update_read(ctypes.byref(uargs), _ptr(ws), ws.numel(), ctypes.byref(rargs),
+                                         _stream(final.device)), "memt_gdn2_update_read")
     return read.unsqueeze(0), final
 
 
@@ -300,8 +317,11 @@ def gdn2_chunked(q, k, v, g, beta, initial_state, cu_seqlens, *, w=None, scale=N
         max_len = int((cu_host[1:] - cu_host[:-1]).max())
         cu = cu_seqlens.to(device=k3.device, dtype=torch.int32).contiguous()
     scale = K ** -0.5 if scale is None else scale
-    final = gdn2_update(k3, v, g, initial_state, cu, num_samples=N, total_tokens=L, beta=beta,
-                        erase=erase, write=w, chunk_tokens=chunk_tokens)
+    lib, uargs, ws, final, _keep_u = _update_args(k3, v, g, initial_state, cu, N, L, beta, erase, w, chunk_tokens,
+                                                  None)
     rs = initial_state if read_states is None else read_states
-    o = _read(q, rs, cu, N, max(max_len, 1), scale, _tokens(v, "v").dtype)
+    _, rargs, o, _keep_r = _read_args(q, rs, cu, N, max(max_len, 1), scale, _tokens(v, "v").dtype)
+    # one call: the read overlaps the update's state scan (memt_gdn2_update_read)
+    _lib.check(lib.memt_gdn2_update_read(ctypes.byref(uargs), _ptr(ws), ws.numel(), ctypes.byref(rargs),
+                                         _stream(final.device)), "memt_gdn2_update_read")
     return o, final

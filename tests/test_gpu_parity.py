@@ -6,6 +6,7 @@ Tolerances (relative Frobenius):
   * fp32 mode: <= 1e-5 against float64 exact math and the reference's fp32 outputs.
 """
 
+import ctypes
 import zlib
 
 import numpy as np
@@ -13,7 +14,7 @@ import pytest
 import torch
 
 import memt_b200 as M
-from memt_b200 import ops
+from memt_b200 import _lib, ops
 from oracle import gdn2 as O
 
 pytestmark = pytest.mark.gpu
@@ -189,6 +190,36 @@ def test_update_fp32_exact(cuda, case):
     torch.cuda.synchronize()
     ref = oracle_update(x, ct, "exact")
     assert O.rel_fro(out.cpu().numpy(), ref) <= TOL_F32
+
+
+def test_update_read_matches_separate_calls(cuda):
+    """memt_gdn2_update_read (the read overlapping the update's state scan on a second stream)
+    gives exactly the results of memt_gdn2_update followed by memt_gdn2_read, also when the
+    read states are the update's own output (then the two run in order)."""
+    x = to_bf16(make_inputs(5, [300, 64, 129], 4, 128, gate="head", beta="head", erase=False, write=True))
+    bf = torch.bfloat16
+    q, k, v = (_t(x[n], cuda, bf) for n in ("q", "k", "v"))
+    g, beta, w = _t(x["g"], cuda), _t(x["beta"], cuda, bf), _t(x["w"], cuda, bf)
+    h0 = _t(x["h0"], cuda)
+    rs = h0 + 0.01
+    cu = torch.from_numpy(x["cu"]).to(cuda)
+    N, L = len(x["lengths"]), int(x["cu"][-1])
+    o_ref_fin = ops.gdn2_update(k, v, g, h0, cu, num_samples=N, total_tokens=L, beta=beta, write=w)
+    o_ref = ops._read(q, rs, cu, N, 300, 128 ** -0.5, bf)
+    o, fin = ops.gdn2_chunked(q, k, v, g, beta, h0, cu, w=w, read_states=rs, max_seqlen=300)
+    torch.cuda.synchronize()
+    assert torch.equal(o, o_ref) and torch.equal(fin, o_ref_fin)
+    # read of the state the update writes: in order on the caller's stream
+    lib = _lib.load()
+    final = torch.empty_like(h0)
+    uargs_lib, uargs, ws, out, keep_u = ops._update_args(k, v, g, h0, cu, N, L, beta, None, w, 2048, final)
+    _, rargs, o2, keep_r = ops._read_args(q, final, cu, N, 300, 128 ** -0.5, bf)
+    st = lib.memt_gdn2_update_read(ctypes.byref(uargs), ops._ptr(ws), ws.numel(), ctypes.byref(rargs),
+                                   ops._stream(cuda))
+    assert st == 0
+    torch.cuda.synchronize()
+    assert torch.equal(final, o_ref_fin)
+    assert torch.equal(o2, ops._read(q, o_ref_fin, cu, N, 300, 128 ** -0.5, bf))
 
 
 def test_update_partial_chunk_ignores_next_sample(cuda):
