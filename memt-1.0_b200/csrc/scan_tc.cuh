@@ -151,10 +151,15 @@ __global__ void __launch_bounds__(ScanTcCfg::kThreads, 1) scan_tc_kernel(ScanPar
       tc::fence_after();
       float P0[32], P1[32];
       tc::ld32x2(tc::lane_addr(tP, 32 * quarter, 64 * half), tc::lane_addr(tP, 32 * quarter, 64 * half + 32), P0, P1);
+      const uint64_t e2 = f32x2_splat(el);  // packed fp32 pairs: the same rounding per lane
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        S[j] = fmaf(el, S[j], P0[j]);
-        S[32 + j] = fmaf(el, S[32 + j], P1[j]);
+      for (int j = 0; j < 32; j += 2) {
+        const uint64_t a = fma_f32x2(e2, f32x2_pack(S[j], S[j + 1]), f32x2_pack(P0[j], P0[j + 1]));
+        const uint64_t b = fma_f32x2(e2, f32x2_pack(S[32 + j], S[33 + j]), f32x2_pack(P1[j], P1[j + 1]));
+        S[j] = f32x2_lo(a);
+        S[j + 1] = f32x2_hi(a);
+        S[32 + j] = f32x2_lo(b);
+        S[33 + j] = f32x2_hi(b);
       }
     };
     auto hand_over = [&](int b) {  // operand tile written: make it visible to the tensor cores
@@ -204,13 +209,16 @@ __global__ void __launch_bounds__(ScanTcCfg::kThreads, 1) scan_tc_kernel(ScanPar
         float X[32];
         tc::ld32(tc::lane_addr(tX, 32 * quarter, 32 * half), X);  // value `key`, tokens 32 half ..
         unsigned char* vrow = sVn + (key >> 3) * 1024 + (key & 7) * 128;
+        auto vnew = [&](int e) {  // bf16(u - X) of columns e, e + 1
+          return f32x2_to_bf16x2(sub_f32x2(f32x2_pack(uv[e], uv[e + 1]), f32x2_pack(X[e], X[e + 1])));
+        };
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint4 pk;
-          pk.x = pack_bf16x2(uv[8 * c] - X[8 * c], uv[8 * c + 1] - X[8 * c + 1]);
-          pk.y = pack_bf16x2(uv[8 * c + 2] - X[8 * c + 2], uv[8 * c + 3] - X[8 * c + 3]);
-          pk.z = pack_bf16x2(uv[8 * c + 4] - X[8 * c + 4], uv[8 * c + 5] - X[8 * c + 5]);
-          pk.w = pack_bf16x2(uv[8 * c + 6] - X[8 * c + 6], uv[8 * c + 7] - X[8 * c + 7]);
+          pk.x = vnew(8 * c);
+          pk.y = vnew(8 * c + 2);
+          pk.z = vnew(8 * c + 4);
+          pk.w = vnew(8 * c + 6);
           *reinterpret_cast<uint4*>(vrow + (((4 * half + c) ^ (key & 7)) << 4)) = pk;
         }
       }
