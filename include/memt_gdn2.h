@@ -73,7 +73,7 @@ typedef struct CUstream_st *memt_stream_t;
 #define MEMT_GATE_PER_CHANNEL 2
 
 /* Library version (major*10000 + minor*100 + patch). */
-int memt_version(void);
+int memt_version(void);  /* 200 (0.2.0): state_slots / num_slots appended to the read and readout args */
 
 /* Human-readable name of a status code. */
 const char *memt_status_string(int status);
@@ -191,6 +191,12 @@ typedef struct memt_gdn2_read_args {
   float scale;
   void *out;               /* [L,H,V]                                           */
   int32_t out_dtype;       /* MEMT_BF16 or MEMT_F32                             */
+  /* Optional state pool (replaces the executor's gather of the step's states,
+   * runtime/executor.py:84-91): NULL, or device [num_blocks] slot indices; block n then
+   * reads states[state_slots[n]] of a pool states[num_slots,H,K,V]. A block whose slot lies
+   * outside [0, num_slots) is skipped and its output rows are left unwritten. */
+  const int32_t *state_slots;
+  int32_t num_slots;
 } memt_gdn2_read_args;
 
 int memt_gdn2_read(const memt_gdn2_read_args *args, memt_stream_t stream);
@@ -240,6 +246,8 @@ typedef struct memt_memory_readout_args {
   void *out;               /* bf16 [L, row_stride]                              */
   int64_t row_stride;      /* elements per token row of residual/out (>= (head_offset+H)*D) */
   int32_t head_offset;     /* first head column written                         */
+  const int32_t *state_slots; /* optional state pool, as in memt_gdn2_read_args  */
+  int32_t num_slots;
 } memt_memory_readout_args;
 
 int memt_memory_readout(const memt_memory_readout_args *args, memt_stream_t stream);

@@ -326,6 +326,9 @@ struct ReadParams {
   const __nv_bfloat16* residual;
   int64_t row_stride;
   int32_t head_offset;
+  // optional: block n reads states[slots[n]] of a pool of num_slots snapshots (null: states[n])
+  const int32_t* slots;
+  int32_t num_slots;
 };
 
 struct RecurrentParams {

@@ -192,6 +192,7 @@ int check_read(const memt_gdn2_read_args* a) {
   if ((a->q_dtype != MEMT_BF16 && a->q_dtype != MEMT_F32) || (a->out_dtype != MEMT_BF16 && a->out_dtype != MEMT_F32))
     return MEMT_ERR_INVALID_ARGUMENT;
   if (!aligned16(a->q) || !aligned16(a->states) || !aligned16(a->out)) return MEMT_ERR_MISALIGNED;
+  if (a->state_slots != nullptr && a->num_slots < 1) return MEMT_ERR_INVALID_ARGUMENT;
   return MEMT_OK;
 }
 
@@ -208,6 +209,8 @@ int read_launch(const memt_gdn2_read_args* a, memt_stream_t stream) {
   p.scale = a->scale;
   p.out = a->out;
   p.out_bf16 = a->out_dtype == MEMT_BF16;
+  p.slots = a->state_slots;
+  p.num_slots = a->num_slots;
   const int64_t maxlen = a->max_block_tokens > 0 ? a->max_block_tokens : a->total_tokens;
   return launch_read(p, a->key_dim, a->q_dtype == MEMT_F32, maxlen, reinterpret_cast<cudaStream_t>(stream));
 }
@@ -216,7 +219,7 @@ int read_launch(const memt_gdn2_read_args* a, memt_stream_t stream) {
 
 extern "C" {
 
-int memt_version(void) { return 100; }
+int memt_version(void) { return 200; }
 
 const char* memt_status_string(int status) {
   switch (status) {
@@ -288,7 +291,8 @@ int memt_gdn2_update_read(const memt_gdn2_update_args* u, void* workspace, size_
   if (st != MEMT_OK) return st;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const size_t state_bytes = size_t(u->num_samples) * u->num_heads * u->key_dim * u->value_dim * sizeof(float);
-  const size_t read_state_bytes = size_t(r->num_blocks) * r->num_heads * r->key_dim * r->value_dim * sizeof(float);
+  const size_t read_state_bytes = size_t(r->state_slots != nullptr ? r->num_slots : r->num_blocks) * r->num_heads *
+                                  r->key_dim * r->value_dim * sizeof(float);
   const bool overlap_ok = u->dtype == MEMT_BF16 && r->total_tokens > 0 &&
                           !ranges_overlap(r->states, read_state_bytes, u->final_state, state_bytes);
   if (!overlap_ok) {  // the fp32 recurrence, or a read of the state the update writes: in order
@@ -335,6 +339,7 @@ int memt_memory_readout(const memt_memory_readout_args* a, memt_stream_t stream)
   if (!aligned16(a->q) || !aligned16(a->states) || !aligned16(a->gate) || !aligned16(a->out) ||
       !aligned16(a->residual) || !aligned16(a->norm_weight))
     return MEMT_ERR_MISALIGNED;
+  if (a->state_slots != nullptr && a->num_slots < 1) return MEMT_ERR_INVALID_ARGUMENT;
   if (a->total_tokens == 0) return MEMT_OK;
   ReadParams p{};
   p.num_blocks = a->num_blocks;
@@ -356,6 +361,8 @@ int memt_memory_readout(const memt_memory_readout_args* a, memt_stream_t stream)
   p.residual = static_cast<const __nv_bfloat16*>(a->residual);
   p.row_stride = a->row_stride;
   p.head_offset = a->head_offset;
+  p.slots = a->state_slots;
+  p.num_slots = a->num_slots;
   const int64_t maxlen = a->max_block_tokens > 0 ? a->max_block_tokens : a->total_tokens;
   return launch_read(p, a->head_dim, false, maxlen, reinterpret_cast<cudaStream_t>(stream));
 }

@@ -25,6 +25,14 @@ __device__ __forceinline__ void block_range(const ReadParams& p, int n, int64_t&
   eos = b < bos ? bos : (b > p.L ? p.L : b);
 }
 
+// snapshot of block n: n itself, or slots[n] when the caller passes slot indices into a state
+// pool; -1 for an index outside the pool (the block is skipped and its outputs left unwritten)
+__device__ __forceinline__ int64_t state_slot(const ReadParams& p, int n) {
+  if (p.slots == nullptr) return n;
+  const int s = p.slots[n];
+  return (s >= 0 && s < p.num_slots) ? s : -1;
+}
+
 // softcapped SiLU gate and the gated RMSNorm output for one element (fp32 math, bf16
 // rounding points of MemTRMSNormGated.forward)
 __device__ __forceinline__ float gated_norm_value(float o, float rstd, float w, float gate, float softcap) {
@@ -64,12 +72,14 @@ __global__ void __launch_bounds__(256, 2) read_gemv_kernel(ReadParams p) {
   block_range(p, n, bos, eos);
   const int64_t t0 = bos + (int64_t)blockIdx.y * TQ;
   if (t0 >= eos) return;
+  const int64_t slot = state_slot(p, n);
+  if (slot < 0) return;
   const int nt = (int)((eos - t0) < TQ ? (eos - t0) : TQ);
   const int64_t qrow = (int64_t)p.H * D;
 
   // 1. state stream: first batch in flight before anything else
   const int cg = tid % TPR, ro = tid / TPR;
-  const float4* S4 = reinterpret_cast<const float4*>(p.states + ((int64_t)n * p.H + h) * D * D) + ro * TPR + cg;
+  const float4* S4 = reinterpret_cast<const float4*>(p.states + (slot * p.H + h) * D * D) + ro * TPR + cg;
   float4 cur[BATCH];
 #pragma unroll
   for (int i = 0; i < BATCH; ++i) cur[i] = __ldg(S4 + (int64_t)i * RPP * TPR);
@@ -248,6 +258,8 @@ __global__ void __launch_bounds__(ReadTileCfg<D>::kNW * 32) read_tile_kernel(Rea
   block_range(p, n, bos, eos);
   const int64_t first = bos + (int64_t)blockIdx.y * kReadTilesPerCta * kTile;
   if (first >= eos) return;
+  const int64_t slot = state_slot(p, n);
+  if (slot < 0) return;
   int ntiles = (int)((eos - first + kTile - 1) / kTile);
   if (ntiles > kReadTilesPerCta) ntiles = kReadTilesPerCta;
   const int64_t qrow = (int64_t)p.H * D;
@@ -266,7 +278,7 @@ __global__ void __launch_bounds__(ReadTileCfg<D>::kNW * 32) read_tile_kernel(Rea
   load_q(0, 0);
 
   // bf16(S) -> shared (read.py:64)
-  const float4* S4 = reinterpret_cast<const float4*>(p.states + ((int64_t)n * p.H + h) * D * D);
+  const float4* S4 = reinterpret_cast<const float4*>(p.states + (slot * p.H + h) * D * D);
   for (int i = tid; i < D * D / 4; i += NT) {
     const int row = i / (D / 4), col = (i % (D / 4)) * 4;
     const float4 s = __ldg(S4 + i);

@@ -62,6 +62,8 @@ __global__ void __launch_bounds__(ReadTcCfg::kThreads, 2) read_tc_kernel(const _
   block_range(p, n, bos, eos);
   const int64_t first = bos + (int64_t)blockIdx.y * kReadTcTiles * Cfg::kTok;
   if (first >= eos) return;
+  const int64_t slot = state_slot(p, n);
+  if (slot < 0) return;
   int ntiles = (int)((eos - first + Cfg::kTok - 1) / Cfg::kTok);
   if (ntiles > kReadTcTiles) ntiles = kReadTcTiles;
   const bool tma_out = p.out_bf16 != 0;
@@ -148,7 +150,7 @@ __global__ void __launch_bounds__(ReadTcCfg::kThreads, 2) read_tc_kernel(const _
     // snapshot -> bf16 MN-major operand: thread t converts row t / 2, values 64 (t % 2) ..
     {
       const int row = tid >> 1, pan = tid & 1;
-      const float4* src = reinterpret_cast<const float4*>(p.states + ((int64_t)n * p.H + h) * D * D +
+      const float4* src = reinterpret_cast<const float4*>(p.states + (slot * p.H + h) * D * D +
                                                           (int64_t)row * D + 64 * pan);
       unsigned char* dst = sS + pan * (Cfg::kBytesS / 2) + (row >> 3) * 1024 + (row & 7) * 128;
 #pragma unroll

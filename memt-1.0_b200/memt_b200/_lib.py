@@ -42,7 +42,7 @@ class ReadArgs(ctypes.Structure):
         ("num_blocks", c_int32), ("num_heads", c_int32), ("key_dim", c_int32), ("value_dim", c_int32),
         ("total_tokens", c_int64), ("max_block_tokens", c_int32), ("cu_seqlens", c_void_p),
         ("q", c_void_p), ("q_dtype", c_int32), ("states", c_void_p), ("scale", c_float),
-        ("out", c_void_p), ("out_dtype", c_int32),
+        ("out", c_void_p), ("out_dtype", c_int32), ("state_slots", c_void_p), ("num_slots", c_int32),
     ]
 
 
@@ -52,7 +52,8 @@ class ReadoutArgs(ctypes.Structure):
         ("max_block_tokens", c_int32), ("cu_seqlens", c_void_p), ("q", c_void_p), ("normalize_q", c_int32),
         ("q_eps", c_float), ("states", c_void_p), ("scale", c_float), ("gate", c_void_p),
         ("norm_weight", c_void_p), ("norm_eps", c_float), ("softcap", c_float), ("residual", c_void_p),
-        ("out", c_void_p), ("row_stride", c_int64), ("head_offset", c_int32),
+        ("out", c_void_p), ("row_stride", c_int64), ("head_offset", c_int32), ("state_slots", c_void_p),
+        ("num_slots", c_int32),
     ]
 
 

@@ -121,6 +121,19 @@ def _states(x, N, H, K, V, device, name):
     return x.contiguous()
 
 
+def _pool(states, slots, N, H, K, V, device, name):
+    """states and slot arguments for the C ABI: with ``slots`` (int32 [N] on the device), states
+    is a pool [S, H, K, V] and sample n uses states[slots[n]]; without, states is [N, H, K, V]."""
+    if slots is None:
+        return _states(states, N, H, K, V, device, name), None, 0
+    if (states.dim() != 4 or tuple(states.shape[1:]) != (H, K, V) or states.dtype != torch.float32
+            or states.device != device or not states.is_contiguous()):
+        raise ValueError(f"{name}: expected a contiguous FP32 state pool [S, {H}, {K}, {V}] on {device}")
+    if slots.dtype != torch.int32 or slots.device != device or tuple(slots.shape) != (N,):
+        raise ValueError(f"{name}: slot indices must be int32 [{N}] on {device}")
+    return states, slots.contiguous(), states.shape[0]
+
+
 def gdn2_update(k, v, g, initial_state, cu_seqlens, *, num_samples, total_tokens, beta=None, erase=None,
                 write=None, chunk_tokens=2048, final_state=None):
     """GDN-2 write path over packed samples. Returns the final state [N, H, K, V] fp32.
@@ -193,37 +206,40 @@ def _read(q, states, cu, num_blocks, max_block_tokens, scale, out_dtype):
     return out
 
 
-def _read_args(q, states, cu, num_blocks, max_block_tokens, scale, out_dtype):
+def _read_args(q, states, cu, num_blocks, max_block_tokens, scale, out_dtype, slots=None):
     """Checked C arguments of a snapshot read (plus the tensors they point into)."""
     q = _tokens(q, "q")
     L, H, K = q.shape
     if q.dtype not in _DTYPE or out_dtype not in _DTYPE:
         raise ValueError("q and output must be bfloat16 or float32")
-    states = _states(states, num_blocks, H, K, states.shape[-1], q.device, "states")
+    states, slots, num_slots = _pool(states, slots, num_blocks, H, K, states.shape[-1], q.device, "states")
     V = states.shape[-1]
     out = torch.empty(L, H, V, device=q.device, dtype=out_dtype)
     lib = _lib.load()
     args = _lib.ReadArgs(
         num_blocks=num_blocks, num_heads=H, key_dim=K, value_dim=V, total_tokens=L,
         max_block_tokens=int(max_block_tokens), cu_seqlens=cu.data_ptr(), q=q.data_ptr(), q_dtype=_DTYPE[q.dtype],
-        states=states.data_ptr(), scale=float(scale), out=out.data_ptr(), out_dtype=_DTYPE[out_dtype])
-    return lib, args, out, (q, states)
+        states=states.data_ptr(), scale=float(scale), out=out.data_ptr(), out_dtype=_DTYPE[out_dtype],
+        state_slots=slots.data_ptr() if slots is not None else None, num_slots=num_slots)
+    return lib, args, out, (q, states, slots)
 
 
 def token_memory_packed(q, k, v, log_decay, write, read_states, write_states, *, erase=None, lengths, scale,
-                        chunk_tokens):
+                        chunk_tokens, read_slots=None):
     """Write packed GDN-2 events and read each sample's fixed incoming snapshot.
 
     Returns (read [1, L, H, V] in v.dtype, final_state [N, H, K, V] fp32), like the
     reference. ``erase`` is the Qwen flavour's channel-wise erase factor; the DeepSeek
-    flavour passes none.
+    flavour passes none. With ``read_slots`` (int32 [N] on the device) ``read_states`` is the
+    state pool [S, H, K, V] and sample n reads read_states[read_slots[n]] in place.
     """
     L = _tokens(q, "q").shape[0]
     _check_lengths(lengths, L)
     cu = _cu_seqlens(lengths, q.device)
     lib, uargs, ws, final, _keep_u = _update_args(k, v, log_decay, write_states, cu, len(lengths), L, None, erase,
                                                   write, chunk_tokens, None)
-    _, rargs, read, _keep_r = _read_args(q, read_states, cu, len(lengths), max(lengths), scale, v.dtype)
+    _, rargs, read, _keep_r = _read_args(q, read_states, cu, len(lengths), max(lengths), scale, v.dtype,
+                                         slots=read_slots)
     # one call: the read of the incoming snapshot overlaps the update's state scan
     _lib.check(lib.memt_gdn2_update_read(ctypes.byref(uargs), _ptr(ws), ws.numel(), ctypes.byref(rargs),
                                          _stream(final.device)), "memt_gdn2_update_read")
@@ -252,12 +268,14 @@ def snapshot_read(query, states, lengths, scale, *, bf16_accumulator_output=Fals
 
 
 def memory_readout(q, states, lengths, scale, gate, norm_weight, *, eps=1e-6, softcap, residual=None,
-                   out=None, head_offset=0, normalize_q=True, q_eps=1e-6):
+                   out=None, head_offset=0, normalize_q=True, q_eps=1e-6, state_slots=None):
     """Fused decode/query readout over bf16 activations.
 
     y = MemTRMSNormGated(read(l2norm(q), states), gate) and out = residual + y, written into
     out[:, (head_offset + h) * D + v] (``residual`` may be ``out`` for an in-place add into
-    the attention output). Returns out [L, row_stride].
+    the attention output). Returns out [L, row_stride]. With ``state_slots`` (int32 [N] on the
+    device) ``states`` is the state pool [S, H, D, D] and sample n reads states[state_slots[n]]
+    directly, without gathering the step's states into a new tensor first.
     """
     q = _tokens(q, "q")
     L, H, D = q.shape
@@ -267,7 +285,7 @@ def memory_readout(q, states, lengths, scale, gate, norm_weight, *, eps=1e-6, so
     gate = _tokens(gate, "gate")
     if tuple(gate.shape) != (L, H, D) or gate.dtype != torch.bfloat16:
         raise ValueError("gate must be bf16 [L, H, D]")
-    states = _states(states, len(lengths), H, D, D, q.device, "states")
+    states, slots, num_slots = _pool(states, state_slots, len(lengths), H, D, D, q.device, "states")
     if tuple(norm_weight.shape) != (D,) or norm_weight.dtype != torch.bfloat16:
         raise ValueError("norm_weight must be bf16 [D]")
     norm_weight = norm_weight.contiguous()
@@ -286,7 +304,8 @@ def memory_readout(q, states, lengths, scale, gate, norm_weight, *, eps=1e-6, so
         states=states.data_ptr(), scale=float(scale), gate=gate.data_ptr(), norm_weight=norm_weight.data_ptr(),
         norm_eps=float(eps), softcap=float(softcap),
         residual=residual.data_ptr() if residual is not None else None, out=out.data_ptr(),
-        row_stride=out.shape[1], head_offset=int(head_offset))
+        row_stride=out.shape[1], head_offset=int(head_offset),
+        state_slots=slots.data_ptr() if slots is not None else None, num_slots=num_slots)
     _lib.check(lib.memt_memory_readout(ctypes.byref(args), _stream(q.device)), "memt_memory_readout")
     return out
 

@@ -222,6 +222,46 @@ def test_update_read_matches_separate_calls(cuda):
     assert torch.equal(o2, ops._read(q, o_ref_fin, cu, N, 300, 128 ** -0.5, bf))
 
 
+def test_reads_from_a_state_pool(cuda):
+    """Slot indices into a state pool (instead of gathering the step's states into a new
+    tensor) give bit-identical readouts and commit reads; a slot outside the pool leaves its
+    block's output untouched."""
+    gen = torch.Generator(device=cuda).manual_seed(3)
+    bf = torch.bfloat16
+    H, D, S = 4, 128, 11
+    pool = 0.05 * torch.randn(S, H, D, D, device=cuda, generator=gen)
+    slots = torch.tensor([7, 2, 9], dtype=torch.int32, device=cuda)
+    gathered = pool[slots.long()].contiguous()
+    # decode readout: one token per session
+    n = 3
+    q = torch.randn(n, H, D, device=cuda, generator=gen).to(bf)
+    gate = torch.randn(n, H, D, device=cuda, generator=gen).to(bf)
+    w = (1 + 0.1 * torch.randn(D, device=cuda, generator=gen)).to(bf)
+    res = torch.randn(n, H * D, device=cuda, generator=gen).to(bf)
+    ref = M.memory_readout(q, gathered, [1] * n, D ** -0.5, gate, w, softcap=10.0, residual=res)
+    got = M.memory_readout(q, pool, [1] * n, D ** -0.5, gate, w, softcap=10.0, residual=res, state_slots=slots)
+    torch.cuda.synchronize()
+    assert torch.equal(got, ref)
+    # commit read inside token_memory_packed: ragged samples long enough for the tile kernels
+    x = to_bf16(make_inputs(9, [700, 64, 1100], H, D, gate="channel", beta=None, erase=False, write=True))
+    args = dict(lengths=x["lengths"], scale=D ** -0.5, chunk_tokens=2048)
+    kk = _t(x["k"], cuda, bf)
+    tens = [_t(x[name], cuda, bf)[None] for name in ("q",)] + [kk[None], _t(x["v"], cuda, bf)[None],
+                                                              _t(x["g"], cuda)[None], _t(x["w"], cuda, bf)[None]]
+    h0 = _t(x["h0"], cuda)
+    r_ref, f_ref = M.token_memory_packed(*tens, gathered, h0, **args)
+    r_got, f_got = M.token_memory_packed(*tens, pool, h0, read_slots=slots, **args)
+    torch.cuda.synchronize()
+    assert torch.equal(r_got, r_ref) and torch.equal(f_got, f_ref)
+    # a slot outside the pool: that session's output is not written
+    bad = torch.tensor([7, S + 3, 9], dtype=torch.int32, device=cuda)
+    out = torch.full((n, H * D), 7.0, device=cuda, dtype=bf)
+    M.memory_readout(q, pool, [1] * n, D ** -0.5, gate, w, softcap=10.0, residual=res, out=out, state_slots=bad)
+    torch.cuda.synchronize()
+    assert torch.equal(out[1], torch.full_like(out[1], 7.0))
+    assert torch.equal(out[0], ref[0]) and torch.equal(out[2], ref[2])
+
+
 def test_update_partial_chunk_ignores_next_sample(cuda):
     """The last chunk of a sample is a 64-row tile whose rows past the sample are the next
     sample's tokens (the tile loads do not stop at the sample end). Non-finite values there
