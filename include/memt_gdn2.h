@@ -73,7 +73,7 @@ typedef struct CUstream_st *memt_stream_t;
 #define MEMT_GATE_PER_CHANNEL 2
 
 /* Library version (major*10000 + minor*100 + patch). */
-int memt_version(void);  /* 200 (0.2.0): state_slots / num_slots appended to the read and readout args */
+int memt_version(void);  /* 200 (0.2.0): state pools by slot index (fields appended to the update, read and readout args) */
 
 /* Human-readable name of a status code. */
 const char *memt_status_string(int status);
@@ -127,6 +127,17 @@ typedef struct memt_gdn2_update_args {
   int32_t write_layout;
   const float *initial_state; /* [N,H,K,V] fp32                                  */
   float *final_state;         /* [N,H,K,V] fp32                                  */
+  /* Optional state pools (replace the executor's gather before and index_copy_ after the
+   * update, runtime/executor.py:84-110): NULL, or device int32 [N] slot indices. Sample n then
+   * starts from initial_state[initial_slots[n]] of a pool [num_initial_slots,H,K,V] and/or
+   * ends in final_state[final_slots[n]] of a pool [num_final_slots,H,K,V] (the two pools may
+   * be one tensor; distinct samples need distinct final slots). An input slot outside its
+   * pool starts from a zero state, an output slot outside its pool is not written; both set
+   * bit 3 of the workspace status word (bf16 update). Appended in version 0.2.0. */
+  const int32_t *initial_slots;
+  int32_t num_initial_slots;
+  const int32_t *final_slots;
+  int32_t num_final_slots;
 } memt_gdn2_update_args;
 
 /* Workspace bytes memt_gdn2_update needs for these sizes (0 on invalid sizes). */
@@ -164,7 +175,8 @@ int memt_gdn2_update(const memt_gdn2_update_args *args, void *workspace, size_t 
 int memt_gdn2_update_noalloc(const memt_gdn2_update_args *args, memt_stream_t stream);
 
 /* Device status word the last update left in this workspace (0 = clean; bit 0: a sample
- * had negative length or offsets outside [0, L]; bit 1: chunk table overflow). Reading it
+ * had negative length or offsets outside [0, L]; bit 1: chunk table overflow; bit 2: a copy
+ * wait timed out; bit 3: a state slot outside its pool). Reading it
  * synchronises the stream; intended for tests and debugging. */
 int memt_gdn2_workspace_status(const void *workspace, memt_stream_t stream, int32_t *status_out);
 
@@ -210,8 +222,9 @@ int memt_gdn2_read(const memt_gdn2_read_args *args, memt_stream_t stream);
  * update's intra-chunk kernel the scan runs on a library-owned stream of the device's highest
  * priority while the read runs on the caller's stream; the caller's stream then waits for the
  * scan, so everything issued to it afterwards sees both results. When the read's states
- * overlap the update's final_state, or for the fp32 (exact recurrence) update, the two run in
- * order on the caller's stream instead. */
+ * overlap the update's final_state (for example one state pool read and updated in place),
+ * or for the fp32 (exact recurrence) update, the two run in order on the caller's stream
+ * instead, the read first: it reads the incoming snapshot. */
 int memt_gdn2_update_read(const memt_gdn2_update_args *update, void *workspace, size_t workspace_bytes,
                           const memt_gdn2_read_args *read, memt_stream_t stream);
 

@@ -252,7 +252,8 @@ struct ChunkDesc {
 // Workspace header (first 256 bytes of every update workspace).
 struct WsHeader {
   int32_t num_chunks;  // chunks written by the plan kernel
-  int32_t status;      // bit 0: clamped offsets, bit 1: chunk table overflow, bit 2: copy wait timed out
+  int32_t status;      // bit 0: clamped offsets, bit 1: chunk table overflow, bit 2: copy wait timed out,
+                       // bit 3: a state slot outside its pool
   int32_t reserved[62];
 };
 
@@ -295,6 +296,14 @@ struct IntraParams {
   CUtensorMap k_map, v_map, w_map;
 };
 
+// Slot of sample n in a state pool addressed by optional slot indices: n itself when slots is
+// null, slots[n] when it lies in [0, num), and -1 otherwise (the caller skips that state).
+__device__ __forceinline__ int64_t pool_slot(const int32_t* slots, int32_t num, int n) {
+  if (slots == nullptr) return n;
+  const int s = slots[n];
+  return (s >= 0 && s < num) ? s : -1;
+}
+
 struct ScanParams {
   WsHeader* hdr;
   const int32_t* sample_off;  // [N+1] chunk offsets per sample
@@ -305,6 +314,10 @@ struct ScanParams {
   const float* Elast;
   const float* h0;
   float* ht;
+  // optional pools: sample n starts from h0[slots_in[n]] and ends in ht[slots_out[n]]
+  const int32_t* slots_in;
+  const int32_t* slots_out;
+  int32_t num_in, num_out;
 };
 
 struct ReadParams {
@@ -345,6 +358,9 @@ struct RecurrentParams {
   const float* write;
   const float* h0;
   float* ht;
+  const int32_t* slots_in;  // optional pools, as in ScanParams
+  const int32_t* slots_out;
+  int32_t num_in, num_out;
 };
 
 }  // namespace memt

@@ -80,6 +80,8 @@ int check_update(const memt_gdn2_update_args* a) {
       !aligned16(a->final_state) || !aligned16(a->erase) || !aligned16(a->write) ||
       (a->beta_layout == MEMT_GATE_PER_CHANNEL && !aligned16(a->beta)))
     return MEMT_ERR_MISALIGNED;
+  if ((a->initial_slots != nullptr && a->num_initial_slots < 1) || (a->final_slots != nullptr && a->num_final_slots < 1))
+    return MEMT_ERR_INVALID_ARGUMENT;
   return MEMT_OK;
 }
 
@@ -127,6 +129,10 @@ int update_bf16_front(const memt_gdn2_update_args* a, void* ws, cudaStream_t s, 
   sp->Elast = ip.Elast;
   sp->h0 = a->initial_state;
   sp->ht = a->final_state;
+  sp->slots_in = a->initial_slots;
+  sp->num_in = a->num_initial_slots;
+  sp->slots_out = a->final_slots;
+  sp->num_out = a->num_final_slots;
   return MEMT_OK;
 }
 
@@ -181,6 +187,10 @@ int update_f32(const memt_gdn2_update_args* a, cudaStream_t s) {
   p.write = static_cast<const float*>(a->write);
   p.h0 = a->initial_state;
   p.ht = a->final_state;
+  p.slots_in = a->initial_slots;
+  p.num_in = a->num_initial_slots;
+  p.slots_out = a->final_slots;
+  p.num_out = a->num_final_slots;
   return launch_recurrent(a->key_dim, p, s);
 }
 
@@ -290,14 +300,17 @@ int memt_gdn2_update_read(const memt_gdn2_update_args* u, void* workspace, size_
   if (st == MEMT_OK) st = check_read(r);
   if (st != MEMT_OK) return st;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const size_t state_bytes = size_t(u->num_samples) * u->num_heads * u->key_dim * u->value_dim * sizeof(float);
+  const size_t state_bytes = size_t(u->final_slots != nullptr ? u->num_final_slots : u->num_samples) * u->num_heads *
+                             u->key_dim * u->value_dim * sizeof(float);
   const size_t read_state_bytes = size_t(r->state_slots != nullptr ? r->num_slots : r->num_blocks) * r->num_heads *
                                   r->key_dim * r->value_dim * sizeof(float);
   const bool overlap_ok = u->dtype == MEMT_BF16 && r->total_tokens > 0 &&
                           !ranges_overlap(r->states, read_state_bytes, u->final_state, state_bytes);
-  if (!overlap_ok) {  // the fp32 recurrence, or a read of the state the update writes: in order
-    st = memt_gdn2_update(u, workspace, workspace_bytes, stream);
-    return st != MEMT_OK ? st : read_launch(r, stream);
+  if (!overlap_ok) {
+    // the fp32 recurrence, or a read of states the update writes (e.g. one pool updated in
+    // place): in order, the read first, as it reads the incoming snapshot
+    st = read_launch(r, stream);
+    return st != MEMT_OK ? st : memt_gdn2_update(u, workspace, workspace_bytes, stream);
   }
   const size_t need = memt_gdn2_update_workspace_size(u->num_samples, u->total_tokens, u->num_heads,
                                                       u->key_dim, u->value_dim, u->chunk_tokens, u->dtype);

@@ -26,10 +26,11 @@ __global__ void __launch_bounds__(128) recurrent_kernel(RecurrentParams p) {
   int64_t bos = p.cu[n], eos = p.cu[n + 1];
   bos = bos < 0 ? 0 : (bos > p.L ? p.L : bos);
   eos = eos < bos ? bos : (eos > p.L ? p.L : eos);
-  const int64_t soff = ((int64_t)n * p.H + h) * D * D;
+  const int64_t in_slot = pool_slot(p.slots_in, p.num_in, n), out_slot = pool_slot(p.slots_out, p.num_out, n);
+  const int64_t in_off = (in_slot * p.H + h) * D * D, out_off = (out_slot * p.H + h) * D * D;
   float S[RPG];
 #pragma unroll
-  for (int i = 0; i < RPG; ++i) S[i] = p.h0[soff + (int64_t)(grp * RPG + i) * D + v];
+  for (int i = 0; i < RPG; ++i) S[i] = in_slot >= 0 ? p.h0[in_off + (int64_t)(grp * RPG + i) * D + v] : 0.f;
   const int64_t rs = (int64_t)p.H * D;
   for (int64_t t = bos; t < eos; ++t) {
     const int64_t base = t * rs + (int64_t)h * D;
@@ -61,8 +62,9 @@ __global__ void __launch_bounds__(128) recurrent_kernel(RecurrentParams p) {
     for (int i = 0; i < RPG; ++i) S[i] = fmaf(s_k[grp * RPG + i], dl, S[i]);
     __syncthreads();
   }
+  if (out_slot < 0) return;
 #pragma unroll
-  for (int i = 0; i < RPG; ++i) p.ht[soff + (int64_t)(grp * RPG + i) * D + v] = S[i];
+  for (int i = 0; i < RPG; ++i) p.ht[out_off + (int64_t)(grp * RPG + i) * D + v] = S[i];
 }
 
 }  // namespace memt

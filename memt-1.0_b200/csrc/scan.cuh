@@ -79,13 +79,18 @@ __global__ void __launch_bounds__(ScanCfg<D>::kThreads) scan_kernel(ScanParams p
 
   // ---- initial state panel: warp w owns rows 16w..16w+15 (C fragments) ----
   float S[Cfg::kNT][4];
-  const int64_t state_off = ((int64_t)n * p.H + h) * D * D;
+  const int64_t in_slot = pool_slot(p.slots_in, p.num_in, n), out_slot = pool_slot(p.slots_out, p.num_out, n);
+  if (tid == 0 && (in_slot < 0 || out_slot < 0)) atomicOr(&p.hdr->status, 8);  // slot outside its pool
+  const int64_t in_off = (in_slot * p.H + h) * D * D, out_off = (out_slot * p.H + h) * D * D;
   const int r0 = warp * 16 + g;
 #pragma unroll
   for (int nt = 0; nt < Cfg::kNT; ++nt) {
     const int col = v0 + 8 * nt + 2 * t;
-    const float2 a = *reinterpret_cast<const float2*>(p.h0 + state_off + (int64_t)r0 * D + col);
-    const float2 b = *reinterpret_cast<const float2*>(p.h0 + state_off + (int64_t)(r0 + 8) * D + col);
+    float2 a = make_float2(0.f, 0.f), b = a;  // zero state for an input slot outside the pool
+    if (in_slot >= 0) {
+      a = *reinterpret_cast<const float2*>(p.h0 + in_off + (int64_t)r0 * D + col);
+      b = *reinterpret_cast<const float2*>(p.h0 + in_off + (int64_t)(r0 + 8) * D + col);
+    }
     S[nt][0] = a.x;
     S[nt][1] = a.y;
     S[nt][2] = b.x;
@@ -178,11 +183,12 @@ __global__ void __launch_bounds__(ScanCfg<D>::kThreads) scan_kernel(ScanParams p
   }
 
   // ---- final state ----
+  if (out_slot < 0) return;
 #pragma unroll
   for (int nt = 0; nt < Cfg::kNT; ++nt) {
     const int col = v0 + 8 * nt + 2 * t;
-    *reinterpret_cast<float2*>(p.ht + state_off + (int64_t)r0 * D + col) = make_float2(S[nt][0], S[nt][1]);
-    *reinterpret_cast<float2*>(p.ht + state_off + (int64_t)(r0 + 8) * D + col) = make_float2(S[nt][2], S[nt][3]);
+    *reinterpret_cast<float2*>(p.ht + out_off + (int64_t)r0 * D + col) = make_float2(S[nt][0], S[nt][1]);
+    *reinterpret_cast<float2*>(p.ht + out_off + (int64_t)(r0 + 8) * D + col) = make_float2(S[nt][2], S[nt][3]);
   }
 }
 

@@ -88,7 +88,10 @@ __global__ void __launch_bounds__(ScanTcCfg::kThreads, 1) scan_tc_kernel(ScanPar
 
   const int quarter = warp & 3, half = (warp >> 2) & 1;
   const int key = 32 * quarter + lane;  // state row; also the value row of X^T and v_new
-  const int64_t state_off = ((int64_t)n * p.H + h) * D * D + (int64_t)key * D + 64 * half;
+  const int64_t in_slot = pool_slot(p.slots_in, p.num_in, n), out_slot = pool_slot(p.slots_out, p.num_out, n);
+  if (tid == 0 && (in_slot < 0 || out_slot < 0)) atomicOr(&p.hdr->status, 8);  // slot outside its pool
+  const int64_t row_off = (int64_t)key * D + 64 * half;
+  const int64_t in_off = (in_slot * p.H + h) * D * D + row_off, out_off = (out_slot * p.H + h) * D * D + row_off;
   float S[64];
 
   if (warp == Cfg::kWorkerWarps) {
@@ -139,8 +142,8 @@ __global__ void __launch_bounds__(ScanTcCfg::kThreads, 1) scan_tc_kernel(ScanPar
   } else {
     // ---------------- worker warps ----------------
 #pragma unroll
-    for (int j = 0; j < 64; j += 4) {
-      const float4 v = *reinterpret_cast<const float4*>(p.h0 + state_off + j);
+    for (int j = 0; j < 64; j += 4) {  // zero state for an input slot outside the pool
+      const float4 v = in_slot >= 0 ? *reinterpret_cast<const float4*>(p.h0 + in_off + j) : make_float4(0.f, 0.f, 0.f, 0.f);
       S[j] = v.x;
       S[j + 1] = v.y;
       S[j + 2] = v.z;
@@ -231,10 +234,10 @@ __global__ void __launch_bounds__(ScanTcCfg::kThreads, 1) scan_tc_kernel(ScanPar
   }
   // a wait that ran out anywhere in the CTA: leave the final state untouched
   const bool ok = __syncthreads_and(alive) != 0;
-  if (ok && warp < Cfg::kWorkerWarps) {
+  if (ok && warp < Cfg::kWorkerWarps && out_slot >= 0) {
 #pragma unroll
     for (int j = 0; j < 64; j += 4)
-      *reinterpret_cast<float4*>(p.ht + state_off + j) = make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
+      *reinterpret_cast<float4*>(p.ht + out_off + j) = make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
   }
   tc::fence_before();
   __syncthreads();

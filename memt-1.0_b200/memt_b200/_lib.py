@@ -34,6 +34,8 @@ class UpdateArgs(ctypes.Structure):
         ("cu_seqlens", c_void_p), ("k", c_void_p), ("v", c_void_p), ("g", c_void_p), ("g_layout", c_int32),
         ("beta", c_void_p), ("beta_layout", c_int32), ("erase", c_void_p), ("erase_layout", c_int32),
         ("write", c_void_p), ("write_layout", c_int32), ("initial_state", c_void_p), ("final_state", c_void_p),
+        ("initial_slots", c_void_p), ("num_initial_slots", c_int32), ("final_slots", c_void_p),
+        ("num_final_slots", c_int32),
     ]
 
 

@@ -135,23 +135,25 @@ def _pool(states, slots, N, H, K, V, device, name):
 
 
 def gdn2_update(k, v, g, initial_state, cu_seqlens, *, num_samples, total_tokens, beta=None, erase=None,
-                write=None, chunk_tokens=2048, final_state=None):
+                write=None, chunk_tokens=2048, final_state=None, initial_slots=None, final_slots=None):
     """GDN-2 write path over packed samples. Returns the final state [N, H, K, V] fp32.
 
     k, v: [L, H, D] bf16 (tensor-core path, reference GPU rounding) or fp32 (exact fp32
     recurrence). g: fp32 natural-log decay [L, H] or [L, H, K]. beta: sqrt(beta) is folded
     into k ([L, H] or [L, H, K]). erase: FLA channel-wise erase factor [L, H, K]. write:
     write gate [L, H, V]. cu_seqlens: int32 device [N+1]. final_state may alias
-    initial_state (in-place update).
+    initial_state (in-place update). initial_slots / final_slots (int32 [N] on the device):
+    initial_state / final_state are then state pools and sample n starts from
+    initial_state[initial_slots[n]] / ends in final_state[final_slots[n]] (returned: the pool).
     """
     lib, args, ws, out, _keep = _update_args(k, v, g, initial_state, cu_seqlens, num_samples, total_tokens, beta,
-                                             erase, write, chunk_tokens, final_state)
+                                             erase, write, chunk_tokens, final_state, initial_slots, final_slots)
     _lib.check(lib.memt_gdn2_update(ctypes.byref(args), _ptr(ws), ws.numel(), _stream(out.device)), "memt_gdn2_update")
     return out
 
 
 def _update_args(k, v, g, initial_state, cu_seqlens, num_samples, total_tokens, beta, erase, write, chunk_tokens,
-                 final_state):
+                 final_state, initial_slots=None, final_slots=None):
     """Checked C arguments of an update (plus the tensors they point into)."""
     k = _tokens(k, "k")
     v = _tokens(v, "v")
@@ -176,9 +178,17 @@ def _update_args(k, v, g, initial_state, cu_seqlens, num_samples, total_tokens, 
         if tuple(write.shape) != (L, H, V) or write.dtype != k.dtype:
             raise ValueError("write gate must be [L, H, V] in the value dtype")
     N = int(num_samples)
-    h0 = _states(initial_state, N, H, K, V, dev, "initial_state")
-    out = torch.empty_like(h0) if final_state is None else final_state
-    _states(out, N, H, K, V, dev, "final_state")
+    h0, in_slots, n_in = _pool(initial_state, initial_slots, N, H, K, V, dev, "initial_state")
+    if final_state is None:
+        if final_slots is not None:
+            raise ValueError("final_slots index into final_state, which must then be given")
+        out = torch.empty(N, H, K, V, device=dev, dtype=torch.float32)
+    else:
+        out = final_state
+    if final_slots is None:
+        _states(out, N, H, K, V, dev, "final_state")
+    else:
+        _pool(out, final_slots, N, H, K, V, dev, "final_state")
     if not out.is_contiguous():
         raise ValueError("final_state must be contiguous")
     if cu_seqlens.dtype != torch.int32 or cu_seqlens.device != dev or cu_seqlens.numel() != N + 1:
@@ -196,8 +206,11 @@ def _update_args(k, v, g, initial_state, cu_seqlens, num_samples, total_tokens, 
         erase=erase.data_ptr() if erase is not None else None, erase_layout=erase_layout,
         write=write.data_ptr() if write is not None else None,
         write_layout=_lib.GATE_PER_CHANNEL if write is not None else _lib.GATE_NONE,
-        initial_state=h0.data_ptr(), final_state=out.data_ptr())
-    return lib, args, ws, out, (k, v, g, beta, erase, write, h0)
+        initial_state=h0.data_ptr(), final_state=out.data_ptr(),
+        initial_slots=in_slots.data_ptr() if in_slots is not None else None, num_initial_slots=n_in,
+        final_slots=final_slots.data_ptr() if final_slots is not None else None,
+        num_final_slots=out.shape[0] if final_slots is not None else 0)
+    return lib, args, ws, out, (k, v, g, beta, erase, write, h0, in_slots, final_slots)
 
 
 def _read(q, states, cu, num_blocks, max_block_tokens, scale, out_dtype):
@@ -225,19 +238,27 @@ def _read_args(q, states, cu, num_blocks, max_block_tokens, scale, out_dtype, sl
 
 
 def token_memory_packed(q, k, v, log_decay, write, read_states, write_states, *, erase=None, lengths, scale,
-                        chunk_tokens, read_slots=None):
+                        chunk_tokens, read_slots=None, write_slots=None, final_slots=None):
     """Write packed GDN-2 events and read each sample's fixed incoming snapshot.
 
     Returns (read [1, L, H, V] in v.dtype, final_state [N, H, K, V] fp32), like the
     reference. ``erase`` is the Qwen flavour's channel-wise erase factor; the DeepSeek
     flavour passes none. With ``read_slots`` (int32 [N] on the device) ``read_states`` is the
-    state pool [S, H, K, V] and sample n reads read_states[read_slots[n]] in place.
+    state pool [S, H, K, V] and sample n reads read_states[read_slots[n]] in place. With
+    ``write_slots`` ``write_states`` is a pool too: sample n starts from
+    write_states[write_slots[n]] and its final state is written into write_states at
+    ``final_slots`` (default: write_slots, an in-place update); the pool is returned as
+    final_state.
     """
     L = _tokens(q, "q").shape[0]
     _check_lengths(lengths, L)
     cu = _cu_seqlens(lengths, q.device)
+    if write_slots is None and final_slots is not None:
+        raise ValueError("final_slots needs write_slots (write_states is then the pool)")
+    pool_out = write_states if write_slots is not None else None
+    out_slots = (final_slots if final_slots is not None else write_slots) if write_slots is not None else None
     lib, uargs, ws, final, _keep_u = _update_args(k, v, log_decay, write_states, cu, len(lengths), L, None, erase,
-                                                  write, chunk_tokens, None)
+                                                  write, chunk_tokens, pool_out, write_slots, out_slots)
     _, rargs, read, _keep_r = _read_args(q, read_states, cu, len(lengths), max(lengths), scale, v.dtype,
                                          slots=read_slots)
     # one call: the read of the incoming snapshot overlaps the update's state scan

@@ -209,9 +209,9 @@ def test_update_read_matches_separate_calls(cuda):
     o, fin = ops.gdn2_chunked(q, k, v, g, beta, h0, cu, w=w, read_states=rs, max_seqlen=300)
     torch.cuda.synchronize()
     assert torch.equal(o, o_ref) and torch.equal(fin, o_ref_fin)
-    # read of the state the update writes: in order on the caller's stream
+    # read of the states the update writes (an in-place update): in order, the read first
     lib = _lib.load()
-    final = torch.empty_like(h0)
+    final = rs.clone()
     uargs_lib, uargs, ws, out, keep_u = ops._update_args(k, v, g, h0, cu, N, L, beta, None, w, 2048, final)
     _, rargs, o2, keep_r = ops._read_args(q, final, cu, N, 300, 128 ** -0.5, bf)
     st = lib.memt_gdn2_update_read(ctypes.byref(uargs), ops._ptr(ws), ws.numel(), ctypes.byref(rargs),
@@ -219,7 +219,7 @@ def test_update_read_matches_separate_calls(cuda):
     assert st == 0
     torch.cuda.synchronize()
     assert torch.equal(final, o_ref_fin)
-    assert torch.equal(o2, ops._read(q, o_ref_fin, cu, N, 300, 128 ** -0.5, bf))
+    assert torch.equal(o2, o_ref)  # the incoming snapshot rs, not the updated state
 
 
 def test_reads_from_a_state_pool(cuda):
@@ -260,6 +260,31 @@ def test_reads_from_a_state_pool(cuda):
     torch.cuda.synchronize()
     assert torch.equal(out[1], torch.full_like(out[1], 7.0))
     assert torch.equal(out[0], ref[0]) and torch.equal(out[2], ref[2])
+
+
+def test_update_in_a_state_pool(cuda):
+    """The update reading its initial states from and writing its final states into a state
+    pool by slot index (in place, no gather and no index_copy_) equals the gathered update;
+    slots not named stay untouched, and the read of the same pool sees the incoming states."""
+    bf = torch.bfloat16
+    H, D, S = 4, 128, 9
+    x = to_bf16(make_inputs(13, [500, 64, 333], H, D, gate="channel", beta=None, erase=False, write=True))
+    gen = torch.Generator(device=cuda).manual_seed(4)
+    pool = 0.05 * torch.randn(S, H, D, D, device=cuda, generator=gen)
+    slots = torch.tensor([6, 0, 3], dtype=torch.int32, device=cuda)
+    before = pool.clone()
+    gathered = pool[slots.long()].contiguous()
+    q, k, v = (_t(x[n], cuda, bf)[None] for n in ("q", "k", "v"))
+    g, w = _t(x["g"], cuda)[None], _t(x["w"], cuda, bf)[None]
+    args = dict(lengths=x["lengths"], scale=D ** -0.5, chunk_tokens=2048)
+    r_ref, f_ref = M.token_memory_packed(q, k, v, g, w, gathered, gathered.clone(), **args)
+    r_got, pool_out = M.token_memory_packed(q, k, v, g, w, pool, pool, read_slots=slots, write_slots=slots, **args)
+    torch.cuda.synchronize()
+    assert pool_out.data_ptr() == pool.data_ptr()
+    assert torch.equal(r_got, r_ref)
+    assert torch.equal(pool[slots.long()], f_ref)
+    others = [i for i in range(S) if i not in (6, 0, 3)]
+    assert torch.equal(pool[others], before[others])
 
 
 def test_update_partial_chunk_ignores_next_sample(cuda):
