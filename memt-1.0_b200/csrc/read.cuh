@@ -59,8 +59,10 @@ struct GemvCfg {
   static constexpr int kBatches = kPer / kBatch;
 };
 
+// one-token (decode) CTAs at three per SM, so that one CTA's reduction and epilogue overlap
+// two others' state streams
 template <int D, int TQ, bool EXACT>
-__global__ void __launch_bounds__(256, 2) read_gemv_kernel(ReadParams p) {
+__global__ void __launch_bounds__(256, (TQ == 1 && D <= 128) ? 3 : 2) read_gemv_kernel(ReadParams p) {
   using Cfg = GemvCfg<D>;
   constexpr int RPP = Cfg::kRPP, TPR = Cfg::kTPR, BATCH = Cfg::kBatch;
   __shared__ float s_q[TQ][D];
