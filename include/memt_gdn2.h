@@ -72,8 +72,18 @@ typedef struct CUstream_st *memt_stream_t;
 #define MEMT_GATE_PER_HEAD 1
 #define MEMT_GATE_PER_CHANNEL 2
 
-/* Library version (major*10000 + minor*100 + patch). */
-int memt_version(void);  /* 200 (0.2.0): state pools by slot index (fields appended to the update, read and readout args) */
+/* Library version (major*10000 + minor*100 + patch).
+ *   0.2.0  state pools by slot index (fields appended to the update, read and readout args)
+ *   0.3.0  every argument struct starts with struct_size; the Qwen memory-block prologue;
+ *          memt_gdn2_noalloc_status */
+int memt_version(void);  /* 300 */
+
+/* Argument structs start with `uint32_t struct_size`, which the caller sets to
+ * sizeof(the struct) as declared in this header (MEMT_ARGS_INIT does it). An entry point
+ * returns MEMT_ERR_INVALID_ARGUMENT and launches nothing when struct_size is not the size this
+ * library was built with, so a binding written against another version of a struct cannot
+ * make the library read fields the caller never set. */
+#define MEMT_ARGS_INIT(type) {(uint32_t)sizeof(type)}
 
 /* Human-readable name of a status code. */
 const char *memt_status_string(int status);
@@ -107,6 +117,7 @@ int64_t memt_gdn2_count_chunks(const int32_t *cu_seqlens_host, int32_t num_sampl
  * initial_state may alias final_state (in-place update).
  */
 typedef struct memt_gdn2_update_args {
+  uint32_t struct_size;    /* sizeof(memt_gdn2_update_args)                     */
   int32_t num_samples;     /* N >= 1                                            */
   int32_t num_heads;       /* H >= 1                                            */
   int32_t key_dim;         /* K: 64, 128 or 256                                 */
@@ -133,7 +144,7 @@ typedef struct memt_gdn2_update_args {
    * ends in final_state[final_slots[n]] of a pool [num_final_slots,H,K,V] (the two pools may
    * be one tensor; distinct samples need distinct final slots). An input slot outside its
    * pool starts from a zero state, an output slot outside its pool is not written; both set
-   * bit 3 of the workspace status word (bf16 update). Appended in version 0.2.0. */
+   * bit 3 of the workspace status word (bf16 update). */
   const int32_t *initial_slots;
   int32_t num_initial_slots;
   const int32_t *final_slots;
@@ -174,6 +185,11 @@ int memt_gdn2_update(const memt_gdn2_update_args *args, void *workspace, size_t 
 #define MEMT_NOALLOC_SCRATCH_BYTES (64u << 20)
 int memt_gdn2_update_noalloc(const memt_gdn2_update_args *args, memt_stream_t stream);
 
+/* Status word the last memt_gdn2_update_noalloc on the current device left in the static
+ * scratch (the bits of memt_gdn2_workspace_status), for callers that never see the scratch's
+ * address. Synchronises the stream; intended for tests and debugging. */
+int memt_gdn2_noalloc_status(memt_stream_t stream, int32_t *status_out);
+
 /* Device status word the last update left in this workspace (0 = clean; bit 0: a sample
  * had negative length or offsets outside [0, L]; bit 1: chunk table overflow; bit 2: a copy
  * wait timed out; bit 3: a state slot outside its pool). Reading it
@@ -190,12 +206,15 @@ int memt_gdn2_workspace_status(const void *workspace, memt_stream_t stream, int3
  * fp32 (the reference's rounding); F32: exact fp32.
  */
 typedef struct memt_gdn2_read_args {
+  uint32_t struct_size;    /* sizeof(memt_gdn2_read_args)                       */
   int32_t num_blocks;      /* number of snapshots / token blocks                */
   int32_t num_heads;
   int32_t key_dim;         /* 64, 128, 256                                      */
   int32_t value_dim;       /* equal to key_dim                                  */
   int64_t total_tokens;    /* L                                                 */
-  int32_t max_block_tokens;/* host bound on tokens per block (selects the kernel); 0 = L */
+  int32_t max_block_tokens;/* bound on tokens per block that sizes the grid and selects the
+                              kernel; 0 = L. A bound below the longest block costs speed,
+                              not tokens: the kernels walk every tile of a block */
   const int32_t *cu_seqlens; /* device [num_blocks+1]                           */
   const void *q;           /* [L,H,K]                                           */
   int32_t q_dtype;         /* MEMT_BF16 or MEMT_F32                             */
@@ -224,7 +243,9 @@ int memt_gdn2_read(const memt_gdn2_read_args *args, memt_stream_t stream);
  * scan, so everything issued to it afterwards sees both results. When the read's states
  * overlap the update's final_state (for example one state pool read and updated in place),
  * or for the fp32 (exact recurrence) update, the two run in order on the caller's stream
- * instead, the read first: it reads the incoming snapshot. */
+ * instead, the read first: it reads the incoming snapshot.
+ * The library-owned stream is one per device, shared by all callers: scans issued from
+ * different caller streams of one device run one after another on it. */
 int memt_gdn2_update_read(const memt_gdn2_update_args *update, void *workspace, size_t workspace_bytes,
                           const memt_gdn2_read_args *read, memt_stream_t stream);
 
@@ -240,11 +261,12 @@ int memt_gdn2_update_read(const memt_gdn2_update_args *update, void *workspace, 
  * All activations bf16. residual may alias out (in-place add into the attention output).
  */
 typedef struct memt_memory_readout_args {
+  uint32_t struct_size;    /* sizeof(memt_memory_readout_args)                  */
   int32_t num_blocks;
   int32_t num_heads;       /* heads read by this call                           */
   int32_t head_dim;        /* 64, 128, 256                                      */
   int64_t total_tokens;
-  int32_t max_block_tokens;/* host bound on tokens per block; 0 = L             */
+  int32_t max_block_tokens;/* bound on tokens per block (as in memt_gdn2_read_args); 0 = L */
   const int32_t *cu_seqlens; /* device [num_blocks+1]                           */
   const void *q;           /* bf16 [L,H,D]                                      */
   int32_t normalize_q;     /* 1: apply l2norm to q first                        */
@@ -265,15 +287,52 @@ typedef struct memt_memory_readout_args {
 
 int memt_memory_readout(const memt_memory_readout_args *args, memt_stream_t stream);
 
+/* ---- Qwen memory-block prologue -----------------------------------------
+ *
+ * Replaces what QwenMemoryBlock.packed computes between its input projection and
+ * token_memory_packed (models/qwen/layer.py:71-97): _write_gates (erase and write gates),
+ * _log_decay (softplus decay) and _symmetric_inputs (the FLA Triton l2norm of q and k,
+ * _vendor/fla/modules/l2norm.py:84-109, and the sqrt-erase fold into the key). For every token
+ * t, head h and channel c, in fp32 with the reference's rounding points:
+ *   q_out[t,h,:]     = bf16(q / sqrt(sum q^2 + eps))
+ *   k_out[t,h,c]     = bf16(bf16(exp(0.5 logsigmoid(erase[t,h,c]))) * bf16(k / sqrt(sum k^2 + eps)))
+ *   write_out[t,h,c] = bf16(sigmoid(write[t,h,c]))
+ *   log_decay_out[t,h,c] = -exp(decay_scale_log[h]) * softplus(decay[t,h,c] + decay_bias[h*D+c])
+ * The reference then passes erase = ones to the update; with these outputs the update is
+ * called with no erase factor (erase NULL), which is the same computation.
+ * The bf16 inputs are token rows of *_stride elements (>= H*D, a multiple of 8), head h at
+ * column h*D, so the q/k/v and gate projections' split views need no copy. Outputs are
+ * contiguous [L, H, D]. */
+typedef struct memt_qwen_prologue_args {
+  uint32_t struct_size;    /* sizeof(memt_qwen_prologue_args)                   */
+  int32_t num_heads;       /* H                                                 */
+  int32_t head_dim;        /* D: 64, 128 or 256                                 */
+  int64_t total_tokens;    /* L                                                 */
+  const void *q;            int64_t q_stride;      /* bf16 query projection      */
+  const void *k;            int64_t k_stride;      /* bf16 key projection        */
+  const void *erase_latent; int64_t erase_stride;  /* bf16 erase-gate pre-activation (write_gates[0]) */
+  const void *write_latent; int64_t write_stride;  /* bf16 write-gate pre-activation (write_gates[1]) */
+  const void *decay_latent; int64_t decay_stride;  /* bf16 f_down(decay latent), [L, H*D] */
+  const void *decay_bias;       /* bf16 [H*D]                                    */
+  const void *decay_scale_log;  /* bf16 [H]                                      */
+  float eps;                    /* l2norm epsilon (1e-6 in the reference)        */
+  void *q_out;                  /* bf16 [L,H,D]                                  */
+  void *k_out;                  /* bf16 [L,H,D]                                  */
+  void *write_out;              /* bf16 [L,H,D]                                  */
+  float *log_decay_out;         /* fp32 [L,H,D]                                  */
+} memt_qwen_prologue_args;
+
+int memt_qwen_prologue(const memt_qwen_prologue_args *args, memt_stream_t stream);
+
 /* ---- kernel timing (benchmarks) ----------------------------------------
  *
  * No counterpart in the reference (its kernels are timed from Python). When enabled,
  * every kernel this library launches is bracketed by CUDA events on its own stream and
  * its device time is accumulated per kernel family; disabled (the default) it costs
  * nothing. Families: 0 plan, 1 intra (WY operands), 2 scan, 3 read (GEMV),
- * 4 read (tensor-core tiles), 5 fp32 recurrence.
+ * 4 read (tensor-core tiles), 5 fp32 recurrence, 6 Qwen prologue.
  */
-#define MEMT_PROF_FAMILIES 6
+#define MEMT_PROF_FAMILIES 7
 int memt_profiler_enable(int on);
 int memt_profiler_reset(void);
 /* Synchronises the recorded events, then fills ms[i] (total device milliseconds) and

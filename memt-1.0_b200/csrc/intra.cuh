@@ -68,9 +68,12 @@ struct IntraCfg {
   static constexpr size_t offA = offEi + kBytesE;
   static constexpr size_t offAi = offA + kBytesA;
   // per-head decay without erase, D <= 128: k, v and write tiles arrive by TMA (the tiles need
-  // the 1024-byte aligned base of the 128-byte swizzle: slack for aligning the dynamic base)
+  // the 1024-byte aligned base of the 128-byte swizzle). Every configuration rounds the dynamic
+  // base up to 1024 bytes itself (the slack below): the kernel also declares static shared
+  // arrays, and where the dynamic region starts after them is the toolchain's choice (a build
+  // with relocatable device code started it at an address that broke 16-byte accesses).
   static constexpr bool kTma = HEAD && !ERASE && kPanels == 1;
-  static constexpr size_t kSmem = offAi + kBytesAi + (kTma ? 1024 : 0);
+  static constexpr size_t kSmem = offAi + kBytesAi + 1024;
   static constexpr int kSmall = 9 * kTile + kThreads;  // static per-head factors + scan totals
 };
 
@@ -1385,8 +1388,7 @@ __global__ void __launch_bounds__(256, 2) intra_kernel(const __grid_constant__ I
   extern __shared__ __align__(1024) unsigned char smem_intra[];
   using Cfg = IntraCfg<D, HEAD, ERASE>;
   IntraKernel<D, HEAD, ERASE> k;
-  unsigned char* base = smem_intra;
-  if constexpr (Cfg::kTma) base += (1024u - (smem_u32(smem_intra) & 1023u)) & 1023u;
+  unsigned char* base = smem_intra + ((1024u - (smem_u32(smem_intra) & 1023u)) & 1023u);
   k.sK = reinterpret_cast<__nv_bfloat16*>(base + Cfg::offK);
   k.sB = reinterpret_cast<__nv_bfloat16*>(base + Cfg::offB);
   k.sV = reinterpret_cast<__nv_bfloat16*>(base + Cfg::offV);

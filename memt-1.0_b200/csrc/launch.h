@@ -37,7 +37,7 @@ cudaError_t ensure_smem(Kernel kernel, size_t bytes) {
 
 // Optional per-launch CUDA-event timing (memt_profiler_*). Usage around a launch:
 //   ProfScope prof(kProfIntra, stream);  kernel<<<...>>>(...);
-enum ProfFamily { kProfPlan = 0, kProfIntra, kProfScan, kProfReadGemv, kProfReadTile, kProfRecurrent };
+enum ProfFamily { kProfPlan = 0, kProfIntra, kProfScan, kProfReadGemv, kProfReadTile, kProfRecurrent, kProfPrologue };
 void prof_begin(int family, cudaStream_t s, void** token);
 void prof_end(void* token, cudaStream_t s);
 struct ProfScope {

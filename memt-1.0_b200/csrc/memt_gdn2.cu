@@ -59,7 +59,7 @@ WsLayout ws_layout(int32_t N, int64_t L, int32_t H, int32_t K, int32_t V, int32_
 bool dim_ok(int32_t d) { return d == 64 || d == 128 || d == 256; }
 
 int check_update(const memt_gdn2_update_args* a) {
-  if (a == nullptr) return MEMT_ERR_INVALID_ARGUMENT;
+  if (a == nullptr || a->struct_size != sizeof(memt_gdn2_update_args)) return MEMT_ERR_INVALID_ARGUMENT;
   if (a->num_samples < 1 || a->num_heads < 1 || a->total_tokens < 0 || a->total_tokens > INT32_MAX - 1 ||
       a->chunk_tokens < 1)
     return MEMT_ERR_INVALID_ARGUMENT;
@@ -166,6 +166,30 @@ int scan_stream(cudaStream_t* out) {
   return MEMT_OK;
 }
 
+// The fork/join event pair of memt_gdn2_update_read, created once per (host thread, device)
+// and reused by every later call of that thread on that device. Per thread, because an event
+// re-recorded by another thread between this thread's record and its wait would make the wait
+// follow the other thread's stream. The events live until the process exits.
+int fork_join_events(cudaEvent_t* fork, cudaEvent_t* join) {
+  thread_local cudaEvent_t events[64][2] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e);
+  if (dev < 0 || dev >= 64) return MEMT_ERR_UNSUPPORTED;
+  for (int i = 0; i < 2; ++i) {
+    if (events[dev][i] == nullptr) {
+      e = cudaEventCreateWithFlags(&events[dev][i], cudaEventDisableTiming);
+      if (e != cudaSuccess) {
+        events[dev][i] = nullptr;
+        return cuda_status(e);
+      }
+    }
+  }
+  *fork = events[dev][0];
+  *join = events[dev][1];
+  return MEMT_OK;
+}
+
 bool ranges_overlap(const void* a, size_t na, const void* b, size_t nb) {
   const uintptr_t x = reinterpret_cast<uintptr_t>(a), y = reinterpret_cast<uintptr_t>(b);
   return x < y + nb && y < x + na;
@@ -195,7 +219,8 @@ int update_f32(const memt_gdn2_update_args* a, cudaStream_t s) {
 }
 
 int check_read(const memt_gdn2_read_args* a) {
-  if (a == nullptr || a->num_blocks < 1 || a->num_heads < 1 || a->total_tokens < 0 ||
+  if (a == nullptr || a->struct_size != sizeof(memt_gdn2_read_args)) return MEMT_ERR_INVALID_ARGUMENT;
+  if (a->num_blocks < 1 || a->num_heads < 1 || a->total_tokens < 0 ||
       a->cu_seqlens == nullptr || a->q == nullptr || a->states == nullptr || a->out == nullptr)
     return MEMT_ERR_INVALID_ARGUMENT;
   if (!dim_ok(a->key_dim) || a->value_dim != a->key_dim) return MEMT_ERR_UNSUPPORTED;
@@ -229,7 +254,7 @@ int read_launch(const memt_gdn2_read_args* a, memt_stream_t stream) {
 
 extern "C" {
 
-int memt_version(void) { return 200; }
+int memt_version(void) { return 300; }
 
 const char* memt_status_string(int status) {
   switch (status) {
@@ -318,15 +343,14 @@ int memt_gdn2_update_read(const memt_gdn2_update_args* u, void* workspace, size_
     return MEMT_ERR_WORKSPACE;
   cudaStream_t side = nullptr;
   st = scan_stream(&side);
+  cudaEvent_t fork = nullptr, join = nullptr;
+  if (st == MEMT_OK) st = fork_join_events(&fork, &join);
   if (st != MEMT_OK) return st;
   ScanParams sp;
   st = update_bf16_front(u, workspace, s, &sp);
   if (st != MEMT_OK) return st;
   // fork after the intra kernel: the scan on the high-priority stream, the read on the caller's
-  cudaEvent_t fork = nullptr, join = nullptr;
-  cudaError_t e = cudaEventCreateWithFlags(&fork, cudaEventDisableTiming);
-  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&join, cudaEventDisableTiming);
-  if (e == cudaSuccess) e = cudaEventRecord(fork, s);
+  cudaError_t e = cudaEventRecord(fork, s);
   if (e == cudaSuccess) e = cudaStreamWaitEvent(side, fork, 0);
   if (e == cudaSuccess) {
     st = launch_scan(u->key_dim, sp, side);
@@ -335,14 +359,13 @@ int memt_gdn2_update_read(const memt_gdn2_update_args* u, void* workspace, size_
     if (e == cudaSuccess) e = cudaStreamWaitEvent(s, join, 0);
     if (st == MEMT_OK) st = st_read;
   }
-  if (fork != nullptr) cudaEventDestroy(fork);
-  if (join != nullptr) cudaEventDestroy(join);
   if (e != cudaSuccess) return cuda_status(e);
   return st;
 }
 
 int memt_memory_readout(const memt_memory_readout_args* a, memt_stream_t stream) {
-  if (a == nullptr || a->num_blocks < 1 || a->num_heads < 1 || a->total_tokens < 0 || a->head_offset < 0 ||
+  if (a == nullptr || a->struct_size != sizeof(memt_memory_readout_args)) return MEMT_ERR_INVALID_ARGUMENT;
+  if (a->num_blocks < 1 || a->num_heads < 1 || a->total_tokens < 0 || a->head_offset < 0 ||
       a->cu_seqlens == nullptr || a->q == nullptr || a->states == nullptr || a->gate == nullptr ||
       a->norm_weight == nullptr || a->out == nullptr)
     return MEMT_ERR_INVALID_ARGUMENT;

@@ -38,7 +38,7 @@ int scratch_address(void** out) {
 }  // namespace
 
 extern "C" int memt_gdn2_update_noalloc(const memt_gdn2_update_args* args, memt_stream_t stream) {
-  if (args == nullptr) return MEMT_ERR_INVALID_ARGUMENT;
+  if (args == nullptr || args->struct_size != sizeof(memt_gdn2_update_args)) return MEMT_ERR_INVALID_ARGUMENT;
   const size_t need = memt_gdn2_update_workspace_size(args->num_samples, args->total_tokens, args->num_heads,
                                                       args->key_dim, args->value_dim, args->chunk_tokens,
                                                       args->dtype);
@@ -48,4 +48,14 @@ extern "C" int memt_gdn2_update_noalloc(const memt_gdn2_update_args* args, memt_
   if (st != MEMT_OK) return st;
   // Same kernels and argument checks as the allocating entry point.
   return memt_gdn2_update(args, scratch, MEMT_NOALLOC_SCRATCH_BYTES, stream);
+}
+
+// The status word the last memt_gdn2_update_noalloc on this device left at the start of the
+// static scratch; the same word memt_gdn2_workspace_status reads from a caller's workspace.
+extern "C" int memt_gdn2_noalloc_status(memt_stream_t stream, int32_t* status_out) {
+  if (status_out == nullptr) return MEMT_ERR_INVALID_ARGUMENT;
+  void* scratch = nullptr;
+  const int st = scratch_address(&scratch);
+  if (st != MEMT_OK) return st;
+  return memt_gdn2_workspace_status(scratch, stream, status_out);
 }

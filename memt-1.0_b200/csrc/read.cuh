@@ -25,6 +25,22 @@ __device__ __forceinline__ void block_range(const ReadParams& p, int n, int64_t&
   eos = b < bos ? bos : (b > p.L ? p.L : b);
 }
 
+// Tiles of a block owned by the CTA with blockIdx.y = y: runs of `per` consecutive tiles,
+// run y, y + gridDim.y, ...; strided_tile_index(i) is the block-relative index of the CTA's
+// i-th tile and strided_tiles the number of them for a block of `len` tokens.
+__device__ __forceinline__ int64_t strided_tile_index(int i, int per) {
+  return ((int64_t)blockIdx.y + (int64_t)(i / per) * gridDim.y) * per + i % per;
+}
+__device__ __forceinline__ int strided_tiles(int64_t len, int tok, int per) {
+  const int64_t total = (len + tok - 1) / tok;
+  int64_t count = 0;
+  for (int64_t run = blockIdx.y; run * per < total; run += gridDim.y) {
+    const int64_t left = total - run * per;
+    count += left < per ? left : per;
+  }
+  return (int)count;
+}
+
 // snapshot of block n: n itself, or slots[n] when the caller passes slot indices into a state
 // pool; -1 for an index outside the pool (the block is skipped and its outputs left unwritten)
 __device__ __forceinline__ int64_t state_slot(const ReadParams& p, int n) {
@@ -61,22 +77,14 @@ struct GemvCfg {
 
 // one-token (decode) CTAs at three per SM, so that one CTA's reduction and epilogue overlap
 // two others' state streams
+// one group of up to TQ tokens [t0, t0 + nt) of head h reading snapshot `slot`; every thread
+// of the CTA calls it (it synchronises the CTA)
 template <int D, int TQ, bool EXACT>
-__global__ void __launch_bounds__(256, (TQ == 1 && D <= 128) ? 3 : 2) read_gemv_kernel(ReadParams p) {
+__device__ __forceinline__ void gemv_group(const ReadParams& p, int h, int64_t slot, int64_t t0, int nt,
+                                           float (*s_q)[D], float (*s_red)[TQ][D], float (*s_ss)[8]) {
   using Cfg = GemvCfg<D>;
   constexpr int RPP = Cfg::kRPP, TPR = Cfg::kTPR, BATCH = Cfg::kBatch;
-  __shared__ float s_q[TQ][D];
-  __shared__ float s_red[RPP][TQ][D];
-  __shared__ float s_ss[TQ][8];
   const int tid = threadIdx.x;
-  const int n = blockIdx.x / p.H, h = blockIdx.x % p.H;
-  int64_t bos, eos;
-  block_range(p, n, bos, eos);
-  const int64_t t0 = bos + (int64_t)blockIdx.y * TQ;
-  if (t0 >= eos) return;
-  const int64_t slot = state_slot(p, n);
-  if (slot < 0) return;
-  const int nt = (int)((eos - t0) < TQ ? (eos - t0) : TQ);
   const int64_t qrow = (int64_t)p.H * D;
 
   // 1. state stream: first batch in flight before anything else
@@ -221,6 +229,30 @@ __global__ void __launch_bounds__(256, (TQ == 1 && D <= 128) ? 3 : 2) read_gemv_
   }
 }
 
+// CTA (block, head, y): token groups y, y + gridDim.y, ... of the block, so that every token is
+// read whatever bound on the block length the host sized the grid with
+template <int D, int TQ, bool EXACT>
+__global__ void __launch_bounds__(256, (TQ == 1 && D <= 128) ? 3 : 2) read_gemv_kernel(ReadParams p) {
+  using Cfg = GemvCfg<D>;
+  __shared__ float s_q[TQ][D];
+  __shared__ float s_red[Cfg::kRPP][TQ][D];
+  __shared__ float s_ss[TQ][8];
+  const int n = blockIdx.x / p.H, h = blockIdx.x % p.H;
+  int64_t bos, eos;
+  block_range(p, n, bos, eos);
+  int64_t t0 = bos + (int64_t)blockIdx.y * TQ;
+  if (t0 >= eos) return;
+  const int64_t slot = state_slot(p, n);
+  if (slot < 0) return;
+  for (;;) {
+    const int nt = (int)((eos - t0) < TQ ? (eos - t0) : TQ);
+    gemv_group<D, TQ, EXACT>(p, h, slot, t0, nt, s_q, s_red, s_ss);
+    t0 += (int64_t)gridDim.y * TQ;
+    if (t0 >= eos) break;
+    __syncthreads();  // the shared buffers are reused by the next group
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Tile kernel: CTA = (block, head, run of up to kTilesPerCta 64-token tiles).
 // bf16 state panel [D][D] (swizzled) resident in shared memory; warps split rows
@@ -235,7 +267,8 @@ struct ReadTileCfg {
   static constexpr int kNT = D / 8 / kColSplit;  // n-tiles per warp
   static constexpr size_t kBytesS = size_t(D) * D * 2;
   static constexpr size_t kBytesQ = size_t(kTile) * D * 2;
-  static constexpr size_t kSmem = kBytesS + 2 * kBytesQ + 4 * 16 * 2 * 4;
+  // + slack: the kernel rounds the dynamic base up to 128 bytes itself
+  static constexpr size_t kSmem = kBytesS + 2 * kBytesQ + 4 * 16 * 2 * 4 + 128;
 };
 
 template <int RL>
@@ -247,7 +280,7 @@ template <int D>
 __global__ void __launch_bounds__(ReadTileCfg<D>::kNW * 32) read_tile_kernel(ReadParams p) {
   using Cfg = ReadTileCfg<D>;
   extern __shared__ __align__(128) unsigned char smem_read[];
-  unsigned char* smem = smem_read;
+  unsigned char* smem = smem_read + ((128u - (smem_u32(smem_read) & 127u)) & 127u);
   __nv_bfloat16* sS = reinterpret_cast<__nv_bfloat16*>(smem);
   __nv_bfloat16* sQ[2] = {reinterpret_cast<__nv_bfloat16*>(smem + Cfg::kBytesS),
                           reinterpret_cast<__nv_bfloat16*>(smem + Cfg::kBytesS + Cfg::kBytesQ)};
@@ -258,17 +291,18 @@ __global__ void __launch_bounds__(ReadTileCfg<D>::kNW * 32) read_tile_kernel(Rea
   const int n = blockIdx.x / p.H, h = blockIdx.x % p.H;
   int64_t bos, eos;
   block_range(p, n, bos, eos);
-  const int64_t first = bos + (int64_t)blockIdx.y * kReadTilesPerCta * kTile;
-  if (first >= eos) return;
+  // this CTA's tiles: runs y, y + gridDim.y, ... of kReadTilesPerCta tiles, so that every token
+  // is read whatever bound on the block length the host sized the grid with
+  const int ntiles = strided_tiles(eos - bos, kTile, kReadTilesPerCta);
+  if (ntiles == 0) return;
   const int64_t slot = state_slot(p, n);
   if (slot < 0) return;
-  int ntiles = (int)((eos - first + kTile - 1) / kTile);
-  if (ntiles > kReadTilesPerCta) ntiles = kReadTilesPerCta;
+  auto tile_start = [&](int i) { return bos + strided_tile_index(i, kReadTilesPerCta) * kTile; };
   const int64_t qrow = (int64_t)p.H * D;
   const __nv_bfloat16* q = static_cast<const __nv_bfloat16*>(p.q);
 
   auto load_q = [&](int tile, int buf) {
-    const int64_t tb = first + (int64_t)tile * kTile;
+    const int64_t tb = tile_start(tile);
     for (int i = tid; i < kTile * D / 8; i += NT) {
       const int row = i / (D / 8), col = (i % (D / 8)) * 8;
       const bool valid = tb + row < eos;
@@ -330,7 +364,7 @@ __global__ void __launch_bounds__(ReadTileCfg<D>::kNW * 32) read_tile_kernel(Rea
         mma_bf16_16816(acc[np + 1], a, b1);
       }
     }
-    const int64_t tb = first + (int64_t)tile * kTile;
+    const int64_t tb = tile_start(tile);
     const int64_t r0 = tb + 16 * rb + g, r1 = r0 + 8;
     const bool ok0 = r0 < eos, ok1 = r1 < eos;
     if (!p.fused) {

@@ -60,14 +60,15 @@ __global__ void __launch_bounds__(ReadTcCfg::kThreads, 2) read_tc_kernel(const _
   const int n = blockIdx.x / p.H, h = blockIdx.x % p.H;
   int64_t bos, eos;
   block_range(p, n, bos, eos);
-  const int64_t first = bos + (int64_t)blockIdx.y * kReadTcTiles * Cfg::kTok;
-  if (first >= eos) return;
+  // this CTA's tiles: runs y, y + gridDim.y, ... of kReadTcTiles tiles, so that every token is
+  // read whatever bound on the block length the host sized the grid with
+  const int ntiles = strided_tiles(eos - bos, Cfg::kTok, kReadTcTiles);
+  if (ntiles == 0) return;
   const int64_t slot = state_slot(p, n);
   if (slot < 0) return;
-  int ntiles = (int)((eos - first + Cfg::kTok - 1) / Cfg::kTok);
-  if (ntiles > kReadTcTiles) ntiles = kReadTcTiles;
   const bool tma_out = p.out_bf16 != 0;
-  auto full_tile = [&](int i) { return first + (int64_t)(i + 1) * Cfg::kTok <= eos; };
+  auto tile_start = [&](int i) { return bos + strided_tile_index(i, kReadTcTiles) * Cfg::kTok; };
+  auto full_tile = [&](int i) { return tile_start(i) + Cfg::kTok <= eos; };
 
   // barriers: [0, NS) stage holds the query tile (TMA); [QF, QF + NA) accumulator full
   // (commit); [AE, AE + NA) accumulator drained; SR snapshot operand written; [OR, OR + NS)
@@ -102,7 +103,7 @@ __global__ void __launch_bounds__(ReadTcCfg::kThreads, 2) read_tc_kernel(const _
       // the control thread never waits for a store's read of shared memory.
       auto load_q = [&](int i) {
         const int s = i % NS;
-        const int y = static_cast<int>(first + (int64_t)i * Cfg::kTok);
+        const int y = static_cast<int>(tile_start(i));
         mbar_expect_tx(B(s), Cfg::kBytesQ);
         tma_load_2d(sQ + s * Cfg::kBytesQ, &P.q_map, h * D, y, B(s));
         tma_load_2d(sQ + s * Cfg::kBytesQ + Cfg::kBytesBox, &P.q_map, h * D + 64, y, B(s));
@@ -115,7 +116,7 @@ __global__ void __launch_bounds__(ReadTcCfg::kThreads, 2) read_tc_kernel(const _
         wait(OR + s, (i / NS) & 1);
         if (tma_out && full_tile(i)) {
           fence_proxy_async_smem();
-          const int y = static_cast<int>(first + (int64_t)i * Cfg::kTok);
+          const int y = static_cast<int>(tile_start(i));
           tma_store_2d(&P.o_map, h * D, y, sQ + s * Cfg::kBytesQ);
           tma_store_2d(&P.o_map, h * D + 64, y, sQ + s * Cfg::kBytesQ + Cfg::kBytesBox);
         }
@@ -183,7 +184,7 @@ __global__ void __launch_bounds__(ReadTcCfg::kThreads, 2) read_tc_kernel(const _
       tc::fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(B(AE + a));  // the accumulator may be overwritten
-      const int64_t tok = first + (int64_t)i * Cfg::kTok + r;
+      const int64_t tok = tile_start(i) + r;
       if (lane < 16) {
         if (tma_out && full_tile(i)) {
           // output tile in the box layout of the TMA store: value panel `half`, row r

@@ -29,7 +29,8 @@ struct ScanCfg {
   static constexpr uint32_t kBytesStage = 2 * kBytesWK + kBytesU + kBytesEl;
   static constexpr uint32_t kBytesSb = uint32_t(D) * BV * 2;
   static constexpr uint32_t kBytesVn = uint32_t(kTile) * BV * 2;
-  static constexpr size_t kSmem = 2 * size_t(kBytesStage) + kBytesSb + kBytesVn + 64;
+  // + slack: the kernel rounds the dynamic base up to 128 bytes itself
+  static constexpr size_t kSmem = 2 * size_t(kBytesStage) + kBytesSb + kBytesVn + 64 + 128;
   static_assert(kXNT % 2 == 0 && kXNT >= 2, "value tiles per warp");
 };
 
@@ -37,7 +38,8 @@ template <int D>
 __global__ void __launch_bounds__(ScanCfg<D>::kThreads) scan_kernel(ScanParams p) {
   using Cfg = ScanCfg<D>;
   constexpr int BV = Cfg::BV;
-  extern __shared__ __align__(128) unsigned char smem_scan[];
+  extern __shared__ __align__(128) unsigned char smem_scan_raw[];
+  unsigned char* smem_scan = smem_scan_raw + ((128u - (smem_u32(smem_scan_raw) & 127u)) & 127u);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
   constexpr int NV = D / BV;

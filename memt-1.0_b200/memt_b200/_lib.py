@@ -7,7 +7,7 @@ importing an operator without the library raises immediately.
 from __future__ import annotations
 
 import ctypes
-from ctypes import POINTER, c_char_p, c_float, c_int, c_int32, c_int64, c_size_t, c_void_p
+from ctypes import POINTER, c_char_p, c_float, c_int, c_int32, c_int64, c_size_t, c_uint32, c_void_p
 from pathlib import Path
 
 LIB_PATH = Path(__file__).with_name("libmemt_gdn2.so")
@@ -27,8 +27,18 @@ GATE_PER_HEAD = 1
 GATE_PER_CHANNEL = 2
 
 
-class UpdateArgs(ctypes.Structure):
+class _SizedArgs(ctypes.Structure):
+    """An argument struct whose leading ``struct_size`` is set to its own size (the library
+    rejects any other value with MEMT_ERR_INVALID_ARGUMENT)."""
+
+    def __init__(self, **fields):
+        fields.setdefault("struct_size", ctypes.sizeof(type(self)))
+        super().__init__(**fields)
+
+
+class UpdateArgs(_SizedArgs):
     _fields_ = [
+        ("struct_size", c_uint32),
         ("num_samples", c_int32), ("num_heads", c_int32), ("key_dim", c_int32), ("value_dim", c_int32),
         ("total_tokens", c_int64), ("chunk_tokens", c_int32), ("dtype", c_int32),
         ("cu_seqlens", c_void_p), ("k", c_void_p), ("v", c_void_p), ("g", c_void_p), ("g_layout", c_int32),
@@ -39,8 +49,9 @@ class UpdateArgs(ctypes.Structure):
     ]
 
 
-class ReadArgs(ctypes.Structure):
+class ReadArgs(_SizedArgs):
     _fields_ = [
+        ("struct_size", c_uint32),
         ("num_blocks", c_int32), ("num_heads", c_int32), ("key_dim", c_int32), ("value_dim", c_int32),
         ("total_tokens", c_int64), ("max_block_tokens", c_int32), ("cu_seqlens", c_void_p),
         ("q", c_void_p), ("q_dtype", c_int32), ("states", c_void_p), ("scale", c_float),
@@ -48,14 +59,27 @@ class ReadArgs(ctypes.Structure):
     ]
 
 
-class ReadoutArgs(ctypes.Structure):
+class ReadoutArgs(_SizedArgs):
     _fields_ = [
+        ("struct_size", c_uint32),
         ("num_blocks", c_int32), ("num_heads", c_int32), ("head_dim", c_int32), ("total_tokens", c_int64),
         ("max_block_tokens", c_int32), ("cu_seqlens", c_void_p), ("q", c_void_p), ("normalize_q", c_int32),
         ("q_eps", c_float), ("states", c_void_p), ("scale", c_float), ("gate", c_void_p),
         ("norm_weight", c_void_p), ("norm_eps", c_float), ("softcap", c_float), ("residual", c_void_p),
         ("out", c_void_p), ("row_stride", c_int64), ("head_offset", c_int32), ("state_slots", c_void_p),
         ("num_slots", c_int32),
+    ]
+
+
+class PrologueArgs(_SizedArgs):
+    _fields_ = [
+        ("struct_size", c_uint32),
+        ("num_heads", c_int32), ("head_dim", c_int32), ("total_tokens", c_int64),
+        ("q", c_void_p), ("q_stride", c_int64), ("k", c_void_p), ("k_stride", c_int64),
+        ("erase_latent", c_void_p), ("erase_stride", c_int64), ("write_latent", c_void_p),
+        ("write_stride", c_int64), ("decay_latent", c_void_p), ("decay_stride", c_int64),
+        ("decay_bias", c_void_p), ("decay_scale_log", c_void_p), ("eps", c_float), ("q_out", c_void_p),
+        ("k_out", c_void_p), ("write_out", c_void_p), ("log_decay_out", c_void_p),
     ]
 
 
@@ -71,13 +95,15 @@ SIGNATURES = {
     "memt_gdn2_read": (c_int, [POINTER(ReadArgs), c_void_p]),
     "memt_gdn2_update_read": (c_int, [POINTER(UpdateArgs), c_void_p, c_size_t, POINTER(ReadArgs), c_void_p]),
     "memt_memory_readout": (c_int, [POINTER(ReadoutArgs), c_void_p]),
+    "memt_qwen_prologue": (c_int, [POINTER(PrologueArgs), c_void_p]),
     "memt_gdn2_update_noalloc": (c_int, [POINTER(UpdateArgs), c_void_p]),
+    "memt_gdn2_noalloc_status": (c_int, [c_void_p, POINTER(c_int32)]),
     "memt_profiler_enable": (c_int, [c_int]),
     "memt_profiler_reset": (c_int, []),
     "memt_profiler_read": (c_int, [POINTER(ctypes.c_double), POINTER(c_int64), c_int]),
 }
 
-PROF_FAMILIES = ["plan", "intra", "scan", "read_gemv", "read_tile", "recurrent"]
+PROF_FAMILIES = ["plan", "intra", "scan", "read_gemv", "read_tile", "recurrent", "prologue"]
 
 
 def profiler_enable(on: bool) -> None:

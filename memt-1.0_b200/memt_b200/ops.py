@@ -9,6 +9,8 @@ Signatures, argument meaning and error behaviour follow the reference plugin
 * ``snapshot_read``        models/deepseek/ops/read.py:6-31
 * ``memory_readout``       l2norm(q) -> read -> MemTRMSNormGated -> residual add
                            (models/qwen/layer.py:15-31,112-131; models/qwen/integration.py:61-64)
+* ``qwen_prologue``        QwenMemoryBlock._write_gates / _log_decay / _symmetric_inputs and their
+                           l2norm (models/qwen/layer.py:71-97)
 * ``gdn2_chunked``         the BASELINE-style (q, k, v, g, beta, initial_state, cu_seqlens)
                            -> (o, final_state) entry over the same kernels.
 
@@ -25,11 +27,11 @@ from collections import OrderedDict
 import torch
 
 from . import _lib
-from .layout import ChunkPlan
+from .layout import ChunkPlan, read_segments
 
 __all__ = [
     "token_memory_packed", "memt_gdn2_read_fwd", "snapshot_read", "memory_readout", "gdn2_chunked",
-    "gdn2_update", "Workspace",
+    "gdn2_update", "qwen_prologue", "Workspace",
 ]
 
 _DTYPE = {torch.bfloat16: _lib.MEMT_BF16, torch.float32: _lib.MEMT_F32}
@@ -268,11 +270,22 @@ def token_memory_packed(q, k, v, log_decay, write, read_states, write_states, *,
 
 
 def memt_gdn2_read_fwd(q, snaps, plan: ChunkPlan, scale, out_dtype):
-    """Read each token from its read-block snapshot (models/qwen/ops/read.py:10-39)."""
+    """Read each token from its read-block snapshot (models/qwen/ops/read.py:10-39).
+
+    ``plan`` is a plan of ``memt_b200.layout`` or the reference's own ``ChunkPlan``: each chunk
+    reads the snapshot ``plan.chunk_block_ids`` names. A reference plan carries no read-block
+    offsets, so its small chunk tables are copied to the host once per call to find them.
+    """
     read_slice = getattr(plan, "read_slice", None)
-    if read_slice is None:
-        raise ValueError("plan must come from memt_b200.layout.build_chunk_plan")
-    out = _read(q, snaps, read_slice, plan.num_block, plan.max_block_tokens, scale, out_dtype)
+    if read_slice is not None:
+        out = _read(q, snaps, read_slice, plan.num_block, plan.max_block_tokens, scale, out_dtype)
+        return out.unsqueeze(0)
+    cu, ids, longest = read_segments(plan)
+    dev = _tokens(q, "q").device
+    cu_t = torch.tensor(cu, dtype=torch.int32).to(dev, non_blocking=True)
+    ids_t = torch.tensor(ids, dtype=torch.int32).to(dev, non_blocking=True)
+    lib, args, out, _keep = _read_args(q, snaps, cu_t, len(ids), max(longest, 1), scale, out_dtype, slots=ids_t)
+    _lib.check(lib.memt_gdn2_read(ctypes.byref(args), _stream(out.device)), "memt_gdn2_read")
     return out.unsqueeze(0)
 
 
@@ -329,6 +342,71 @@ def memory_readout(q, states, lengths, scale, gate, norm_weight, *, eps=1e-6, so
         state_slots=slots.data_ptr() if slots is not None else None, num_slots=num_slots)
     _lib.check(lib.memt_memory_readout(ctypes.byref(args), _stream(q.device)), "memt_memory_readout")
     return out
+
+
+def _token_rows(x, L, H, D, name):
+    """A bf16 CUDA tensor of L token rows holding H heads of D contiguous values ([1, L, H, D],
+    [L, H, D], [1, L, H*D] or [L, H*D], e.g. a split view of a projection output) ->
+    (tensor, elements per token row)."""
+    if x.dim() == 4 and x.shape[0] == 1:
+        x = x[0]
+    elif x.dim() == 3 and tuple(x.shape) != (L, H, D) and tuple(x.shape) == (1, L, H * D):
+        x = x[0]
+    if x.dim() == 3:
+        if tuple(x.shape) != (L, H, D) or x.stride(2) != 1 or x.stride(1) != D:
+            raise ValueError(f"{name}: expected [L, {H}, {D}] with contiguous heads")
+    elif x.dim() == 2:
+        if tuple(x.shape) != (L, H * D) or x.stride(1) != 1:
+            raise ValueError(f"{name}: expected [L, {H * D}] rows")
+    else:
+        raise ValueError(f"{name}: expected token rows of {H} x {D} values")
+    if x.dtype != torch.bfloat16 or not x.is_cuda:
+        raise ValueError(f"{name}: expected a bf16 CUDA tensor")
+    return x, x.stride(0) if L > 1 else H * D
+
+
+def qwen_prologue(q, k, erase_gate, write_gate, decay_latent, decay_bias, decay_scale_log, *, eps=1e-6):
+    """The Qwen memory block's prologue in one kernel: (q_hat, k_scaled, write, log_decay).
+
+    Replaces ``QwenMemoryBlock._write_gates`` / ``_log_decay`` / ``_symmetric_inputs``
+    (models/qwen/layer.py:71-97) including their FLA Triton ``l2norm`` of q and k:
+    q_hat = l2norm(q), k_scaled = bf16(sqrt(sigmoid(erase_gate)) * l2norm(k)),
+    write = sigmoid(write_gate), log_decay = -exp(decay_scale_log) * softplus(decay_latent +
+    decay_bias) (fp32). ``erase_gate`` and ``write_gate`` are the bf16 pre-activations the
+    reference splits out of its gate projection and ``decay_latent`` is ``f_down`` of its
+    decay rows; q, k and the gates may be the projections' split views. The erase factor the
+    update needs afterwards is one, so call ``token_memory_packed`` with ``erase=None``.
+    Outputs are [1, L, H, D] (bf16; log_decay fp32).
+    """
+    q4 = q if q.dim() == 4 else q[None]
+    if q4.dim() != 4:
+        raise ValueError("q: expected [1, L, H, D] or [L, H, D]")
+    _, L, H, D = q4.shape
+    q2, sq = _token_rows(q, L, H, D, "q")
+    k2, sk = _token_rows(k, L, H, D, "k")
+    e2, se = _token_rows(erase_gate, L, H, D, "erase_gate")
+    w2, sw = _token_rows(write_gate, L, H, D, "write_gate")
+    d2, sd = _token_rows(decay_latent, L, H, D, "decay_latent")
+    dev = q2.device
+    if (decay_bias.numel() != H * D or decay_bias.dtype != torch.bfloat16 or decay_bias.device != dev
+            or decay_scale_log.numel() != H or decay_scale_log.dtype != torch.bfloat16
+            or decay_scale_log.device != dev):
+        raise ValueError(f"decay_bias must be bf16 [{H * D}] and decay_scale_log bf16 [{H}] on {dev}")
+    bias = decay_bias.contiguous()
+    scale_log = decay_scale_log.contiguous()
+    q_out = torch.empty(L, H, D, device=dev, dtype=torch.bfloat16)
+    k_out = torch.empty_like(q_out)
+    w_out = torch.empty_like(q_out)
+    g_out = torch.empty(L, H, D, device=dev, dtype=torch.float32)
+    lib = _lib.load()
+    args = _lib.PrologueArgs(
+        num_heads=H, head_dim=D, total_tokens=L, q=q2.data_ptr(), q_stride=sq, k=k2.data_ptr(), k_stride=sk,
+        erase_latent=e2.data_ptr(), erase_stride=se, write_latent=w2.data_ptr(), write_stride=sw,
+        decay_latent=d2.data_ptr(), decay_stride=sd, decay_bias=bias.data_ptr(),
+        decay_scale_log=scale_log.data_ptr(), eps=float(eps), q_out=q_out.data_ptr(), k_out=k_out.data_ptr(),
+        write_out=w_out.data_ptr(), log_decay_out=g_out.data_ptr())
+    _lib.check(lib.memt_qwen_prologue(ctypes.byref(args), _stream(dev)), "memt_qwen_prologue")
+    return q_out[None], k_out[None], w_out[None], g_out[None]
 
 
 def gdn2_chunked(q, k, v, g, beta, initial_state, cu_seqlens, *, w=None, scale=None, read_states=None,

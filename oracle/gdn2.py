@@ -25,6 +25,8 @@ It restates, in numpy, the reference's algorithm for the memory path:
 * ``gated_rms_norm``  w * bf16(x rsqrt(mean x^2 + eps)) * L tanh(SiLU(gate)/L)
                       (models/qwen/layer.py:15-31).
 * ``l2norm``          x / sqrt(sum x^2 + eps)   (_vendor/fla/modules/l2norm.py:95-109).
+* ``qwen_gates``, ``qwen_prologue``  gates, decay and the symmetric q/k inputs of the Qwen
+                      memory block (models/qwen/layer.py:71-97).
 * ``plan_chunks``     write events every ``chunk_tokens`` inside each sample, 64-token tiles
                       inside each event (models/qwen/ops/packed.py:16-31, ops/layout.py:128-189).
 
@@ -293,6 +295,50 @@ def l2norm(x, eps=1e-6, *, mode="exact"):
     x = _id(x)
     y = x / np.sqrt((x * x).sum(-1, keepdims=True) + eps)
     return bf16(y) if mode == "bf16" else y
+
+
+def qwen_gates(erase_gate, write_gate, decay_latent, decay_bias, decay_scale_log, *, mode="exact"):
+    """QwenMemoryBlock._write_gates / _log_decay (models/qwen/layer.py:71-88): (erase_sqrt,
+    write, log_decay) from the [L, H, D] pre-activations, decay_bias [H*D], decay_scale_log [H].
+
+    erase_sqrt = exp(0.5 * logsigmoid(e)) with logsigmoid = min(0, x) - log1p(exp(-|x|));
+    write = sigmoid(w); log_decay = -exp(decay_scale_log) * softplus(d + bias), softplus
+    threshold 20. ``mode="bf16"`` evaluates in float32 and rounds erase_sqrt and write to bf16
+    as the reference does (log_decay stays fp32); ``mode="exact"`` is float64 without rounding.
+    """
+    L, H, D = np.shape(erase_gate)
+    f = np.float32 if mode == "bf16" else np.float64
+    e = np.asarray(erase_gate, f)
+    es = np.exp(f(0.5) * (np.minimum(f(0), e) - np.log1p(np.exp(-np.abs(e)))))
+    w = f(1) / (f(1) + np.exp(-np.asarray(write_gate, f)))
+    x = np.asarray(decay_latent, f) + np.asarray(decay_bias, f).reshape(1, H, D)
+    sp = np.where(x > f(20), x, np.log1p(np.exp(np.minimum(x, f(20)))))
+    g = -np.exp(np.asarray(decay_scale_log, f)).reshape(1, H, 1) * sp
+    if mode == "bf16":
+        return bf16(es.astype(f)), bf16(w.astype(f)), g.astype(f).astype(np.float64)
+    return es, w, g
+
+
+def qwen_prologue(q, k, erase_gate, write_gate, decay_latent, decay_bias, decay_scale_log, eps=1e-6, *,
+                  mode="exact"):
+    """The Qwen memory block's inputs to the update: (q_hat, k_scaled, write, log_decay).
+
+    _symmetric_inputs (models/qwen/layer.py:90-97): q_hat = l2norm(q), k_scaled =
+    erase_sqrt * l2norm(k), with the gates of ``qwen_gates``. ``mode="bf16"`` follows the
+    eager rounding points in float32: l2norm in fp32 with a bf16 result (l2norm.py:104-108) and
+    k_scaled = bf16(erase_sqrt * k_hat) (layer.py:94).
+    """
+    es, w, g = qwen_gates(erase_gate, write_gate, decay_latent, decay_bias, decay_scale_log, mode=mode)
+    if mode == "bf16":
+        f = np.float32
+
+        def l2(x):
+            x = np.asarray(x, f)
+            rstd = f(1) / np.sqrt((x * x).sum(-1, keepdims=True, dtype=f) + f(eps))
+            return bf16(x * rstd)
+
+        return l2(q), bf16(es.astype(f) * l2(k).astype(f)), w, g
+    return l2norm(q, eps), es * l2norm(k, eps), w, g
 
 
 def gated_rms_norm(x, gate, weight, eps, softcap, *, mode="exact"):

@@ -203,6 +203,45 @@ def l2norm_case(name, seed, rows, D):
     print(f"{name}: done", flush=True)
 
 
+def qwen_prologue_case(name, seed, L, H, D):
+    """The Qwen memory block's own gate and input preparation on CPU: ``_write_gates`` (which
+    calls ``_log_decay``) in bf16 on a block built from a small config, and
+    ``_symmetric_inputs`` (the FLA l2norm, under the interpreter, so in fp32) on fp32 q, k and
+    the block's erase factor."""
+    from types import SimpleNamespace
+
+    from memt_sglang.models.qwen.layer import QwenMemoryBlock
+
+    rng = np.random.default_rng(seed)
+    cfg = SimpleNamespace(hidden_size=64, num_heads=H, head_dim=D, chunk_tokens=2048, rms_norm_eps=1e-6,
+                          output_gate_softcap=10.0)
+    block = QwenMemoryBlock(cfg, device="cpu")
+    bf = torch.bfloat16
+    with torch.no_grad():
+        block.f_down.weight.copy_(torch.from_numpy(0.3 * rng.standard_normal((H * D, D))).to(bf))
+        block.decay_bias.copy_(torch.from_numpy(rng.normal(-1.0, 1.0, H * D)).to(bf))
+        block.decay_scale_log.copy_(torch.from_numpy(rng.normal(0.0, 0.5, H)).to(bf))
+    gates = torch.from_numpy(rng.normal(0.0, 2.0, (1, L, 2 * H * D + D)).astype(np.float32)).to(bf)
+    *write_gates, decay_in = torch.split(gates, block.write_gate_rows, dim=-1)
+    with torch.no_grad():
+        decay_latent = block.f_down(decay_in)
+        erase, write, log_decay = block._write_gates(gates, 1, L)
+    q = rng.standard_normal((1, L, H, D)).astype(np.float32)
+    k = rng.standard_normal((1, L, H, D)).astype(np.float32)
+    q_hat, k_scaled, _ = QwenMemoryBlock._symmetric_inputs(_t(q), _t(k), erase.float())
+
+    def f32(t):
+        return t.detach().float().numpy()
+
+    np.savez_compressed(
+        HERE / f"{name}.npz", erase_gate=f32(write_gates[0]).reshape(L, H, D),
+        write_gate=f32(write_gates[1]).reshape(L, H, D), decay_latent=f32(decay_latent).reshape(L, H, D),
+        decay_bias=f32(block.decay_bias), decay_scale_log=f32(block.decay_scale_log),
+        erase_sqrt=f32(erase)[0], write=f32(write)[0], log_decay=f32(log_decay)[0], q=q[0], k=k[0],
+        q_hat=f32(q_hat)[0], k_scaled=f32(k_scaled)[0], eps=np.float32(1e-6))
+    print(f"{name}: done", flush=True)
+
+
 def main():
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference", required=True, help="path to the MemT-1.0 checkout")
@@ -230,6 +269,8 @@ def main():
         "read_qwen": lambda: qwen_read_case("read_qwen", 4, [1, 1, 3, 70, 64], 2, 64),
         "readout_bf16": lambda: bf16_readout_case("readout_bf16", 5, [1, 1, 1, 5, 1, 2], 2, 128, 10.0),
         "l2norm": lambda: l2norm_case("l2norm", 6, 300, 128),
+        # the Qwen memory block's gates, decay and symmetric q/k inputs (layer.py:71-97)
+        "qwen_prologue": lambda: qwen_prologue_case("qwen_prologue", 7, 37, 2, 64),
     }
     for name, fn in cases.items():
         if args.only and name not in args.only.split(","):

@@ -105,3 +105,84 @@ def test_rounding_helpers():
     assert O.bf16(np.array([1.00390625]))[0] == 1.0  # tie to even
     t = O.tf32(np.array([1.0 + 2 ** -11]))[0]
     assert t == 1.0 + 2 ** -10  # tie away from zero
+
+
+def _bf16_ulps(a, b):
+    """Per-element distance in bf16 units of the last place (both already bf16 values)."""
+    ia = np.asarray(a, np.float32).view(np.int32) >> 16
+    ib = np.asarray(b, np.float32).view(np.int32) >> 16
+    return np.abs(ia.astype(np.int64) - ib.astype(np.int64))
+
+
+def test_qwen_gates_match_reference(golden):
+    """The reference's _write_gates / _log_decay (eager bf16 on CPU) against the oracle's
+    float32 restatement: bf16 outputs within one unit of the last place (the libm exp and log1p
+    of numpy and torch may differ by an ulp), log-decay within fp32 rounding."""
+    z = golden("qwen_prologue")
+    es, w, g = O.qwen_gates(z["erase_gate"], z["write_gate"], z["decay_latent"], z["decay_bias"],
+                            z["decay_scale_log"], mode="bf16")
+    for got, ref in ((es, z["erase_sqrt"]), (w, z["write"])):
+        d = _bf16_ulps(got, ref)
+        assert d.max() <= 1 and np.mean(d > 0) < 0.01
+    assert O.rel_fro(g, z["log_decay"]) < 1e-6
+    es_x, w_x, g_x = O.qwen_gates(z["erase_gate"], z["write_gate"], z["decay_latent"], z["decay_bias"],
+                                  z["decay_scale_log"], mode="exact")
+    assert O.rel_fro(g_x, z["log_decay"]) < 1e-6 and O.rel_fro(es_x, z["erase_sqrt"]) < 1e-2
+
+
+def test_qwen_symmetric_inputs_match_reference(golden):
+    """_symmetric_inputs (FLA l2norm of q and k, the erase factor folded into the key) run by the
+    reference in fp32: the oracle's l2norm and product in float64."""
+    z = golden("qwen_prologue")
+    eps = float(z["eps"])
+    assert O.rel_fro(O.l2norm(z["q"], eps), z["q_hat"]) < 1e-6
+    assert O.rel_fro(z["erase_sqrt"] * O.l2norm(z["k"], eps), z["k_scaled"]) < 1e-6
+
+
+@pytest.mark.parametrize("gate", ["head", "channel"])
+def test_torch_cpu_restatement_matches_recurrence(gate):
+    """The fp32 PyTorch chunked restatement (the timed CPU baseline) against the float64 token
+    recurrence and the reference's own fp32 outputs."""
+    import torch
+
+    from oracle import gdn2_torch as OT
+
+    rng = np.random.default_rng(17)
+    lengths, H, D = [300, 64, 129, 1], 3, 64
+    L = sum(lengths)
+    cu = np.concatenate([[0], np.cumsum(lengths)])
+    k = rng.standard_normal((L, H, D))
+    k /= np.linalg.norm(k, axis=-1, keepdims=True)
+    v = rng.standard_normal((L, H, D))
+    gshape = (L, H, D) if gate == "channel" else (L, H)
+    g = -np.logaddexp(0, -rng.normal(2, .5, gshape))
+    w = 1 / (1 + np.exp(-rng.standard_normal((L, H, D))))
+    h0 = 0.02 * rng.standard_normal((4, H, D, D))
+    g3 = g if g.ndim == 3 else np.broadcast_to(g[:, :, None], (L, H, D))
+    ref = O.recurrence(k, v, g3, h0, cu, w=w)
+
+    def t(a):
+        return torch.from_numpy(np.ascontiguousarray(a)).float()
+
+    got = OT.chunked_update(t(k), t(v), t(g), t(h0), cu, w=t(w), chunk_tokens=128).numpy()
+    assert O.rel_fro(got, ref) < 1e-5
+
+
+def test_torch_cpu_restatement_matches_reference_golden(golden):
+    import torch
+
+    from oracle import gdn2_torch as OT
+
+    z = golden("d128_qwen")
+    k = z["k"]
+
+    def t(a):
+        return torch.from_numpy(np.ascontiguousarray(a)).float()
+
+    # d128_qwen has no channel-wise erase (b = 1), so the key is already the update's key
+    assert np.allclose(z["b"], 1.0)
+    s = OT.chunked_update(t(k), t(z["v"]), t(z["g"]), t(z["h0"]), list(z["cu_seqlens"]), w=t(z["w"]),
+                          chunk_tokens=int(z["chunk_tokens"])).numpy()
+    assert O.rel_fro(s, z["final_state"]) < 1e-5
+    o = OT.read(t(z["q"]), t(z["r0"]), list(z["cu_seqlens"]), float(z["scale"])).numpy()
+    assert O.rel_fro(o, z["read"]) < 1e-5

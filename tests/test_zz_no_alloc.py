@@ -64,6 +64,11 @@ def test_noalloc_update_matches_allocating_entry(cuda):
         torch.cuda.synchronize()
         err = O.rel_fro(out.cpu().numpy(), ref.cpu().numpy())
         assert err <= TOL_BF16, (seed, err)
+        # the status word of the call, read from the static scratch by the library itself
+        status = ctypes.c_int32(-1)
+        _lib.check(_lib.load().memt_gdn2_noalloc_status(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream),
+                                                        ctypes.byref(status)), "memt_gdn2_noalloc_status")
+        assert status.value == 0
 
 
 def test_noalloc_rejects_problems_beyond_its_scratch(cuda):
