@@ -383,7 +383,7 @@ def leg_gpu_bar(dev, gen, args, stream, flush):
 
     ref_y = ref_decode()
     it[0] = 0
-    our_y = our_decode()
+    our_y = our_decode().clone()  # later calls overwrite the output buffer
     torch.cuda.synchronize()
     it[0] = 0
     out["qwen_decode_readout"] = {
@@ -589,7 +589,7 @@ def run_ours(args, rank, world, local_rank):
     only_update = args.only == "update"
     gen = torch.Generator(device=dev).manual_seed(1234 + rank)
     L = sessions * T
-    x = config1_inputs(dev, gen, sessions, channel=False)
+    x = config1_inputs(dev, gen, sessions, channel=args.gate == "channel")
     q, k, v, g, beta, w, h0, cu = (x[n] for n in ("q", "k", "v", "g", "beta", "w", "h0", "cu"))
     flush = torch.empty(256 * 2 ** 20, dtype=torch.uint8, device=dev)  # > 126 MB L2
 
@@ -804,6 +804,8 @@ def main():
     ap.add_argument("--skip-gpu-bar", action="store_true")
     ap.add_argument("--skip-head-sharded", action="store_true")
     ap.add_argument("--sessions", type=int, default=SESSIONS, help="sessions per GPU (profiling cases)")
+    ap.add_argument("--gate", choices=["head", "channel"], default="head",
+                    help="log-decay layout of the headline step (channel: profiling the per-channel path)")
     ap.add_argument("--only", choices=["all", "update"], default="all",
                     help="update: time only the commit step (no e2e, other legs, CPU baseline)")
     args = ap.parse_args()

@@ -66,12 +66,13 @@ __device__ __forceinline__ float gated_norm_value(float o, float rstd, float w, 
 // gate and residual loads and the query normalisation: the state stream and the
 // prologue latencies overlap and each SM keeps >= 64 KB in flight.
 // ---------------------------------------------------------------------------
-template <int D>
+// LEAN: two loads per batch, for the rare extra token groups of a CTA (few live registers)
+template <int D, bool LEAN = false>
 struct GemvCfg {
   static constexpr int kTPR = D / 4;                     // threads per state row (one float4 each)
   static constexpr int kRPP = 256 / kTPR;                // rows per pass
   static constexpr int kPer = D / kRPP;                  // float4 loads per thread
-  static constexpr int kBatch = kPer < 16 ? kPer : (D >= 256 ? 8 : 16);
+  static constexpr int kBatch = LEAN ? 2 : (kPer < 16 ? kPer : (D >= 256 ? 8 : 16));
   static constexpr int kBatches = kPer / kBatch;
 };
 
@@ -79,11 +80,14 @@ struct GemvCfg {
 // two others' state streams
 // one group of up to TQ tokens [t0, t0 + nt) of head h reading snapshot `slot`; every thread
 // of the CTA calls it (it synchronises the CTA)
-template <int D, int TQ, bool EXACT>
-__device__ __forceinline__ void gemv_group(const ReadParams& p, int h, int64_t slot, int64_t t0, int nt,
-                                           float (*s_q)[D], float (*s_red)[TQ][D], float (*s_ss)[8]) {
-  using Cfg = GemvCfg<D>;
+template <int D, int TQ, bool EXACT, bool LEAN = false>
+__device__ __forceinline__ void gemv_group(const ReadParams& p, int h, int64_t slot, int64_t t0, int nt) {
+  using Cfg = GemvCfg<D, LEAN>;
   constexpr int RPP = Cfg::kRPP, TPR = Cfg::kTPR, BATCH = Cfg::kBatch;
+  // declared here rather than passed in, so that every access compiles to a shared-memory one
+  __shared__ float s_q[TQ][D];
+  __shared__ float s_red[RPP][TQ][D];
+  __shared__ float s_ss[TQ][8];
   const int tid = threadIdx.x;
   const int64_t qrow = (int64_t)p.H * D;
 
@@ -230,26 +234,27 @@ __device__ __forceinline__ void gemv_group(const ReadParams& p, int h, int64_t s
 }
 
 // CTA (block, head, y): token groups y, y + gridDim.y, ... of the block, so that every token is
-// read whatever bound on the block length the host sized the grid with
+// read whatever bound on the block length the host sized the grid with. Groups past the first
+// exist only when the bound is below the block length; they run on a lean variant (two loads per
+// batch) with the block's bounds re-read, so that the serving path keeps its registers.
 template <int D, int TQ, bool EXACT>
 __global__ void __launch_bounds__(256, (TQ == 1 && D <= 128) ? 3 : 2) read_gemv_kernel(ReadParams p) {
-  using Cfg = GemvCfg<D>;
-  __shared__ float s_q[TQ][D];
-  __shared__ float s_red[Cfg::kRPP][TQ][D];
-  __shared__ float s_ss[TQ][8];
+  {
+    const int n = blockIdx.x / p.H, h = blockIdx.x % p.H;
+    int64_t bos, eos;
+    block_range(p, n, bos, eos);
+    const int64_t t0 = bos + (int64_t)blockIdx.y * TQ;
+    if (t0 >= eos) return;
+    const int64_t slot = state_slot(p, n);
+    if (slot < 0) return;
+    gemv_group<D, TQ, EXACT>(p, h, slot, t0, (int)((eos - t0) < TQ ? (eos - t0) : TQ));
+  }
   const int n = blockIdx.x / p.H, h = blockIdx.x % p.H;
   int64_t bos, eos;
   block_range(p, n, bos, eos);
-  int64_t t0 = bos + (int64_t)blockIdx.y * TQ;
-  if (t0 >= eos) return;
-  const int64_t slot = state_slot(p, n);
-  if (slot < 0) return;
-  for (;;) {
-    const int nt = (int)((eos - t0) < TQ ? (eos - t0) : TQ);
-    gemv_group<D, TQ, EXACT>(p, h, slot, t0, nt, s_q, s_red, s_ss);
-    t0 += (int64_t)gridDim.y * TQ;
-    if (t0 >= eos) break;
+  for (int64_t t0 = bos + ((int64_t)blockIdx.y + gridDim.y) * TQ; t0 < eos; t0 += (int64_t)gridDim.y * TQ) {
     __syncthreads();  // the shared buffers are reused by the next group
+    gemv_group<D, TQ, EXACT, true>(p, h, state_slot(p, n), t0, (int)((eos - t0) < TQ ? (eos - t0) : TQ));
   }
 }
 

