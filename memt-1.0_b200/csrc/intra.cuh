@@ -50,31 +50,36 @@ struct IntraCfg {
   static constexpr int kPanel = D < 128 ? D : 128;
   static constexpr int kPanels = D / kPanel;
   static constexpr int kThreads = 256;
-  static constexpr int kLdE = kPanel + 4;   // fp32 decay tables
+  static constexpr int kLdE = kPanel;       // fp32 cumulative log2 decay (per channel), eidx layout
   static constexpr int kLdA = kTile + 4;    // fp32 64x64 scores / inverse blocks
   static constexpr int kLdAi = kTile + 8;   // bf16 64x64 inverse
   static constexpr size_t kTileB = size_t(kTile) * kPanel * 2;  // one bf16 [64][panel] tile
   static constexpr size_t kBytesE = HEAD ? 0 : size_t(kTile) * kLdE * 4;
   static constexpr size_t kBytesA = size_t(kTile) * kLdA * 4;
   static constexpr size_t kBytesAi = size_t(kTile) * kLdAi * 2;
-  // sK | sB? | sV | sW (later the w operand) | sO | sE? | sEi? | sA | sAi
+  // per-head decay without erase, D <= 128: k, v and write tiles arrive by TMA (the tiles need
+  // the 1024-byte aligned base of the 128-byte swizzle)
+  static constexpr bool kTma = HEAD && !ERASE && kPanels == 1;
+  // the fifth tile: the TMA loop's second k buffer, or the output tile of the panel loop (D = 256)
+  static constexpr bool kNeedO = kTma || kPanels > 1;
+  // sK | sB? | sV | sW (later the w operand) | sO? | sE? | sA | sAi
   static constexpr size_t offK = 0;
   static constexpr size_t offB = offK + kTileB;
   static constexpr size_t offV = offB + (ERASE ? kTileB : 0);
   static constexpr size_t offW = offV + kTileB;
   static constexpr size_t offO = offW + kTileB;
-  static constexpr size_t offE = offO + kTileB;
-  static constexpr size_t offEi = offE + kBytesE;
-  static constexpr size_t offA = offEi + kBytesE;
+  static constexpr size_t offE = offO + (kNeedO ? kTileB : 0);
+  static constexpr size_t offA = offE + kBytesE;
   static constexpr size_t offAi = offA + kBytesA;
-  // per-head decay without erase, D <= 128: k, v and write tiles arrive by TMA (the tiles need
-  // the 1024-byte aligned base of the 128-byte swizzle). Every configuration rounds the dynamic
-  // base up to 1024 bytes itself (the slack below): the kernel also declares static shared
-  // arrays, and where the dynamic region starts after them is the toolchain's choice (a build
-  // with relocatable device code started it at an address that broke 16-byte accesses).
-  static constexpr bool kTma = HEAD && !ERASE && kPanels == 1;
-  static constexpr size_t kSmem = offAi + kBytesAi + 1024;
+  // Every configuration rounds the dynamic base up itself (the slack below; 1024 bytes for the
+  // swizzled TMA tiles, 128 otherwise): the kernel also declares static shared arrays, and where
+  // the dynamic region starts after them is the toolchain's choice (a build with relocatable
+  // device code started it at an address that broke 16-byte accesses).
+  static constexpr uint32_t kAlign = kTma ? 1024u : 128u;
+  static constexpr size_t kSmem = offAi + kBytesAi + kAlign;
   static constexpr int kSmall = 9 * kTile + kThreads;  // static per-head factors + scan totals
+  // static factor buffer: two units' per-head factors, or the per-channel scan totals
+  static constexpr int kFacFloats = HEAD ? 2 * kSmall : 2 * 128;
 };
 
 __device__ __forceinline__ void named_sync(int id, int nthreads) {
@@ -202,7 +207,7 @@ struct IntraKernel {
   static constexpr uint32_t kTileBytes = static_cast<uint32_t>(Cfg::kTileB);
 
   __nv_bfloat16 *sK, *sB, *sV, *sW, *sO, *sAi;
-  float *sE, *sEi, *sA;
+  float *sE, *sA;  // sE (per channel): G, the cumulative log2 decay of the panel, [64][P] (eidx)
   // per-head factors: G, left (row) factor, right factors per row block, 2^G, 2^(G_last-G),
   // bf16(sqrt(beta)) per token
   float *sG, *sLf, *sRf, *sEh, *sKgf;
@@ -369,6 +374,10 @@ struct IntraKernel {
   }
   // point the factor arrays at buffer b of sFac
   __device__ __forceinline__ void use_factors(int b) {
+    if constexpr (!HEAD) {  // per channel: only the scan totals of channel_tables
+      sSeg = sFac;
+      return;
+    }
     float* f = sFac + b * Cfg::kSmall;
     sG = f;
     sLf = f + kTile;
@@ -376,6 +385,13 @@ struct IntraKernel {
     sKgf = f + 3 * kTile;
     sRf = f + 4 * kTile;  // [4][64], rows 1..3 used
     sSeg = f + 9 * kTile;
+  }
+
+  // Element (row, col) of the per-channel decay table: rows of P floats whose 16-byte chunks
+  // are XOR-permuted by (row & 7), so that the score fragments (8 rows x 4 channel pairs) fall
+  // in distinct banks without padding; chunk-granular, so cp.async fills it directly.
+  __device__ __forceinline__ static int eidx(int row, int col) {
+    return row * Cfg::kLdE + ((((col >> 2) ^ row) & 7) | ((col >> 2) & ~7)) * 4 + (col & 3);
   }
 
   // ---- decay, per-channel layout: cumulative sum and factor tables of one panel ----
@@ -387,8 +403,8 @@ struct IntraKernel {
       float acc = 0.f;
 #pragma unroll 8
       for (int i = sg * kSegLen; i < (sg + 1) * kSegLen; ++i) {
-        acc += sE[i * Cfg::kLdE + c];
-        sE[i * Cfg::kLdE + c] = acc;
+        acc += sE[eidx(i, c)];
+        sE[eidx(i, c)] = acc;
       }
       sSeg[sg * P + c] = acc;
     }
@@ -399,37 +415,27 @@ struct IntraKernel {
       for (int s2 = 0; s2 < sg; ++s2) off += sSeg[s2 * P + c];
 #pragma unroll 8
       for (int i = sg * kSegLen; i < (sg + 1) * kSegLen; ++i) {
-        const float G = (sE[i * Cfg::kLdE + c] + off) * kRcpLn2;
+        const float G = (sE[eidx(i, c)] + off) * kRcpLn2;
         ok = ok && (G >= -60.f) && (G <= 60.f);
-        sE[i * Cfg::kLdE + c] = G;
+        sE[eidx(i, c)] = G;
       }
     }
+    // fast: every exponent of the panel in [-60, 60], so that the factorised diagonal blocks
+    // (left factor <= 1, right factor >= 1) cannot overflow; otherwise the diagonal blocks are
+    // evaluated pair by pair
     fast = __syncthreads_and(ok) != 0;
-    if (fast) {
-      for (int idx = tid; idx < kTile * P; idx += NT) {
-        const int i = idx / P, cc = idx % P;
-        const float G = sE[i * Cfg::kLdE + cc];
-        sEi[i * Cfg::kLdE + cc] = fast_exp2(-G);
-        sE[i * Cfg::kLdE + cc] = fast_exp2(G);
-      }
-    }
-    __syncthreads();
   }
   __device__ __forceinline__ float2 ld2(const float* a, int row, int col) const {
-    return *reinterpret_cast<const float2*>(a + row * Cfg::kLdE + col);
+    return *reinterpret_cast<const float2*>(a + eidx(row, col));  // col even
   }
-  // 2^(G_i - G_n) for the channel pair (c, c+1)
+  // 2^(G_i - G_n) for the channel pair (c, c+1): one exp2 of the difference, which stays
+  // finite whatever the decay (the shared memory of a second, 2^-G table goes to a second CTA)
   __device__ __forceinline__ float2 p2d2(int i, int n, int c) const {
-    if (fast) {
-      const float2 e = ld2(sE, i, c), ei = ld2(sEi, n, c);
-      return make_float2(e.x * ei.x, e.y * ei.y);
-    }
     const float2 gi = ld2(sE, i, c), gn = ld2(sE, n, c);
     return make_float2(fast_exp2(gi.x - gn.x), fast_exp2(gi.y - gn.y));
   }
   __device__ __forceinline__ float2 p22(int i, int c) const {
     const float2 e = ld2(sE, i, c);
-    if (fast) return e;
     return make_float2(fast_exp2(e.x), fast_exp2(e.y));
   }
 
@@ -644,7 +650,7 @@ struct IntraKernel {
                 float kb = __bfloat162float(sK[pswz(i, c)]);
                 if constexpr (ERASE) kb *= __bfloat162float(sB[pswz(i, c)]);
                 sum += kb * __bfloat162float(sK[pswz(j, c)]) *
-                       fast_exp2(sE[i * Cfg::kLdE + c] - sE[j * Cfg::kLdE + c]);
+                       fast_exp2(sE[eidx(i, c)] - sE[eidx(j, c)]);
               }
             }
             acc[s][q] += sum;
@@ -906,7 +912,7 @@ struct IntraKernel {
       if constexpr (HEAD)
         gEl[c0 + j] = sSeg[0];
       else
-        gEl[c0 + j] = fast ? sE[last * Cfg::kLdE + j] : fast_exp2(sE[last * Cfg::kLdE + j]);
+        gEl[c0 + j] = fast_exp2(sE[eidx(last, j)]);
     }
   }
 
@@ -1053,7 +1059,7 @@ struct IntraKernel {
       for (int i = tid; i < kChunks; i += NT) {
         const int row = i / (P / 4), col = (i % (P / 4)) * 4;
         const bool valid = row < len;
-        cp_async16_zfill(sE + row * Cfg::kLdE + col, valid ? base + (int64_t)row * row_stride + col : p.g, valid);
+        cp_async16_zfill(sE + eidx(row, col), valid ? base + (int64_t)row * row_stride + col : p.g, valid);
       }
     };
     auto load_key_panel = [&](int c0) {
@@ -1388,17 +1394,17 @@ __global__ void __launch_bounds__(256, 2) intra_kernel(const __grid_constant__ I
   extern __shared__ __align__(1024) unsigned char smem_intra[];
   using Cfg = IntraCfg<D, HEAD, ERASE>;
   IntraKernel<D, HEAD, ERASE> k;
-  unsigned char* base = smem_intra + ((1024u - (smem_u32(smem_intra) & 1023u)) & 1023u);
+  constexpr uint32_t kA = Cfg::kAlign;
+  unsigned char* base = smem_intra + ((kA - (smem_u32(smem_intra) & (kA - 1))) & (kA - 1));
   k.sK = reinterpret_cast<__nv_bfloat16*>(base + Cfg::offK);
   k.sB = reinterpret_cast<__nv_bfloat16*>(base + Cfg::offB);
   k.sV = reinterpret_cast<__nv_bfloat16*>(base + Cfg::offV);
   k.sW = reinterpret_cast<__nv_bfloat16*>(base + Cfg::offW);
-  k.sO = reinterpret_cast<__nv_bfloat16*>(base + Cfg::offO);
+  k.sO = Cfg::kNeedO ? reinterpret_cast<__nv_bfloat16*>(base + Cfg::offO) : nullptr;
   k.sE = reinterpret_cast<float*>(base + Cfg::offE);
-  k.sEi = reinterpret_cast<float*>(base + Cfg::offEi);
   k.sA = reinterpret_cast<float*>(base + Cfg::offA);
   k.sAi = reinterpret_cast<__nv_bfloat16*>(base + Cfg::offAi);
-  __shared__ __align__(16) float s_fac[2 * Cfg::kSmall];
+  __shared__ __align__(16) float s_fac[Cfg::kFacFloats];
   __shared__ __align__(16) float s_scr[4 * 256];
   k.sScr = s_scr;
   k.sFac = s_fac;

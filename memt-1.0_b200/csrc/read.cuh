@@ -235,27 +235,35 @@ __device__ __forceinline__ void gemv_group(const ReadParams& p, int h, int64_t s
 
 // CTA (block, head, y): token groups y, y + gridDim.y, ... of the block, so that every token is
 // read whatever bound on the block length the host sized the grid with. Groups past the first
-// exist only when the bound is below the block length; they run on a lean variant (two loads per
-// batch) with the block's bounds re-read, so that the serving path keeps its registers.
+// exist only when that bound is below the block length. They run first, on a lean variant (two
+// loads per batch); the CTA's first group, the only one when the bound holds, then runs as the
+// kernel's last code with nothing else live, so the serving path keeps its registers.
 template <int D, int TQ, bool EXACT>
 __global__ void __launch_bounds__(256, (TQ == 1 && D <= 128) ? 3 : 2) read_gemv_kernel(ReadParams p) {
   {
     const int n = blockIdx.x / p.H, h = blockIdx.x % p.H;
     int64_t bos, eos;
     block_range(p, n, bos, eos);
-    const int64_t t0 = bos + (int64_t)blockIdx.y * TQ;
-    if (t0 >= eos) return;
-    const int64_t slot = state_slot(p, n);
-    if (slot < 0) return;
-    gemv_group<D, TQ, EXACT>(p, h, slot, t0, (int)((eos - t0) < TQ ? (eos - t0) : TQ));
+    const int64_t stride = (int64_t)gridDim.y * TQ;
+    int64_t t0 = bos + (int64_t)blockIdx.y * TQ + stride;
+    if (t0 < eos) {
+      const int64_t slot = state_slot(p, n);
+      if (slot >= 0) {
+        for (; t0 < eos; t0 += stride) {
+          gemv_group<D, TQ, EXACT, true>(p, h, slot, t0, (int)((eos - t0) < TQ ? (eos - t0) : TQ));
+          __syncthreads();  // the shared buffers are reused by the next group
+        }
+      }
+    }
   }
   const int n = blockIdx.x / p.H, h = blockIdx.x % p.H;
   int64_t bos, eos;
   block_range(p, n, bos, eos);
-  for (int64_t t0 = bos + ((int64_t)blockIdx.y + gridDim.y) * TQ; t0 < eos; t0 += (int64_t)gridDim.y * TQ) {
-    __syncthreads();  // the shared buffers are reused by the next group
-    gemv_group<D, TQ, EXACT, true>(p, h, state_slot(p, n), t0, (int)((eos - t0) < TQ ? (eos - t0) : TQ));
-  }
+  const int64_t t0 = bos + (int64_t)blockIdx.y * TQ;
+  if (t0 >= eos) return;
+  const int64_t slot = state_slot(p, n);
+  if (slot < 0) return;
+  gemv_group<D, TQ, EXACT>(p, h, slot, t0, (int)((eos - t0) < TQ ? (eos - t0) : TQ));
 }
 
 // ---------------------------------------------------------------------------
