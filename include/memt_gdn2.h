@@ -213,8 +213,11 @@ typedef struct memt_gdn2_read_args {
   int32_t value_dim;       /* equal to key_dim                                  */
   int64_t total_tokens;    /* L                                                 */
   int32_t max_block_tokens;/* bound on tokens per block that sizes the grid and selects the
-                              kernel; 0 = L. A bound below the longest block costs speed,
-                              not tokens: the kernels walk every tile of a block */
+                              kernel; 0 = L. A bound with bound * num_blocks < L is rejected.
+                              Above 1, a bound below the longest block costs speed, not tokens:
+                              the kernels walk every token of a block. A bound of 1 selects the
+                              one-token decode kernel, which reads only the first token of a
+                              longer block and records that in memt_read_status */
   const int32_t *cu_seqlens; /* device [num_blocks+1]                           */
   const void *q;           /* [L,H,K]                                           */
   int32_t q_dtype;         /* MEMT_BF16 or MEMT_F32                             */
@@ -231,6 +234,12 @@ typedef struct memt_gdn2_read_args {
 } memt_gdn2_read_args;
 
 int memt_gdn2_read(const memt_gdn2_read_args *args, memt_stream_t stream);
+
+/* Status of the reads on the current device since the last call, then cleared: bit 0 = the
+ * one-token decode kernel met a block of more than one token (possible only with empty blocks
+ * beside it, as bounds with bound * num_blocks < L are rejected) and read only its first token.
+ * Synchronises the stream; intended for tests and debugging. */
+int memt_read_status(memt_stream_t stream, int32_t *status_out);
 
 /* ---- one memory layer's commit: update and read together ---------------
  *

@@ -228,6 +228,8 @@ int check_read(const memt_gdn2_read_args* a) {
     return MEMT_ERR_INVALID_ARGUMENT;
   if (!aligned16(a->q) || !aligned16(a->states) || !aligned16(a->out)) return MEMT_ERR_MISALIGNED;
   if (a->state_slots != nullptr && a->num_slots < 1) return MEMT_ERR_INVALID_ARGUMENT;
+  if (a->max_block_tokens < 0 || (a->max_block_tokens > 0 && int64_t(a->max_block_tokens) * a->num_blocks < a->total_tokens))
+    return MEMT_ERR_INVALID_ARGUMENT;  // a bound the blocks cannot satisfy
   return MEMT_OK;
 }
 
@@ -376,6 +378,8 @@ int memt_memory_readout(const memt_memory_readout_args* a, memt_stream_t stream)
       !aligned16(a->residual) || !aligned16(a->norm_weight))
     return MEMT_ERR_MISALIGNED;
   if (a->state_slots != nullptr && a->num_slots < 1) return MEMT_ERR_INVALID_ARGUMENT;
+  if (a->max_block_tokens < 0 || (a->max_block_tokens > 0 && int64_t(a->max_block_tokens) * a->num_blocks < a->total_tokens))
+    return MEMT_ERR_INVALID_ARGUMENT;  // a bound the blocks cannot satisfy
   if (a->total_tokens == 0) return MEMT_OK;
   ReadParams p{};
   p.num_blocks = a->num_blocks;

@@ -78,3 +78,18 @@ int launch_read(const ReadParams& p, int D, bool exact, int64_t maxlen, cudaStre
 }
 
 }  // namespace memt
+
+// Status of the one-token decode kernel on the current device (g_read_status), then cleared.
+extern "C" int memt_read_status(memt_stream_t stream, int32_t* status_out) {
+  if (status_out == nullptr) return MEMT_ERR_INVALID_ARGUMENT;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int32_t v = 0;
+  const int32_t zero = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(&v, memt::g_read_status, sizeof(v), 0, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e == cudaSuccess) e = cudaMemcpyToSymbolAsync(memt::g_read_status, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return memt::cuda_status(e);
+  *status_out = v;
+  return MEMT_OK;
+}

@@ -66,13 +66,12 @@ __device__ __forceinline__ float gated_norm_value(float o, float rstd, float w, 
 // gate and residual loads and the query normalisation: the state stream and the
 // prologue latencies overlap and each SM keeps >= 64 KB in flight.
 // ---------------------------------------------------------------------------
-// LEAN: two loads per batch, for the rare extra token groups of a CTA (few live registers)
-template <int D, bool LEAN = false>
+template <int D>
 struct GemvCfg {
   static constexpr int kTPR = D / 4;                     // threads per state row (one float4 each)
   static constexpr int kRPP = 256 / kTPR;                // rows per pass
   static constexpr int kPer = D / kRPP;                  // float4 loads per thread
-  static constexpr int kBatch = LEAN ? 2 : (kPer < 16 ? kPer : (D >= 256 ? 8 : 16));
+  static constexpr int kBatch = kPer < 16 ? kPer : (D >= 256 ? 8 : 16);
   static constexpr int kBatches = kPer / kBatch;
 };
 
@@ -80,9 +79,9 @@ struct GemvCfg {
 // two others' state streams
 // one group of up to TQ tokens [t0, t0 + nt) of head h reading snapshot `slot`; every thread
 // of the CTA calls it (it synchronises the CTA)
-template <int D, int TQ, bool EXACT, bool LEAN = false>
+template <int D, int TQ, bool EXACT>
 __device__ __forceinline__ void gemv_group(const ReadParams& p, int h, int64_t slot, int64_t t0, int nt) {
-  using Cfg = GemvCfg<D, LEAN>;
+  using Cfg = GemvCfg<D>;
   constexpr int RPP = Cfg::kRPP, TPR = Cfg::kTPR, BATCH = Cfg::kBatch;
   // declared here rather than passed in, so that every access compiles to a shared-memory one
   __shared__ float s_q[TQ][D];
@@ -233,37 +232,37 @@ __device__ __forceinline__ void gemv_group(const ReadParams& p, int h, int64_t s
   }
 }
 
-// CTA (block, head, y): token groups y, y + gridDim.y, ... of the block, so that every token is
-// read whatever bound on the block length the host sized the grid with. Groups past the first
-// exist only when that bound is below the block length. They run first, on a lean variant (two
-// loads per batch); the CTA's first group, the only one when the bound holds, then runs as the
-// kernel's last code with nothing else live, so the serving path keeps its registers.
+// Status of the one-token decode kernel on this device: bit 0 = a block held more tokens than
+// the grid's bound covered (its tokens past the first were not read). Read and cleared by
+// memt_read_status.
+static __device__ int g_read_status;
+
+// CTA (block, head, y). Multi-token CTAs (TQ > 1) take token groups y, y + gridDim.y, ... of
+// the block, so every token is read whatever bound the host sized the grid with. The one-token
+// decode CTA runs its group alone: a loop costs it registers it does not have (18 % of its
+// time), so a block longer than the bound is only detected, in g_read_status (the host rejects
+// bounds that are provably short before launch).
 template <int D, int TQ, bool EXACT>
 __global__ void __launch_bounds__(256, (TQ == 1 && D <= 128) ? 3 : 2) read_gemv_kernel(ReadParams p) {
-  {
-    const int n = blockIdx.x / p.H, h = blockIdx.x % p.H;
-    int64_t bos, eos;
-    block_range(p, n, bos, eos);
-    const int64_t stride = (int64_t)gridDim.y * TQ;
-    int64_t t0 = bos + (int64_t)blockIdx.y * TQ + stride;
-    if (t0 < eos) {
-      const int64_t slot = state_slot(p, n);
-      if (slot >= 0) {
-        for (; t0 < eos; t0 += stride) {
-          gemv_group<D, TQ, EXACT, true>(p, h, slot, t0, (int)((eos - t0) < TQ ? (eos - t0) : TQ));
-          __syncthreads();  // the shared buffers are reused by the next group
-        }
-      }
-    }
-  }
   const int n = blockIdx.x / p.H, h = blockIdx.x % p.H;
   int64_t bos, eos;
   block_range(p, n, bos, eos);
-  const int64_t t0 = bos + (int64_t)blockIdx.y * TQ;
+  int64_t t0 = bos + (int64_t)blockIdx.y * TQ;
   if (t0 >= eos) return;
   const int64_t slot = state_slot(p, n);
   if (slot < 0) return;
-  gemv_group<D, TQ, EXACT>(p, h, slot, t0, (int)((eos - t0) < TQ ? (eos - t0) : TQ));
+  const int64_t stride = (int64_t)gridDim.y * TQ;
+  if constexpr (TQ == 1) {
+    if (t0 + stride < eos && threadIdx.x == 0) atomicOr(&g_read_status, 1);
+    gemv_group<D, TQ, EXACT>(p, h, slot, t0, 1);
+  } else {
+    for (;;) {
+      gemv_group<D, TQ, EXACT>(p, h, slot, t0, (int)((eos - t0) < TQ ? (eos - t0) : TQ));
+      t0 += stride;
+      if (t0 >= eos) break;
+      __syncthreads();  // the shared buffers are reused by the next group
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------

@@ -93,6 +93,7 @@ SIGNATURES = {
     "memt_gdn2_update": (c_int, [POINTER(UpdateArgs), c_void_p, c_size_t, c_void_p]),
     "memt_gdn2_workspace_status": (c_int, [c_void_p, c_void_p, POINTER(c_int32)]),
     "memt_gdn2_read": (c_int, [POINTER(ReadArgs), c_void_p]),
+    "memt_read_status": (c_int, [c_void_p, POINTER(c_int32)]),
     "memt_gdn2_update_read": (c_int, [POINTER(UpdateArgs), c_void_p, c_size_t, POINTER(ReadArgs), c_void_p]),
     "memt_memory_readout": (c_int, [POINTER(ReadoutArgs), c_void_p]),
     "memt_qwen_prologue": (c_int, [POINTER(PrologueArgs), c_void_p]),

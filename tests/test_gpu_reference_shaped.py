@@ -228,46 +228,79 @@ def test_state_pool_update_against_oracle(cuda, gate):
 # reads: grid bound below the longest block, the reference's own ChunkPlan
 # ---------------------------------------------------------------------------
 
+def _read_call(q, states, cu, n_blocks, bound, D, cuda):
+    _, args, out, keep = ops._read_args(q, states, cu, n_blocks, bound, D ** -0.5, torch.bfloat16)
+    return _lib.load().memt_gdn2_read(ctypes.byref(args), ops._stream(cuda)), out, keep
+
+
+def _readout_call(q, states, cu, n_blocks, bound, gate, nw, cuda):
+    L, H, D = q.shape
+    out = torch.zeros(L, H * D, device=cuda, dtype=torch.bfloat16)
+    args = _lib.ReadoutArgs(num_blocks=n_blocks, num_heads=H, head_dim=D, total_tokens=L, max_block_tokens=bound,
+                            cu_seqlens=cu.data_ptr(), q=q.data_ptr(), normalize_q=1, q_eps=1e-6,
+                            states=states.data_ptr(), scale=D ** -0.5, gate=gate.data_ptr(), norm_weight=nw.data_ptr(),
+                            norm_eps=1e-6, softcap=10.0, residual=None, out=out.data_ptr(), row_stride=H * D,
+                            head_offset=0)
+    return _lib.load().memt_memory_readout(ctypes.byref(args), ops._stream(cuda)), out
+
+
 @pytest.mark.parametrize("D", [64, 128, 256])
 def test_read_with_a_short_block_bound_reads_every_token(cuda, D):
-    """max_block_tokens only sizes the grid: with a bound below the longest block (which also
-    selects the one-token GEMV kernel) every token is still read, bit for bit as with the true
-    bound, for the plain read and the fused readout."""
+    """max_block_tokens sizes the grid and picks the kernel. A bound the blocks cannot satisfy
+    (bound * blocks < tokens) is rejected before launch; any other bound below the longest block
+    still reads every token, on the tile kernels (bounds > 16) and on the multi-token GEMV
+    (bounds 2..16), for the plain read and the fused readout."""
     rng = np.random.default_rng(D)
-    lengths, H = [1500, 3, 700], 2
-    L, N = sum(lengths), len(lengths)
     bf = torch.bfloat16
-    q = torch.from_numpy(rng.standard_normal((L, H, D)).astype(np.float32)).to(cuda).to(bf)
-    states = torch.from_numpy((0.05 * rng.standard_normal((N, H, D, D))).astype(np.float32)).to(cuda)
-    cu = torch.tensor(np.concatenate([[0], np.cumsum(lengths)]), dtype=torch.int32, device=cuda)
+    for lengths, bounds in (([1500, 3, 700], (800, 1000)), ([40] + [1] * 9, (5, 16))):
+        L, N, H = sum(lengths), len(lengths), 2
+        q = torch.from_numpy(rng.standard_normal((L, H, D)).astype(np.float32)).to(cuda).to(bf)
+        states = torch.from_numpy((0.05 * rng.standard_normal((N, H, D, D))).astype(np.float32)).to(cuda)
+        cu = torch.tensor(np.concatenate([[0], np.cumsum(lengths)]), dtype=torch.int32, device=cuda)
+        gate = torch.from_numpy(rng.standard_normal((L, H, D)).astype(np.float32)).to(cuda).to(bf)
+        nw = torch.ones(D, device=cuda, dtype=bf)
+        st, _, _ = _read_call(q, states, cu, N, 1, D, cuda)
+        assert st == _lib.MEMT_ERR_INVALID_ARGUMENT
+        st, _ = _readout_call(q, states, cu, N, 1, gate, nw, cuda)
+        assert st == _lib.MEMT_ERR_INVALID_ARGUMENT
+        ref = O.read(_np(q), states.cpu().numpy(), cu.cpu().numpy(), D ** -0.5, mode="bf16")
+        st, full_fused = _readout_call(q, states, cu, N, max(lengths), gate, nw, cuda)
+        assert st == 0
+        for bound in bounds:
+            st, out, keep = _read_call(q, states, cu, N, bound, D, cuda)
+            assert st == 0
+            st, fused = _readout_call(q, states, cu, N, bound, gate, nw, cuda)
+            assert st == 0
+            torch.cuda.synchronize()
+            assert O.rel_fro(_np(out), ref) <= TOL_BF16, (lengths, bound)
+            assert bool((fused.float().abs().sum(-1) > 0).all()), (lengths, bound)  # every token row written
+            assert O.rel_fro(_np(fused), _np(full_fused)) <= 4e-3, (lengths, bound)
+
+
+def test_decode_read_records_a_block_longer_than_its_bound(cuda):
+    """With an empty block beside it, a block of two tokens passes the host's bound check for
+    bound 1: the one-token decode kernel reads its first token and sets bit 0 of the read
+    status, which memt_read_status reports once and clears."""
     lib = _lib.load()
-    outs = []
-    for bound in (max(lengths), 1, 17, 100):
-        _, args, out, keep = ops._read_args(q, states, cu, N, bound, D ** -0.5, bf)
-        assert lib.memt_gdn2_read(ctypes.byref(args), ops._stream(cuda)) == 0
-        outs.append(out)
-    gate = torch.from_numpy(rng.standard_normal((L, H, D)).astype(np.float32)).to(cuda).to(bf)
-    nw = torch.ones(D, device=cuda, dtype=bf)
-    fused = []
-    for bound in (max(lengths), 1, 40):
-        out = torch.zeros(L, H * D, device=cuda, dtype=bf)
-        args = _lib.ReadoutArgs(num_blocks=N, num_heads=H, head_dim=D, total_tokens=L, max_block_tokens=bound,
-                                cu_seqlens=cu.data_ptr(), q=q.data_ptr(), normalize_q=1, q_eps=1e-6,
-                                states=states.data_ptr(), scale=D ** -0.5, gate=gate.data_ptr(),
-                                norm_weight=nw.data_ptr(), norm_eps=1e-6, softcap=10.0, residual=None,
-                                out=out.data_ptr(), row_stride=H * D, head_offset=0)
-        assert lib.memt_memory_readout(ctypes.byref(args), ops._stream(cuda)) == 0
-        fused.append(out)
-    torch.cuda.synchronize()
-    ref = O.read(_np(q), states.cpu().numpy(), cu.cpu().numpy(), D ** -0.5, mode="bf16")
-    assert O.rel_fro(_np(outs[0]), ref) <= TOL_BF16
-    # the true bound and the short bounds pick different kernels for some of these; all read
-    # every token to within the bf16 tolerance, and each kernel reproduces itself
-    for o in outs[1:]:
-        assert O.rel_fro(_np(o), ref) <= TOL_BF16
-    for f in fused[1:]:
-        assert bool((f.float().abs().sum(-1) > 0).all())
-        assert O.rel_fro(_np(f), _np(fused[0])) <= 4e-3
+    bf = torch.bfloat16
+    H, D = 2, 128
+    rng = np.random.default_rng(4)
+    q = torch.from_numpy(rng.standard_normal((2, H, D)).astype(np.float32)).to(cuda).to(bf)
+    states = torch.from_numpy((0.05 * rng.standard_normal((2, H, D, D))).astype(np.float32)).to(cuda)
+    stream = ops._stream(cuda)
+    status = ctypes.c_int32(-1)
+    assert lib.memt_read_status(stream, ctypes.byref(status)) == 0  # clear what earlier tests left
+    good = torch.tensor([0, 1, 2], dtype=torch.int32, device=cuda)
+    st, ref, _ = _read_call(q, states, good, 2, 1, D, cuda)
+    assert st == 0
+    assert lib.memt_read_status(stream, ctypes.byref(status)) == 0 and status.value == 0
+    cu = torch.tensor([0, 0, 2], dtype=torch.int32, device=cuda)  # block 0 empty, block 1 two tokens
+    st, out, _ = _read_call(q, states, cu, 2, 1, D, cuda)
+    assert st == 0
+    assert lib.memt_read_status(stream, ctypes.byref(status)) == 0 and status.value == 1
+    assert lib.memt_read_status(stream, ctypes.byref(status)) == 0 and status.value == 0
+    want = O.read(_np(q[:1]), states[1:].cpu().numpy(), np.array([0, 1]), D ** -0.5, mode="bf16")
+    assert O.rel_fro(_np(out[:1]), want) <= TOL_BF16
 
 
 def test_read_fwd_takes_the_reference_chunk_plan(cuda):
