@@ -260,9 +260,15 @@ def leg_config1_channel(dev, gen, args, stream, flush, hbm):
 
 
 def leg_readout(dev, gen, stream, hbm):
+    """Decode readout kernel throughput: the C entry point called with argument structs built
+    once per resident layer, so the loop measures the device, not Python's per-call work
+    (``python_api_us_per_layer`` is the same loop through memt_b200.memory_readout)."""
+    import ctypes
+
     import torch
 
     import memt_b200 as M
+    from memt_b200 import _lib, ops
 
     bf = torch.bfloat16
     states = torch.randn(RO_LAYERS_RESIDENT, RO_SESSIONS, H, D, D, device=dev, generator=gen) * 0.05
@@ -272,19 +278,35 @@ def leg_readout(dev, gen, stream, hbm):
     attn = torch.randn(RO_SESSIONS, H * D, device=dev, generator=gen).to(bf)
     out = torch.empty_like(attn)
     lengths = [1] * RO_SESSIONS
+    cu = torch.arange(RO_SESSIONS + 1, dtype=torch.int32, device=dev)
+    lib = _lib.load()
+    args = [_lib.ReadoutArgs(
+        num_blocks=RO_SESSIONS, num_heads=H, head_dim=D, total_tokens=RO_SESSIONS, max_block_tokens=1,
+        cu_seqlens=cu.data_ptr(), q=q.data_ptr(), normalize_q=1, q_eps=1e-6, states=states[i].data_ptr(),
+        scale=D ** -0.5, gate=gate.data_ptr(), norm_weight=w.data_ptr(), norm_eps=1e-6, softcap=10.0,
+        residual=attn.data_ptr(), out=out.data_ptr(), row_stride=H * D, head_offset=0)
+        for i in range(RO_LAYERS_RESIDENT)]
+    sp = ops._stream(dev)
     it = [0]
 
     def step():
+        st = lib.memt_memory_readout(ctypes.byref(args[it[0] % RO_LAYERS_RESIDENT]), sp)
+        if st != 0:
+            raise RuntimeError(f"memt_memory_readout: {st}")
+        it[0] += 1
+
+    def step_api():
         M.memory_readout(q, states[it[0] % RO_LAYERS_RESIDENT], lengths, D ** -0.5, gate, w, softcap=10.0,
                          residual=attn, out=out)
         it[0] += 1
 
     us = time_steps(step, 40, 8, stream) * 1e3  # the resident states cycle through 1 GB >> L2
+    us_api = time_steps(step_api, 40, 8, stream) * 1e3
     nbytes = RO_SESSIONS * H * (4 * D * D + 4 * 2 * D) + 2 * D  # state + q, gate, attn in, out
     return {"workload": "config2: 256 sessions x 16 heads, fp32 128x128 state, 1 bf16 query each, fused "
                         "l2norm/read/gated RMSNorm/residual, one layer per call (4 layers' states cycled)",
             "us_per_layer": us, "gbs": nbytes / (us * 1e-6) / 1e9, "frac": nbytes / (us * 1e-6) / 1e9 / hbm,
-            "bytes_per_layer": nbytes}
+            "bytes_per_layer": nbytes, "python_api_us_per_layer": us_api}
 
 
 def leg_gpu_bar(dev, gen, args, stream, flush):

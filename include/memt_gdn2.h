@@ -74,8 +74,8 @@ typedef struct CUstream_st *memt_stream_t;
 
 /* Library version (major*10000 + minor*100 + patch).
  *   0.2.0  state pools by slot index (fields appended to the update, read and readout args)
- *   0.3.0  every argument struct starts with struct_size; the Qwen memory-block prologue;
- *          memt_gdn2_noalloc_status */
+ *   0.3.0  every argument struct starts with struct_size; the memory-block prologue; the
+ *          DeepSeek grouped latent RMS norm; memt_gdn2_noalloc_status, memt_read_status */
 int memt_version(void);  /* 300 */
 
 /* Argument structs start with `uint32_t struct_size`, which the caller sets to
@@ -308,7 +308,11 @@ int memt_memory_readout(const memt_memory_readout_args *args, memt_stream_t stre
  *   write_out[t,h,c] = bf16(sigmoid(write[t,h,c]))
  *   log_decay_out[t,h,c] = -exp(decay_scale_log[h]) * softplus(decay[t,h,c] + decay_bias[h*D+c])
  * The reference then passes erase = ones to the update; with these outputs the update is
- * called with no erase factor (erase NULL), which is the same computation.
+ * called with no erase factor (erase NULL), which is the same computation. The DeepSeek block's
+ * gate and q/k preparation (expand_write_gates and prepare_stable_qk,
+ * models/deepseek/ops/compiled_tensor_ops.py:54-78,102-107) is the same arithmetic with its
+ * rsqrt l2norm (norm_kind 1); its erase, write and decay pre-activations are the b_up, w_up and
+ * f_down projections.
  * The bf16 inputs are token rows of *_stride elements (>= H*D, a multiple of 8), head h at
  * column h*D, so the q/k/v and gate projections' split views need no copy. Outputs are
  * contiguous [L, H, D]. */
@@ -325,6 +329,9 @@ typedef struct memt_qwen_prologue_args {
   const void *decay_bias;       /* bf16 [H*D]                                    */
   const void *decay_scale_log;  /* bf16 [H]                                      */
   float eps;                    /* l2norm epsilon (1e-6 in the reference)        */
+  int32_t norm_kind;            /* 0: x / sqrt(sum x^2 + eps), the FLA l2norm of the Qwen block;
+                                   1: x * rsqrt(sum x^2 + eps), the DeepSeek block's l2norm
+                                   (models/deepseek/ops/normalization.py:6-8, compiled_tensor_ops.py:102-107) */
   void *q_out;                  /* bf16 [L,H,D]                                  */
   void *k_out;                  /* bf16 [L,H,D]                                  */
   void *write_out;              /* bf16 [L,H,D]                                  */
@@ -333,13 +340,35 @@ typedef struct memt_qwen_prologue_args {
 
 int memt_qwen_prologue(const memt_qwen_prologue_args *args, memt_stream_t stream);
 
+/* ---- DeepSeek grouped latent RMS norm ------------------------------------
+ *
+ * Replaces _latent_norm as the DeepSeek memory block's low-rank q/k/v expansion applies it
+ * (models/deepseek/ops/compiled_tensor_ops.py:12-41, expand_grouped_qkv): for every token t and
+ * group g of a row of `groups` latents of `rank` values,
+ *   out[t, g, :] = bf16( (x * rsqrt(mean(x^2) + eps[g])) * weight[g, :] ),  x = fp32(x[t, g, :])
+ * The q latent is one group. The up-projections that follow are plain (grouped) GEMMs. */
+typedef struct memt_latent_norm_args {
+  uint32_t struct_size;    /* sizeof(memt_latent_norm_args)                     */
+  int32_t groups;          /* G >= 1                                            */
+  int32_t rank;            /* R, a multiple of 8                                */
+  int64_t total_tokens;    /* L                                                 */
+  const void *x;           /* bf16 token rows, group g at column g*R            */
+  int64_t x_stride;        /* elements per token row (>= G*R, a multiple of 8)  */
+  const void *weight;      /* bf16 [G, R] gains                                 */
+  const float *eps;        /* device fp32 [G] epsilons, or NULL: eps_scalar     */
+  float eps_scalar;
+  void *out;               /* bf16 [L, G, R]                                    */
+} memt_latent_norm_args;
+
+int memt_latent_rms_norm(const memt_latent_norm_args *args, memt_stream_t stream);
+
 /* ---- kernel timing (benchmarks) ----------------------------------------
  *
  * No counterpart in the reference (its kernels are timed from Python). When enabled,
  * every kernel this library launches is bracketed by CUDA events on its own stream and
  * its device time is accumulated per kernel family; disabled (the default) it costs
  * nothing. Families: 0 plan, 1 intra (WY operands), 2 scan, 3 read (GEMV),
- * 4 read (tensor-core tiles), 5 fp32 recurrence, 6 Qwen prologue.
+ * 4 read (tensor-core tiles), 5 fp32 recurrence, 6 prologue and latent norm.
  */
 #define MEMT_PROF_FAMILIES 7
 int memt_profiler_enable(int on);

@@ -29,7 +29,8 @@ extern "C" int memt_qwen_prologue(const memt_qwen_prologue_args* a, memt_stream_
   if (a == nullptr || a->struct_size != sizeof(memt_qwen_prologue_args)) return MEMT_ERR_INVALID_ARGUMENT;
   const int D = a->head_dim;
   if (D != 64 && D != 128 && D != 256) return MEMT_ERR_UNSUPPORTED;
-  if (a->num_heads < 1 || a->total_tokens < 0) return MEMT_ERR_INVALID_ARGUMENT;
+  if (a->num_heads < 1 || a->total_tokens < 0 || (a->norm_kind != 0 && a->norm_kind != 1))
+    return MEMT_ERR_INVALID_ARGUMENT;
   const void* ptrs[] = {a->q, a->k, a->erase_latent, a->write_latent, a->decay_latent, a->decay_bias,
                         a->decay_scale_log, a->q_out, a->k_out, a->write_out, a->log_decay_out};
   for (const void* ptr : ptrs)
@@ -59,6 +60,7 @@ extern "C" int memt_qwen_prologue(const memt_qwen_prologue_args* a, memt_stream_
   p.bias = static_cast<const __nv_bfloat16*>(a->decay_bias);
   p.scale_log = static_cast<const __nv_bfloat16*>(a->decay_scale_log);
   p.eps = a->eps;
+  p.rsqrt_norm = a->norm_kind;
   p.q_out = static_cast<__nv_bfloat16*>(a->q_out);
   p.k_out = static_cast<__nv_bfloat16*>(a->k_out);
   p.w_out = static_cast<__nv_bfloat16*>(a->write_out);

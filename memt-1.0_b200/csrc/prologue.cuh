@@ -4,6 +4,8 @@
 //
 //   q_hat      = bf16(q * 1/sqrt(sum q^2 + eps))                 l2norm(q)
 //   k_hat      = bf16(k * 1/sqrt(sum k^2 + eps))                 l2norm(k)
+//                (or x * rsqrt(sum x^2 + eps): the DeepSeek block's l2norm,
+//                 models/deepseek/ops/normalization.py:6-8)
 //   erase_sqrt = bf16(exp(0.5 * logsigmoid(e)))                  _write_gates, erase
 //   k'         = bf16(erase_sqrt * k_hat)                        _symmetric_inputs
 //   write      = bf16(sigmoid(w))                                _write_gates, write
@@ -31,6 +33,7 @@ struct PrologueParams {
   const __nv_bfloat16* bias;                            // [H*D]
   const __nv_bfloat16* scale_log;                       // [H]
   float eps;
+  int32_t rsqrt_norm;                                   // l2norm as x * rsqrt(.) instead of x / sqrt(.)
   __nv_bfloat16 *q_out, *k_out, *w_out;                 // [L, H, D]
   float* g_out;                                         // [L, H, D]
 };
@@ -96,7 +99,8 @@ __global__ void __launch_bounds__(256) qwen_prologue_kernel(PrologueParams p) {
     qq = row_sum<LPR>(qq);
     kk = row_sum<LPR>(kk);
     if (!ok) continue;
-    const float rq = 1.f / sqrtf(qq + p.eps), rk = 1.f / sqrtf(kk + p.eps);
+    const float rq = p.rsqrt_norm ? rsqrtf(qq + p.eps) : 1.f / sqrtf(qq + p.eps);
+    const float rk = p.rsqrt_norm ? rsqrtf(kk + p.eps) : 1.f / sqrtf(kk + p.eps);
     const float dscale = -expf(sl);
     float qo[8], ko[8], wo[8], go[8];
 #pragma unroll

@@ -5,13 +5,13 @@ Drop-in operators for the reference plugin's operator layer (``token_memory_pack
 readout and the BASELINE-style ``gdn2_chunked`` entry, all over the C ABI in ``include/memt_gdn2.h``.
 """
 
-from . import shard, snapshots
+from . import flash, shard, snapshots
 from .layout import ChunkPlan, boundaries, build_chunk_plan, packed_plan
 from .ops import (Workspace, gdn2_chunked, gdn2_update, memory_readout, memt_gdn2_read_fwd, qwen_prologue,
                   snapshot_read, token_memory_packed)
 
 __all__ = [
-    "ChunkPlan", "boundaries", "build_chunk_plan", "packed_plan", "Workspace", "gdn2_chunked", "gdn2_update",
+    "ChunkPlan", "boundaries", "build_chunk_plan", "flash", "packed_plan", "Workspace", "gdn2_chunked", "gdn2_update",
     "memory_readout", "memt_gdn2_read_fwd", "qwen_prologue", "shard", "snapshot_read", "snapshots",
     "token_memory_packed",
 ]

@@ -78,8 +78,17 @@ class PrologueArgs(_SizedArgs):
         ("q", c_void_p), ("q_stride", c_int64), ("k", c_void_p), ("k_stride", c_int64),
         ("erase_latent", c_void_p), ("erase_stride", c_int64), ("write_latent", c_void_p),
         ("write_stride", c_int64), ("decay_latent", c_void_p), ("decay_stride", c_int64),
-        ("decay_bias", c_void_p), ("decay_scale_log", c_void_p), ("eps", c_float), ("q_out", c_void_p),
+        ("decay_bias", c_void_p), ("decay_scale_log", c_void_p), ("eps", c_float), ("norm_kind", c_int32),
+        ("q_out", c_void_p),
         ("k_out", c_void_p), ("write_out", c_void_p), ("log_decay_out", c_void_p),
+    ]
+
+
+class LatentNormArgs(_SizedArgs):
+    _fields_ = [
+        ("struct_size", c_uint32),
+        ("groups", c_int32), ("rank", c_int32), ("total_tokens", c_int64), ("x", c_void_p), ("x_stride", c_int64),
+        ("weight", c_void_p), ("eps", c_void_p), ("eps_scalar", c_float), ("out", c_void_p),
     ]
 
 
@@ -97,6 +106,7 @@ SIGNATURES = {
     "memt_gdn2_update_read": (c_int, [POINTER(UpdateArgs), c_void_p, c_size_t, POINTER(ReadArgs), c_void_p]),
     "memt_memory_readout": (c_int, [POINTER(ReadoutArgs), c_void_p]),
     "memt_qwen_prologue": (c_int, [POINTER(PrologueArgs), c_void_p]),
+    "memt_latent_rms_norm": (c_int, [POINTER(LatentNormArgs), c_void_p]),
     "memt_gdn2_update_noalloc": (c_int, [POINTER(UpdateArgs), c_void_p]),
     "memt_gdn2_noalloc_status": (c_int, [c_void_p, POINTER(c_int32)]),
     "memt_profiler_enable": (c_int, [c_int]),

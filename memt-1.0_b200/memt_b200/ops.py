@@ -365,7 +365,8 @@ def _token_rows(x, L, H, D, name):
     return x, x.stride(0) if L > 1 else H * D
 
 
-def qwen_prologue(q, k, erase_gate, write_gate, decay_latent, decay_bias, decay_scale_log, *, eps=1e-6):
+def qwen_prologue(q, k, erase_gate, write_gate, decay_latent, decay_bias, decay_scale_log, *, eps=1e-6,
+                  rsqrt_norm=False):
     """The Qwen memory block's prologue in one kernel: (q_hat, k_scaled, write, log_decay).
 
     Replaces ``QwenMemoryBlock._write_gates`` / ``_log_decay`` / ``_symmetric_inputs``
@@ -376,7 +377,8 @@ def qwen_prologue(q, k, erase_gate, write_gate, decay_latent, decay_bias, decay_
     reference splits out of its gate projection and ``decay_latent`` is ``f_down`` of its
     decay rows; q, k and the gates may be the projections' split views. The erase factor the
     update needs afterwards is one, so call ``token_memory_packed`` with ``erase=None``.
-    Outputs are [1, L, H, D] (bf16; log_decay fp32).
+    Outputs are [1, L, H, D] (bf16; log_decay fp32). ``rsqrt_norm`` selects the DeepSeek
+    block's l2norm, x * rsqrt(sum x^2 + eps) (models/deepseek/ops/normalization.py:6-8).
     """
     q4 = q if q.dim() == 4 else q[None]
     if q4.dim() != 4:
@@ -403,7 +405,8 @@ def qwen_prologue(q, k, erase_gate, write_gate, decay_latent, decay_bias, decay_
         num_heads=H, head_dim=D, total_tokens=L, q=q2.data_ptr(), q_stride=sq, k=k2.data_ptr(), k_stride=sk,
         erase_latent=e2.data_ptr(), erase_stride=se, write_latent=w2.data_ptr(), write_stride=sw,
         decay_latent=d2.data_ptr(), decay_stride=sd, decay_bias=bias.data_ptr(),
-        decay_scale_log=scale_log.data_ptr(), eps=float(eps), q_out=q_out.data_ptr(), k_out=k_out.data_ptr(),
+        decay_scale_log=scale_log.data_ptr(), eps=float(eps), norm_kind=1 if rsqrt_norm else 0,
+        q_out=q_out.data_ptr(), k_out=k_out.data_ptr(),
         write_out=w_out.data_ptr(), log_decay_out=g_out.data_ptr())
     _lib.check(lib.memt_qwen_prologue(ctypes.byref(args), _stream(dev)), "memt_qwen_prologue")
     return q_out[None], k_out[None], w_out[None], g_out[None]

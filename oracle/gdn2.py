@@ -27,6 +27,9 @@ It restates, in numpy, the reference's algorithm for the memory path:
 * ``l2norm``          x / sqrt(sum x^2 + eps)   (_vendor/fla/modules/l2norm.py:95-109).
 * ``qwen_gates``, ``qwen_prologue``  gates, decay and the symmetric q/k inputs of the Qwen
                       memory block (models/qwen/layer.py:71-97).
+* ``latent_rms_norm``, ``expand_grouped_qkv``, ``memory_inject``  the DeepSeek block's grouped
+                      low-rank q/k/v expansion and wo_a injection
+                      (models/deepseek/ops/compiled_tensor_ops.py:12-41, integration.py:56-72).
 * ``plan_chunks``     write events every ``chunk_tokens`` inside each sample, 64-token tiles
                       inside each event (models/qwen/ops/packed.py:16-31, ops/layout.py:128-189).
 
@@ -339,6 +342,42 @@ def qwen_prologue(q, k, erase_gate, write_gate, decay_latent, decay_bias, decay_
 
         return l2(q), bf16(es.astype(f) * l2(k).astype(f)), w, g
     return l2norm(q, eps), es * l2norm(k, eps), w, g
+
+
+def latent_rms_norm(x, weight, eps):
+    """_latent_norm (models/deepseek/ops/compiled_tensor_ops.py:12-20) on bf16 latents
+    [T, G, R] in float32: bf16((x * rsqrt(mean(x^2) + eps[g])) * weight[g])."""
+    f = np.float32
+    x = np.asarray(x, f)
+    w = np.asarray(weight, f).reshape(1, x.shape[1], x.shape[2])
+    e = np.broadcast_to(np.asarray(eps, f).reshape(-1), (x.shape[1],)).reshape(1, -1, 1)
+    ms = (x * x).sum(-1, keepdims=True, dtype=f) / f(x.shape[-1])
+    return bf16((x * (f(1) / np.sqrt(ms + e))) * w)
+
+
+def expand_grouped_qkv(q, k, v, q_norm, q_up, q_eps, k_up, v_up, k_norm, v_norm, k_eps, v_eps):
+    """expand_grouped_qkv (models/deepseek/ops/compiled_tensor_ops.py:23-41): q [T, q_rank],
+    k, v [T, G * rank], q_up [Vd, q_rank], k_up, v_up [G, width, rank]; bf16 outputs of float64
+    products of the bf16 normalised latents."""
+    T = q.shape[0]
+    qn = latent_rms_norm(np.asarray(q).reshape(T, 1, -1), np.asarray(q_norm).reshape(1, -1), q_eps)[:, 0]
+    qo = bf16(qn @ _id(q_up).T)
+
+    def expand(lat, up, gain, eps):
+        G, W, R = up.shape
+        n = latent_rms_norm(np.asarray(lat).reshape(T, G, R), gain, eps)
+        return bf16(np.einsum("tgr,gwr->tgw", n, _id(up))).reshape(T, G * W)
+
+    return qo, expand(k, k_up, k_norm, k_eps), expand(v, v_up, v_norm, v_eps)
+
+
+def memory_inject(memory, wo_a, groups, residual):
+    """residual + einsum("tgd,grd->tgr") of the memory output and wo_a
+    (models/deepseek/integration.py:56-61,66-72), exact (float64)."""
+    T = memory.shape[0]
+    m = _id(memory).reshape(T, groups, -1)
+    w = _id(wo_a).reshape(groups, -1, m.shape[-1])
+    return _id(residual) + np.einsum("tgd,grd->tgr", m, w).reshape(T, -1)
 
 
 def gated_rms_norm(x, gate, weight, eps, softcap, *, mode="exact"):

@@ -242,6 +242,48 @@ def qwen_prologue_case(name, seed, L, H, D):
     print(f"{name}: done", flush=True)
 
 
+def flash_projection_case(name, seed, T, groups, rank, width, q_rank, H, D):
+    """The DeepSeek memory block's projections, eager on CPU in bf16: expand_grouped_qkv
+    (latent norms + grouped up-projections), expand_write_gates's gate math on given b_up /
+    w_up / f_down outputs (the three linears replaced by identity weights) and
+    prepare_stable_qk (DeepSeek rsqrt l2norm, erase fold)."""
+    from memt_sglang.models.deepseek.ops.compiled_tensor_ops import (expand_grouped_qkv, expand_write_gates,
+                                                                   prepare_stable_qk)
+
+    rng = np.random.default_rng(seed)
+    bf = torch.bfloat16
+
+    def t(*shape, scale=1.0, mean=0.0):
+        return torch.from_numpy((mean + scale * rng.standard_normal(shape)).astype(np.float32)).to(bf)
+
+    q_lat, k_lat, v_lat = t(T, q_rank), t(T, groups * rank), t(T, groups * rank)
+    q_norm, k_norm, v_norm = t(q_rank, scale=0.1, mean=1.0), t(groups, rank, scale=0.1, mean=1.0), \
+        t(groups, rank, scale=0.1, mean=1.0)
+    q_up = t(H * D, q_rank, scale=q_rank ** -0.5)
+    k_up, v_up = t(groups, width, rank, scale=rank ** -0.5), t(groups, width, rank, scale=rank ** -0.5)
+    eps = 1e-6
+    with torch.no_grad():
+        q, k, v = expand_grouped_qkv(q_lat, k_lat, v_lat, q_norm, q_up, eps, k_up, v_up, k_norm, v_norm,
+                                     (eps,) * groups, (eps,) * groups)
+        e_lat, w_lat, d_lat = t(1, T, H * D), t(1, T, H * D), t(1, T, H * D, mean=-2.0, scale=0.5)
+        eye = torch.eye(H * D, dtype=bf)
+        bias, scale_log = t(H * D, scale=0.3), t(H, scale=0.3)
+        erase, write, log_decay = expand_write_gates(e_lat, w_lat, d_lat, eye, eye, eye, bias, scale_log, H, D)
+        query, key = prepare_stable_qk(q.view(1, T, H, D), k.view(1, T, H, D), erase)
+
+    def f32(x):
+        return x.detach().float().numpy()
+
+    np.savez_compressed(
+        HERE / f"{name}.npz", q_lat=f32(q_lat), k_lat=f32(k_lat), v_lat=f32(v_lat), q_norm=f32(q_norm),
+        k_norm=f32(k_norm), v_norm=f32(v_norm), q_up=f32(q_up), k_up=f32(k_up), v_up=f32(v_up), eps=np.float32(eps),
+        q=f32(q), k=f32(k), v=f32(v), erase_gate=f32(e_lat)[0], write_gate=f32(w_lat)[0], decay_latent=f32(d_lat)[0],
+        decay_bias=f32(bias), decay_scale_log=f32(scale_log), erase=f32(erase)[0], write=f32(write)[0],
+        log_decay=f32(log_decay)[0], query=f32(query)[0], key=f32(key)[0], groups=np.int32(groups),
+        heads=np.int32(H), head_dim=np.int32(D))
+    print(f"{name}: done", flush=True)
+
+
 def main():
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference", required=True, help="path to the MemT-1.0 checkout")
@@ -271,6 +313,8 @@ def main():
         "l2norm": lambda: l2norm_case("l2norm", 6, 300, 128),
         # the Qwen memory block's gates, decay and symmetric q/k inputs (layer.py:71-97)
         "qwen_prologue": lambda: qwen_prologue_case("qwen_prologue", 7, 37, 2, 64),
+        # the DeepSeek block's grouped low-rank q/k/v expansion, gates and q/k preparation
+        "flash_projections": lambda: flash_projection_case("flash_projections", 8, 33, 2, 64, 128, 96, 4, 64),
     }
     for name, fn in cases.items():
         if args.only and name not in args.only.split(","):

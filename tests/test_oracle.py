@@ -186,3 +186,35 @@ def test_torch_cpu_restatement_matches_reference_golden(golden):
     assert O.rel_fro(s, z["final_state"]) < 1e-5
     o = OT.read(t(z["q"]), t(z["r0"]), list(z["cu_seqlens"]), float(z["scale"])).numpy()
     assert O.rel_fro(o, z["read"]) < 1e-5
+
+
+def test_flash_projections_match_reference(golden):
+    """The DeepSeek block's projections run by the reference (eager, bf16 on CPU) against the
+    oracle: the grouped latent norms and up-projections, the gates, the rsqrt l2norm of q and k
+    with the erase fold. bf16 results: relative Frobenius within bf16 rounding (the reference
+    accumulates its bf16 matmuls in its own order)."""
+    z = golden("flash_projections")
+    G = int(z["groups"])
+    eps = float(z["eps"])
+    q, k, v = O.expand_grouped_qkv(z["q_lat"], z["k_lat"], z["v_lat"], z["q_norm"], z["q_up"], eps, z["k_up"],
+                                   z["v_up"], z["k_norm"], z["v_norm"], [eps] * G, [eps] * G)
+    for got, ref in ((q, z["q"]), (k, z["k"]), (v, z["v"])):
+        assert O.rel_fro(got, ref) < 5e-3
+    es, w, g = O.qwen_gates(z["erase_gate"].reshape(z["erase"].shape), z["write_gate"].reshape(z["write"].shape),
+                            z["decay_latent"].reshape(z["log_decay"].shape), z["decay_bias"], z["decay_scale_log"],
+                            mode="bf16")
+    assert O.rel_fro(es, z["erase"]) < 4e-3 and O.rel_fro(w, z["write"]) < 4e-3
+    assert O.rel_fro(g, z["log_decay"]) < 1e-6
+    H, D = int(z["heads"]), int(z["head_dim"])
+    qh = O.l2norm(z["q"].reshape(-1, H, D), 1e-6)
+    kh = O.bf16(O.l2norm(z["k"].reshape(-1, H, D), 1e-6)) * z["erase"]
+    assert O.rel_fro(qh, z["query"]) < 4e-3 and O.rel_fro(kh, z["key"]) < 4e-3
+
+
+def test_memory_inject_is_a_grouped_product():
+    rng = np.random.default_rng(3)
+    T, G, d, r = 5, 2, 8, 3
+    m, w, res = rng.standard_normal((T, G * d)), rng.standard_normal((G * r, d)), rng.standard_normal((T, G * r))
+    out = O.memory_inject(m, w, G, res)
+    for g in range(G):
+        assert np.allclose(out[:, g * r:(g + 1) * r], res[:, g * r:(g + 1) * r] + m[:, g * d:(g + 1) * d] @ w[g * r:(g + 1) * r].T)
