@@ -126,8 +126,8 @@ typedef struct memt_gdn2_update_args {
   int32_t chunk_tokens;    /* write-event length (reference chunk_tokens), >= 1 */
   int32_t dtype;           /* MEMT_BF16 or MEMT_F32                             */
   const int32_t *cu_seqlens; /* device [N+1]                                    */
-  const void *k;           /* [L,H,K] (already L2-normalised)                   */
-  const void *v;           /* [L,H,V]                                           */
+  const void *k;           /* [L,H,K] (already L2-normalised), rows of k_stride  */
+  const void *v;           /* [L,H,V], rows of v_stride                         */
   const float *g;          /* log-decay, layout g_layout (PER_HEAD or PER_CHANNEL) */
   int32_t g_layout;
   const void *beta;        /* sqrt(beta) folded into k; NONE / PER_HEAD / PER_CHANNEL */
@@ -149,6 +149,12 @@ typedef struct memt_gdn2_update_args {
   int32_t num_initial_slots;
   const int32_t *final_slots;
   int32_t num_final_slots;
+  /* Elements per token row of k, v and write (0: H*K, the contiguous layout). A larger stride
+   * (a multiple of 8, bf16 update only) reads k, v or the write gate in place from a wider
+   * buffer, e.g. the split views of one q/k/v projection output. */
+  int64_t k_stride;
+  int64_t v_stride;
+  int64_t write_stride;
 } memt_gdn2_update_args;
 
 /* Workspace bytes memt_gdn2_update needs for these sizes (0 on invalid sizes). */

@@ -287,6 +287,7 @@ struct IntraParams {
   int32_t beta_layout;  // 0 none, 1 per head, 2 per channel
   const __nv_bfloat16* erase;  // per channel or null
   const __nv_bfloat16* write;  // per channel or null
+  int64_t sk, sv, sw;          // elements per token row of k, v and write (>= H*D)
   __nv_bfloat16* W;
   __nv_bfloat16* U;
   __nv_bfloat16* KG;

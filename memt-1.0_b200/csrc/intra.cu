@@ -13,9 +13,10 @@ static int launch_intra_t(const IntraParams& p0, int64_t max_chunks, cudaStream_
   cudaError_t e = cudaSuccess;
   if constexpr (Cfg::kTma) {  // [L][H*D] bf16 rows, boxes of 64 channels x 64 tokens
     const uint64_t row = static_cast<uint64_t>(p.H) * D, rows = static_cast<uint64_t>(p.L);
-    e = make_tmap_bf16_2d(&p.k_map, p.k, row, rows, row * 2, 64, kTile);
-    if (e == cudaSuccess) e = make_tmap_bf16_2d(&p.v_map, p.v, row, rows, row * 2, 64, kTile);
-    if (e == cudaSuccess && p.write != nullptr) e = make_tmap_bf16_2d(&p.w_map, p.write, row, rows, row * 2, 64, kTile);
+    e = make_tmap_bf16_2d(&p.k_map, p.k, row, rows, static_cast<uint64_t>(p.sk) * 2, 64, kTile);
+    if (e == cudaSuccess) e = make_tmap_bf16_2d(&p.v_map, p.v, row, rows, static_cast<uint64_t>(p.sv) * 2, 64, kTile);
+    if (e == cudaSuccess && p.write != nullptr)
+      e = make_tmap_bf16_2d(&p.w_map, p.write, row, rows, static_cast<uint64_t>(p.sw) * 2, 64, kTile);
     if (e != cudaSuccess) return cuda_status(e);
   }
   e = ensure_smem(kernel, Cfg::kSmem);

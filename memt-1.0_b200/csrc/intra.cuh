@@ -60,8 +60,9 @@ struct IntraCfg {
   // per-head decay without erase, D <= 128: k, v and write tiles arrive by TMA (the tiles need
   // the 1024-byte aligned base of the 128-byte swizzle)
   static constexpr bool kTma = HEAD && !ERASE && kPanels == 1;
-  // the fifth tile: the TMA loop's second k buffer, or the output tile of the panel loop (D = 256)
-  static constexpr bool kNeedO = kTma || kPanels > 1;
+  // the fifth tile: the TMA loop's second k buffer (the panel loop of D = 256 writes its products
+  // into the write-gate tile, which is free at those points)
+  static constexpr bool kNeedO = kTma;
   // sK | sB? | sV | sW (later the w operand) | sO? | sE? | sA | sAi
   static constexpr size_t offK = 0;
   static constexpr size_t offB = offK + kTileB;
@@ -223,21 +224,21 @@ struct IntraKernel {
   bool fast;
 
   // async copy of one [64][P] bf16 panel (rows >= len zero-filled) into a swizzled tile
-  __device__ __forceinline__ void load_tile(__nv_bfloat16* dst, const __nv_bfloat16* src, int c0) {
-    load_tile_for<0, NT>(dst, src, c0, tok0, len, h);
+  __device__ __forceinline__ void load_tile(__nv_bfloat16* dst, const __nv_bfloat16* src, int c0, int64_t stride) {
+    load_tile_for<0, NT>(dst, src, c0, tok0, len, h, stride);
   }
   // the same for an explicit (token range, head) and the threads [T0, T0 + NTH)
   template <int T0, int NTH>
   __device__ __forceinline__ void load_tile_for(__nv_bfloat16* dst, const __nv_bfloat16* src, int c0, int tk0,
-                                                int ln, int hd) {
-    const __nv_bfloat16* base = src + (int64_t)tk0 * row_stride + (int64_t)hd * D + c0;
+                                                int ln, int hd, int64_t stride) {
+    const __nv_bfloat16* base = src + (int64_t)tk0 * stride + (int64_t)hd * D + c0;
     constexpr int kChunks = kTile * P / 8;
     static_assert(kChunks % NTH == 0, "chunks per thread");
 #pragma unroll
     for (int i = tid - T0; i < kChunks; i += NTH) {
       const int row = i / (P / 8), col = (i % (P / 8)) * 8;
       const bool valid = row < ln;
-      cp_async16_zfill(dst + pswz(row, col), valid ? base + (int64_t)row * row_stride + col : src, valid);
+      cp_async16_zfill(dst + pswz(row, col), valid ? base + (int64_t)row * stride + col : src, valid);
     }
   }
 
@@ -388,10 +389,11 @@ struct IntraKernel {
   }
 
   // Element (row, col) of the per-channel decay table: rows of P floats whose 16-byte chunks
-  // are XOR-permuted by (row & 7), so that the score fragments (8 rows x 4 channel pairs) fall
-  // in distinct banks without padding; chunk-granular, so cp.async fills it directly.
+  // are XOR-permuted by (2 row) & 7, so that a half-warp's score fragment reads (4 rows x 4
+  // channel pairs of two adjacent chunks) fall in distinct banks without padding;
+  // chunk-granular, so cp.async fills it directly.
   __device__ __forceinline__ static int eidx(int row, int col) {
-    return row * Cfg::kLdE + ((((col >> 2) ^ row) & 7) | ((col >> 2) & ~7)) * 4 + (col & 3);
+    return row * Cfg::kLdE + ((((col >> 2) ^ (row << 1)) & 7) | ((col >> 2) & ~7)) * 4 + (col & 3);
   }
 
   // ---- decay, per-channel layout: cumulative sum and factor tables of one panel ----
@@ -1063,19 +1065,19 @@ struct IntraKernel {
       }
     };
     auto load_key_panel = [&](int c0) {
-      load_tile(kcur, p.k, c0);
-      if constexpr (ERASE) load_tile(sB, p.erase, c0);
+      load_tile(kcur, p.k, c0, p.sk);
+      if constexpr (ERASE) load_tile(sB, p.erase, c0, row_stride);
       if constexpr (!HEAD) load_decay(c0);
     };
     auto load_value_panel = [&](int c0) {
-      load_tile(sV, p.v, c0);
-      if (p.write != nullptr) load_tile(sW, p.write, c0);
+      load_tile(sV, p.v, c0, p.sv);
+      if (p.write != nullptr) load_tile(sW, p.write, c0, p.sw);
     };
     // with the solve / staging split only the staging warps use v and w: they load them alone
     auto load_value_panel_staging = [&]() {
       if (warp >= 4) {
-        load_tile_for<128, 128>(sV, p.v, 0, tok0, len, h);
-        if (p.write != nullptr) load_tile_for<128, 128>(sW, p.write, 0, tok0, len, h);
+        load_tile_for<128, 128>(sV, p.v, 0, tok0, len, h, p.sv);
+        if (p.write != nullptr) load_tile_for<128, 128>(sW, p.write, 0, tok0, len, h, p.sw);
       }
     };
     auto prepare_key_panel = [&](int c0) {  // after the key panel landed
@@ -1191,10 +1193,10 @@ struct IntraKernel {
           prepare_key_panel(c0);
           stage_w_kg<0, NT>(kcur, gKG, gEl, c0);
           __syncthreads();
-          wy_product(kcur, sO);
+          wy_product(kcur, sW);  // the write-gate tile is not loaded in this loop
           fence_proxy_async_smem();
           __syncthreads();
-          store_tile_async(gW, c0, sO);
+          store_tile_async(gW, c0, sW);
           if (tid == 0) bulk_wait_read();
           __syncthreads();
         }
@@ -1206,11 +1208,12 @@ struct IntraKernel {
           __syncthreads();
           stage_u<0, NT>(p);
           __syncthreads();
-          wy_product(sV, sO);
+          wy_product(sV, sW);  // the write gate is folded into the u operand: its tile is free
           fence_proxy_async_smem();
           __syncthreads();
-          store_tile_async(gU, c0, sO);
+          store_tile_async(gU, c0, sW);
           if (tid == 0) bulk_wait_read();
+          __syncthreads();  // the next panel's value loads overwrite the tile the store read
         }
       }
       if (!has_next) {

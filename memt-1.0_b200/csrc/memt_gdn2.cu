@@ -82,6 +82,14 @@ int check_update(const memt_gdn2_update_args* a) {
     return MEMT_ERR_MISALIGNED;
   if ((a->initial_slots != nullptr && a->num_initial_slots < 1) || (a->final_slots != nullptr && a->num_final_slots < 1))
     return MEMT_ERR_INVALID_ARGUMENT;
+  const int64_t row = int64_t(a->num_heads) * a->key_dim;
+  const int64_t strides[] = {a->k_stride, a->v_stride, a->write_stride};
+  for (int64_t st : strides) {
+    if (st == 0) continue;
+    if (st < row) return MEMT_ERR_INVALID_ARGUMENT;
+    if (a->dtype != MEMT_BF16) return MEMT_ERR_UNSUPPORTED;  // the fp32 recurrence reads contiguous rows
+    if (st % 8 != 0) return MEMT_ERR_MISALIGNED;              // 16-byte token rows
+  }
   return MEMT_OK;
 }
 
@@ -110,6 +118,10 @@ int update_bf16_front(const memt_gdn2_update_args* a, void* ws, cudaStream_t s, 
   ip.beta_layout = a->beta_layout;
   ip.erase = static_cast<const __nv_bfloat16*>(a->erase);
   ip.write = static_cast<const __nv_bfloat16*>(a->write);
+  const int64_t row = int64_t(a->num_heads) * D;
+  ip.sk = a->k_stride > 0 ? a->k_stride : row;
+  ip.sv = a->v_stride > 0 ? a->v_stride : row;
+  ip.sw = a->write_stride > 0 ? a->write_stride : row;
   ip.W = reinterpret_cast<__nv_bfloat16*>(base + w.W);
   ip.KG = reinterpret_cast<__nv_bfloat16*>(base + w.KG);
   ip.U = reinterpret_cast<__nv_bfloat16*>(base + w.U);

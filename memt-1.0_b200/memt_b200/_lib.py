@@ -45,7 +45,7 @@ class UpdateArgs(_SizedArgs):
         ("beta", c_void_p), ("beta_layout", c_int32), ("erase", c_void_p), ("erase_layout", c_int32),
         ("write", c_void_p), ("write_layout", c_int32), ("initial_state", c_void_p), ("final_state", c_void_p),
         ("initial_slots", c_void_p), ("num_initial_slots", c_int32), ("final_slots", c_void_p),
-        ("num_final_slots", c_int32),
+        ("num_final_slots", c_int32), ("k_stride", c_int64), ("v_stride", c_int64), ("write_stride", c_int64),
     ]
 
 

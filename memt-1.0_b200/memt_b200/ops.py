@@ -87,6 +87,23 @@ def _check_lengths(lengths, total):
 
 def _tokens(x, name):
     """Accept [1, L, H, D] (reference layout) or [L, H, D]; return a contiguous [L, H, D] view."""
+    return _tokens_unchecked(x, name).contiguous()
+
+
+def _token_rows_view(x, name):
+    """[1, L, H, D] or [L, H, D] -> ([L, H, D] tensor, elements per token row) without a copy
+    when the heads of a token are contiguous and the token rows start on 16-byte boundaries (a
+    split view of a wider projection output, for instance); otherwise a contiguous copy."""
+    x = _tokens_unchecked(x, name)
+    L, H, D = x.shape
+    if (x.dtype == torch.bfloat16 and x.stride(2) == 1 and x.stride(1) == D and L > 1 and x.stride(0) >= H * D
+            and x.stride(0) % 8 == 0 and x.data_ptr() % 16 == 0):
+        return x, x.stride(0)
+    x = x.contiguous()
+    return x, H * D
+
+
+def _tokens_unchecked(x, name):
     if x.dim() == 4:
         if x.shape[0] != 1:
             raise ValueError(f"{name}: packed inputs have batch size 1")
@@ -95,7 +112,7 @@ def _tokens(x, name):
         raise ValueError(f"{name}: expected [1, L, H, D] or [L, H, D]")
     if not x.is_cuda:
         raise ValueError(f"{name}: expected a CUDA tensor")
-    return x.contiguous()
+    return x
 
 
 def _gate(x, L, H, D, name, dtype=None):
@@ -157,8 +174,12 @@ def gdn2_update(k, v, g, initial_state, cu_seqlens, *, num_samples, total_tokens
 def _update_args(k, v, g, initial_state, cu_seqlens, num_samples, total_tokens, beta, erase, write, chunk_tokens,
                  final_state, initial_slots=None, final_slots=None):
     """Checked C arguments of an update (plus the tensors they point into)."""
-    k = _tokens(k, "k")
-    v = _tokens(v, "v")
+    if _tokens_unchecked(k, "k").dtype == torch.bfloat16:  # bf16 rows are read in place
+        k, k_stride = _token_rows_view(k, "k")
+        v, v_stride = _token_rows_view(v, "v")
+    else:
+        k, v = _tokens(k, "k"), _tokens(v, "v")
+        k_stride = v_stride = 0
     L, H, K = k.shape
     V = v.shape[-1]
     if v.shape[:2] != (L, H) or v.dtype != k.dtype:
@@ -175,8 +196,12 @@ def _update_args(k, v, g, initial_state, cu_seqlens, num_samples, total_tokens, 
     erase, erase_layout = _gate(erase, L, H, K, "erase", k.dtype)
     if erase_layout == _lib.GATE_PER_HEAD:
         raise ValueError("erase must be per channel [L, H, K]")
+    w_stride = 0
     if write is not None:
-        write = _tokens(write, "write")
+        if k.dtype == torch.bfloat16:
+            write, w_stride = _token_rows_view(write, "write")
+        else:
+            write = _tokens(write, "write")
         if tuple(write.shape) != (L, H, V) or write.dtype != k.dtype:
             raise ValueError("write gate must be [L, H, V] in the value dtype")
     N = int(num_samples)
@@ -211,7 +236,9 @@ def _update_args(k, v, g, initial_state, cu_seqlens, num_samples, total_tokens, 
         initial_state=h0.data_ptr(), final_state=out.data_ptr(),
         initial_slots=in_slots.data_ptr() if in_slots is not None else None, num_initial_slots=n_in,
         final_slots=final_slots.data_ptr() if final_slots is not None else None,
-        num_final_slots=out.shape[0] if final_slots is not None else 0)
+        num_final_slots=out.shape[0] if final_slots is not None else 0,
+        k_stride=k_stride if k_stride != H * K else 0, v_stride=v_stride if v_stride != H * V else 0,
+        write_stride=w_stride if w_stride != H * V else 0)
     return lib, args, ws, out, (k, v, g, beta, erase, write, h0, in_slots, final_slots)
 
 
@@ -252,7 +279,7 @@ def token_memory_packed(q, k, v, log_decay, write, read_states, write_states, *,
     ``final_slots`` (default: write_slots, an in-place update); the pool is returned as
     final_state.
     """
-    L = _tokens(q, "q").shape[0]
+    L = _tokens_unchecked(q, "q").shape[0]
     _check_lengths(lengths, L)
     cu = _cu_seqlens(lengths, q.device)
     if write_slots is None and final_slots is not None:
@@ -422,7 +449,7 @@ def gdn2_chunked(q, k, v, g, beta, initial_state, cu_seqlens, *, w=None, scale=N
     cu_seqlens may live on the host (validated there) or on the device; with device offsets
     pass ``max_seqlen`` (the longest sample) to avoid a device-to-host copy.
     """
-    k3 = _tokens(k, "k")
+    k3 = _tokens_unchecked(k, "k")
     L, H, K = k3.shape
     if cu_seqlens.is_cuda and max_seqlen is not None:
         N = cu_seqlens.numel() - 1

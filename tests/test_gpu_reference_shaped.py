@@ -318,3 +318,28 @@ def test_read_fwd_takes_the_reference_chunk_plan(cuda):
     b = M.memt_gdn2_read_fwd(q, snaps, ref_like, D ** -0.5, torch.bfloat16)
     torch.cuda.synchronize()
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("gate", ["head", "channel"])
+def test_update_reads_split_projection_views_in_place(cuda, gate):
+    """k, v and the write gate as split views of one wider projection output (token rows of
+    3 H D elements) give the same states, bit for bit, as their contiguous copies: the kernels
+    read the rows in place (TMA maps and cp.async with the views' row strides)."""
+    L, H, D = 700, 2, 128
+    x = _latents(cuda, L, H, D, 77)
+    gen = torch.Generator(device=cuda).manual_seed(78)
+    w_all = torch.sigmoid(torch.randn(L, 2 * H * D, device=cuda, generator=gen)).to(torch.bfloat16)
+    w = w_all[:, H * D:].view(L, H, D)
+    gshape = (L, H, D) if gate == "channel" else (L, H)
+    g = torch.nn.functional.logsigmoid(2.0 + 0.5 * torch.randn(*gshape, device=cuda, generator=gen))
+    h0 = 0.02 * torch.randn(2, H, D, D, device=cuda, generator=gen)
+    cu = torch.tensor([0, 300, L], dtype=torch.int32, device=cuda)
+    k = (x.k.float() / x.k.float().norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+    kv = torch.cat([k.reshape(L, -1), x.v.reshape(L, -1)], dim=1)  # one [L, 2HD] buffer
+    k_view, v_view = kv[:, :H * D].view(L, H, D), kv[:, H * D:].view(L, H, D)
+    assert not k_view.is_contiguous() and not v_view.is_contiguous()
+    a = ops.gdn2_update(k_view, v_view, g, h0, cu, num_samples=2, total_tokens=L, write=w)
+    b = ops.gdn2_update(k_view.contiguous(), v_view.contiguous(), g, h0, cu, num_samples=2, total_tokens=L,
+                        write=w.contiguous())
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
