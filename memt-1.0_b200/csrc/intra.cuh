@@ -388,12 +388,14 @@ struct IntraKernel {
     sSeg = f + 9 * kTile;
   }
 
-  // Element (row, col) of the per-channel decay table: rows of P floats whose 16-byte chunks
-  // are XOR-permuted by (2 row) & 7, so that a half-warp's score fragment reads (4 rows x 4
-  // channel pairs of two adjacent chunks) fall in distinct banks without padding;
-  // chunk-granular, so cp.async fills it directly.
+  // Element (row, col) of the per-channel decay table: rows of P floats whose 16-byte chunks q
+  // are XOR-permuted within groups of eight by (2 row ^ q / 8) & 7, so that a half-warp's score
+  // fragment reads (4 rows x two adjacent chunks) and a quarter-warp's 16-byte staging reads
+  // (every other chunk of one row) fall in distinct banks without padding; chunk-granular, so
+  // cp.async fills it directly and a chunk stays 16 contiguous bytes.
   __device__ __forceinline__ static int eidx(int row, int col) {
-    return row * Cfg::kLdE + ((((col >> 2) ^ (row << 1)) & 7) | ((col >> 2) & ~7)) * 4 + (col & 3);
+    const int q = col >> 2;  // 16-byte chunk
+    return row * Cfg::kLdE + (((q ^ (row << 1) ^ (q >> 3)) & 7) | (q & ~7)) * 4 + (col & 3);
   }
 
   // ---- decay, per-channel layout: cumulative sum and factor tables of one panel ----
@@ -435,10 +437,6 @@ struct IntraKernel {
   __device__ __forceinline__ float2 p2d2(int i, int n, int c) const {
     const float2 gi = ld2(sE, i, c), gn = ld2(sE, n, c);
     return make_float2(fast_exp2(gi.x - gn.x), fast_exp2(gi.y - gn.y));
-  }
-  __device__ __forceinline__ float2 p22(int i, int c) const {
-    const float2 e = ld2(sE, i, c);
-    return make_float2(fast_exp2(e.x), fast_exp2(e.y));
   }
 
   // ---- key-key scores of this panel, accumulated into acc[piece] ----
@@ -882,9 +880,18 @@ struct IntraKernel {
       if constexpr (ERASE) bv = *reinterpret_cast<const uint4*>(bb + j * Wk::kStride);
       const uint32_t* bw = reinterpret_cast<const uint32_t*>(&bv);
       uint64_t eh = 0, qh = 0;
+      float gr[8], gl[8];  // per channel: G of this row and of the last token, channels col..col+7
       if constexpr (HEAD) {
         eh = f32x2_splat(sEh[row]);
         qh = f32x2_splat(sKgf[row]);
+      } else {
+#pragma unroll
+        for (int h4 = 0; h4 < 2; ++h4) {
+          const float4 a = *reinterpret_cast<const float4*>(sE + eidx(row, col + 4 * h4));
+          const float4 b = *reinterpret_cast<const float4*>(sE + eidx(last, col + 4 * h4));
+          gr[4 * h4] = a.x, gr[4 * h4 + 1] = a.y, gr[4 * h4 + 2] = a.z, gr[4 * h4 + 3] = a.w;
+          gl[4 * h4] = b.x, gl[4 * h4 + 1] = b.y, gl[4 * h4 + 2] = b.z, gl[4 * h4 + 3] = b.w;
+        }
       }
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -894,9 +901,10 @@ struct IntraKernel {
           e2 = eh;
           q2 = qh;
         } else {
-          const float2 ev = p22(row, col + 2 * e), qv = p2d2(last, row, col + 2 * e);
-          e2 = f32x2_pack(ev.x, ev.y);
-          q2 = f32x2_pack(row < len ? qv.x : 0.f, row < len ? qv.y : 0.f);
+          // 2^G (w operand) and 2^(G_last - G) (kg), wy_fast.py:110-116,125-139
+          e2 = f32x2_pack(fast_exp2(gr[2 * e]), fast_exp2(gr[2 * e + 1]));
+          q2 = row < len ? f32x2_pack(fast_exp2(gl[2 * e] - gr[2 * e]), fast_exp2(gl[2 * e + 1] - gr[2 * e + 1]))
+                         : f32x2_pack(0.f, 0.f);
         }
         kgw[e] = f32x2_to_bf16x2(mul_f32x2(k2, q2));
         if constexpr (ERASE) {
