@@ -29,7 +29,7 @@ static int launch_tile(const ReadParams& p, int64_t maxlen, cudaStream_t s) {
   using Cfg = ReadTileCfg<D>;
   cudaError_t e = ensure_smem(read_tile_kernel<D>, Cfg::kSmem);
   if (e != cudaSuccess) return cuda_status(e);
-  const int64_t per = int64_t(kReadTilesPerCta) * kTile;
+  const int64_t per = int64_t(read_tiles_per_cta<D>()) * kTile;
   int64_t groups = (maxlen + per - 1) / per;
   if (groups < 1) groups = 1;
   if (groups > 65535) return MEMT_ERR_UNSUPPORTED;

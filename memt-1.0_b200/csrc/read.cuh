@@ -270,7 +270,10 @@ __global__ void __launch_bounds__(256, (TQ == 1 && D <= 128) ? 3 : 2) read_gemv_
 // bf16 state panel [D][D] (swizzled) resident in shared memory; warps split rows
 // (4 row blocks of 16 tokens) and, for D = 256, column halves.
 // ---------------------------------------------------------------------------
-constexpr int kReadTilesPerCta = 8;
+// 64-token tiles per CTA run: each CTA stages its block's bf16 snapshot (D^2 * 2 bytes) once, so
+// a wider state takes longer runs (d = 256: 128 KB of staging per 2,048 tokens)
+template <int D>
+constexpr int read_tiles_per_cta() { return D >= 256 ? 32 : 8; }
 
 template <int D>
 struct ReadTileCfg {
@@ -305,6 +308,7 @@ __global__ void __launch_bounds__(ReadTileCfg<D>::kNW * 32) read_tile_kernel(Rea
   block_range(p, n, bos, eos);
   // this CTA's tiles: runs y, y + gridDim.y, ... of kReadTilesPerCta tiles, so that every token
   // is read whatever bound on the block length the host sized the grid with
+  constexpr int kReadTilesPerCta = read_tiles_per_cta<D>();
   const int ntiles = strided_tiles(eos - bos, kTile, kReadTilesPerCta);
   if (ntiles == 0) return;
   const int64_t slot = state_slot(p, n);
