@@ -785,6 +785,38 @@ def run_ours(args, rank, world, local_rank):
         dist.destroy_process_group()
 
 
+def run_leg(args):
+    """One leg alone on cuda:0 (profiling cases): the Qwen prologue of config 1 (--sessions sets the
+    size) or the config-2 decode readout."""
+    import torch
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    gen = torch.Generator(device=dev).manual_seed(1234)
+    hbm, _, _ = peaks()
+    stream = torch.cuda.current_stream(dev)
+    if args.only == "readout":
+        print(json.dumps(leg_readout(dev, gen, stream, hbm)), flush=True)
+        return
+    import memt_b200 as M
+
+    bf = torch.bfloat16
+    L = args.sessions * T
+    qkv = torch.randn(L, 3 * H * D, device=dev, generator=gen).to(bf)
+    gates = torch.randn(L, 2 * H * D + D, device=dev, generator=gen).to(bf)
+    decay = (-2.0 + 0.5 * torch.randn(L, H * D, device=dev, generator=gen)).to(bf)
+    bias, scale_log = torch.zeros(H * D, device=dev, dtype=bf), torch.zeros(H, device=dev, dtype=bf)
+    q, k = qkv[:, :H * D].view(L, H, D), qkv[:, H * D:2 * H * D].view(L, H, D)
+
+    def prologue():
+        return M.qwen_prologue(q, k, gates[:, :H * D], gates[:, H * D:2 * H * D], decay, bias, scale_log)
+
+    ms = time_steps(prologue, args.steps, args.warmup, stream)
+    nbytes = L * H * D * (5 * 2 + 3 * 2 + 4)
+    print(json.dumps({"leg": "prologue", "tokens": L, "ms": ms, "gbs": nbytes / (ms * 1e-3) / 1e9,
+                      "frac": nbytes / (ms * 1e-3) / 1e9 / hbm}), flush=True)
+
+
 def run_reference(args, rank, world):
     """The reference has no CPU implementation of its update (Triton only); its fp32 CPU
     restatement in the reference kernel order runs the config-1 step on every host thread."""
@@ -828,8 +860,9 @@ def main():
     ap.add_argument("--sessions", type=int, default=SESSIONS, help="sessions per GPU (profiling cases)")
     ap.add_argument("--gate", choices=["head", "channel"], default="head",
                     help="log-decay layout of the headline step (channel: profiling the per-channel path)")
-    ap.add_argument("--only", choices=["all", "update"], default="all",
-                    help="update: time only the commit step (no e2e, other legs, CPU baseline)")
+    ap.add_argument("--only", choices=["all", "update", "prologue", "readout"], default="all",
+                    help="update: time only the commit step (no e2e, other legs, CPU baseline); "
+                         "prologue / readout: only that leg (profiling cases)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -838,6 +871,8 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
     if args.impl == "reference":
         run_reference(args, rank, world)
+    elif args.only in ("prologue", "readout"):
+        run_leg(args)
     else:
         run_ours(args, rank, world, local_rank)
 
