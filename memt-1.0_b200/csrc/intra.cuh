@@ -1193,12 +1193,16 @@ struct IntraKernel {
         // ---- D = 256: panels one after the other ----
         if (warp < 4) solve();
         __syncthreads();
-        for (int pn = 0; pn < Cfg::kPanels; ++pn) {
+        // last panel first: its key tile (beta folded) and decay table are still resident from
+        // the score loop, so only the other panels are reloaded and prepared again
+        for (int pn = Cfg::kPanels - 1; pn >= 0; --pn) {
           const int c0 = pn * P;
-          load_key_panel(c0);
-          cp_async_commit();
-          cp_async_wait<0>();
-          prepare_key_panel(c0);
+          if (pn != Cfg::kPanels - 1) {
+            load_key_panel(c0);
+            cp_async_commit();
+            cp_async_wait<0>();
+            prepare_key_panel(c0);
+          }
           stage_w_kg<0, NT>(kcur, gKG, gEl, c0);
           __syncthreads();
           wy_product(kcur, sW);  // the write-gate tile is not loaded in this loop

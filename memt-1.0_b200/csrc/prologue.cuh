@@ -107,11 +107,17 @@ __global__ void __launch_bounds__(256) qwen_prologue_kernel(PrologueParams p) {
     for (int i = 0; i < 8; ++i) {
       qo[i] = q[i] * rq;
       const float kn = bf16_round(k[i] * rk);
-      // logsigmoid(x) = min(0, x) - log1p(exp(-|x|)); erase_sqrt = bf16(exp(0.5 logsigmoid(x)))
-      const float ls = fminf(0.f, e[i]) - log1pf(expf(-fabsf(e[i])));
-      const float es = bf16_round(expf(0.5f * ls));
+      // logsigmoid(x) = min(0, x) - log1p(exp(-|x|)); erase_sqrt = bf16(exp(0.5 logsigmoid(x))).
+      // erase_sqrt and the write gate are stored in bf16 (8-bit significand): CUDA's fast exp and
+      // log intrinsics (relative error ~1e-7 here) leave them unchanged except at rounding ties.
+      // log(1 + t) for t = exp(-|x|) in (0, 1]: where 1 + t rounds to 1 the true value (< 6e-8)
+      // moves erase_sqrt by less than half a bf16 unit.
+      const float t = __expf(-fabsf(e[i]));
+      const float ls = fminf(0.f, e[i]) - __logf(1.f + t);
+      const float es = bf16_round(__expf(0.5f * ls));
       ko[i] = es * kn;
-      wo[i] = 1.f / (1.f + expf(-w[i]));
+      wo[i] = __frcp_rn(1.f + __expf(-w[i]));
+      // the fp32 log-decay keeps the accurate functions (the reference's own fp32 arithmetic)
       const float x = d[i] + b[i];
       const float sp = x > 20.f ? x : log1pf(expf(x));  // softplus, threshold 20
       go[i] = dscale * sp;
