@@ -39,28 +39,33 @@ static int launch_tile(const ReadParams& p, int64_t maxlen, cudaStream_t s) {
   return cuda_status(cudaGetLastError());
 }
 
-// d = 128, bf16 queries, plain read: tcgen05 kernel with TMA query tiles
+// d = 128 / 256, bf16 queries, plain read: tcgen05 kernel with TMA query tiles
+template <int D>
 static int launch_read_tc(const ReadParams& p, int64_t maxlen, cudaStream_t s) {
+  using Cfg = ReadTcCfg<D>;
   ReadTcParams P;
   P.p = p;
-  const uint64_t row = static_cast<uint64_t>(p.H) * ReadTcCfg::D;
-  cudaError_t e = make_tmap_bf16_2d(&P.q_map, p.q, row, static_cast<uint64_t>(p.L), row * 2, 64, ReadTcCfg::kTok);
+  const uint64_t row = static_cast<uint64_t>(p.H) * D;
+  cudaError_t e = make_tmap_bf16_2d(&P.q_map, p.q, row, static_cast<uint64_t>(p.L), row * 2, 64, Cfg::kTok);
   if (e == cudaSuccess && p.out_bf16)
-    e = make_tmap_bf16_2d(&P.o_map, p.out, row, static_cast<uint64_t>(p.L), row * 2, 64, ReadTcCfg::kTok);
-  if (e == cudaSuccess) e = ensure_smem(read_tc_kernel, ReadTcCfg::kSmem);
+    e = make_tmap_bf16_2d(&P.o_map, p.out, row, static_cast<uint64_t>(p.L), row * 2, 64, Cfg::kTok);
+  if (e == cudaSuccess) e = ensure_smem(read_tc_kernel<D>, Cfg::kSmem);
   if (e != cudaSuccess) return cuda_status(e);
-  const int64_t per = int64_t(kReadTcTiles) * ReadTcCfg::kTok;
+  const int64_t per = int64_t(kReadTcTiles) * Cfg::kTok;
   int64_t groups = (maxlen + per - 1) / per;
   if (groups < 1) groups = 1;
   if (groups > 65535) return MEMT_ERR_UNSUPPORTED;
   dim3 grid(static_cast<unsigned>(p.num_blocks) * p.H, static_cast<unsigned>(groups));
   ProfScope prof(kProfReadTile, s);
-  read_tc_kernel<<<grid, ReadTcCfg::kThreads, ReadTcCfg::kSmem, s>>>(P);
+  read_tc_kernel<D><<<grid, Cfg::kThreads, Cfg::kSmem, s>>>(P);
   return cuda_status(cudaGetLastError());
 }
 
 int launch_read(const ReadParams& p, int D, bool exact, int64_t maxlen, cudaStream_t s) {
-  if (D == 128 && !exact && !p.fused && maxlen > kGemvMaxBlock) return launch_read_tc(p, maxlen, s);
+  if (!exact && !p.fused && maxlen > kGemvMaxBlock) {
+    if (D == 128) return launch_read_tc<128>(p, maxlen, s);
+    if (D == 256) return launch_read_tc<256>(p, maxlen, s);
+  }
   if (exact || maxlen <= kGemvMaxBlock) {
     switch (D) {
       case 64: return exact ? launch_gemv<64, true>(p, maxlen, s) : launch_gemv<64, false>(p, maxlen, s);

@@ -183,6 +183,12 @@ def test_config4_flash_full_length(cuda):
         ref = _oracle_state(k, v, g, w, h0, s * 16384, (s + 1) * 16384, s, h)
         err = O.rel_fro(_np(final[s, h:h + 1])[None], ref)
         assert err <= TOL_BF16, (s, h, err)
+    # the commit read of the incoming snapshot (d = 256 tensor-core tile read) for two slices
+    for s, h in ((1, 0), (3, 14)):
+        t0, t1 = s * 16384, (s + 1) * 16384
+        o_ref = O.read(_np(q[t0:t1, h:h + 1]), _np(h0[s:s + 1, h:h + 1]), np.array([0, 16384]), D ** -0.5,
+                       mode="bf16")
+        assert O.rel_fro(_np(read[0, t0:t1, h:h + 1]), o_ref) <= TOL_BF16
 
 
 # ---------------------------------------------------------------------------
