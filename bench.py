@@ -420,7 +420,7 @@ def leg_gpu_bar(dev, gen, args, stream, flush):
     return out
 
 
-def leg_head_sharded(dev, gen, args, stream, flush, rank, world, pg, hbm):
+def leg_head_sharded(dev, gen, args, stream, flush, rank, world, pg, hbm, only_config4=False):
     """Config 3 with heads split over the ranks (fixed global problem) and the per-GPU config-4
     shard (16 of 128 heads at d=256) with the attention-output all-reduce at N > 1."""
     import numpy as np
@@ -456,7 +456,7 @@ def leg_head_sharded(dev, gen, args, stream, flush, rank, world, pg, hbm):
 
     if pg:
         dist.barrier()
-    ms3 = time_steps(c3, max(3, args.steps // 2), args.warmup, stream, flush)
+    ms3 = 0.0 if only_config4 else time_steps(c3, max(3, args.steps // 2), args.warmup, stream, flush)
     del q, k, v, g, beta, w, h0
     # ---- config 4 shard: 4 x 16384 tokens, 16 heads of d=256 (this rank's TP8 slice) ----
     D4, H4, N4, T4 = 256, 16, 4, 16384
@@ -484,6 +484,8 @@ def leg_head_sharded(dev, gen, args, stream, flush, rank, world, pg, hbm):
     if pg:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
     ms3, ms4, ar_ms_max = [float(t) for t in vals.tolist()]
+    if only_config4:
+        ms3 = float("nan")
     b3 = L * H * update_bytes_per_token_head(D, False, True) + 32 * H * 12 * D * D
     res["config3"] = {
         "workload": f"config3: 32 sessions, lengths U[1K,32K] seed 3 ({L} tokens), H=16 split over {world} "
@@ -798,6 +800,11 @@ def run_leg(args):
     if args.only == "readout":
         print(json.dumps(leg_readout(dev, gen, stream, hbm)), flush=True)
         return
+    if args.only == "config4":
+        flush = torch.empty(256 * 2 ** 20, dtype=torch.uint8, device=dev)
+        res = leg_head_sharded(dev, gen, args, stream, flush, 0, 1, None, hbm, only_config4=True)
+        print(json.dumps(res), flush=True)
+        return
     import memt_b200 as M
 
     bf = torch.bfloat16
@@ -860,9 +867,9 @@ def main():
     ap.add_argument("--sessions", type=int, default=SESSIONS, help="sessions per GPU (profiling cases)")
     ap.add_argument("--gate", choices=["head", "channel"], default="head",
                     help="log-decay layout of the headline step (channel: profiling the per-channel path)")
-    ap.add_argument("--only", choices=["all", "update", "prologue", "readout"], default="all",
+    ap.add_argument("--only", choices=["all", "update", "prologue", "readout", "config4"], default="all",
                     help="update: time only the commit step (no e2e, other legs, CPU baseline); "
-                         "prologue / readout: only that leg (profiling cases)")
+                         "prologue / readout / config4: only that leg (profiling cases)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -871,7 +878,7 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
     if args.impl == "reference":
         run_reference(args, rank, world)
-    elif args.only in ("prologue", "readout"):
+    elif args.only in ("prologue", "readout", "config4"):
         run_leg(args)
     else:
         run_ours(args, rank, world, local_rank)
