@@ -2,6 +2,7 @@
 #include "launch.h"
 #include "scan.cuh"
 #include "scan_tc.cuh"
+#include "scan_tc256.cuh"
 
 namespace memt {
 
@@ -24,11 +25,21 @@ static int launch_scan_tc(const ScanParams& p, cudaStream_t s) {
   return cuda_status(launch_pdl(scan_tc_kernel, dim3(grid), dim3(ScanTcCfg::kThreads), ScanTcCfg::kSmem, s, p));
 }
 
+// d = 256: tcgen05 kernel, one CTA per (sample, head, 128-value half)
+static int launch_scan_tc256(const ScanParams& p, cudaStream_t s) {
+  cudaError_t e = ensure_smem(scan_tc256_kernel, ScanTc256Cfg::kSmem);
+  if (e != cudaSuccess) return cuda_status(e);
+  const unsigned grid = static_cast<unsigned>(p.N) * p.H * 2;
+  ProfScope prof(kProfScan, s);
+  return cuda_status(
+      launch_pdl(scan_tc256_kernel, dim3(grid), dim3(ScanTc256Cfg::kThreads), ScanTc256Cfg::kSmem, s, p));
+}
+
 int launch_scan(int D, const ScanParams& p, cudaStream_t s) {
   switch (D) {
     case 64: return launch_scan_t<64>(p, s);
     case 128: return launch_scan_tc(p, s);
-    case 256: return launch_scan_t<256>(p, s);
+    case 256: return launch_scan_tc256(p, s);
     default: return MEMT_ERR_UNSUPPORTED;
   }
 }
