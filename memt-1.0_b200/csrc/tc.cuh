@@ -1,7 +1,8 @@
 // Fifth-generation tensor cores (tcgen05) for sm_100a: tensor-memory allocation, shared-memory
 // operand descriptors, single-thread MMA issue with mbarrier completion, and tensor-memory
-// loads. Only the forms used by this library: cta_group::1, M = 128, bf16 (kind::f16) and
-// tf32 (kind::tf32) operands with fp32 accumulation, 128-byte swizzled operand tiles.
+// loads and stores. Only the forms used by this library: cta_group::1, M = 128, bf16 (kind::f16)
+// and tf32 (kind::tf32) operands with fp32 accumulation, 128-byte swizzled operand tiles, bf16 A
+// operands in tensor memory.
 //
 // Operand tiles (see pswz in common.cuh): rows of 128 bytes, 8-row groups of 1024 bytes
 // (SBO), 16-byte chunks XOR-permuted by (row & 7); tile bases 1024-byte aligned.
@@ -13,7 +14,9 @@
 // The tf32 kind truncates fp32 operands to tf32; callers that need round-to-nearest store
 // operands already rounded.
 // Accumulator (M = 128): row i of D is tensor-memory lane i, column j is column j (fp32).
-// Warp w of a CTA reads lanes 32 (w % 4) .. 32 (w % 4) + 31.
+// Warp w of a CTA reads and writes lanes 32 (w % 4) .. 32 (w % 4) + 31.
+// A operand in tensor memory (K-major, bf16): row i of A is lane i, column c holds the K
+// elements 2c (low half) and 2c + 1; a K step of 16 advances the address by 8 columns.
 #pragma once
 
 #include <cstdint>
@@ -60,6 +63,13 @@ __device__ __forceinline__ void mma_tf32(uint32_t d, uint64_t a, uint64_t b, uin
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
       " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
       "l"(a), "l"(b), "r"(id), "r"(static_cast<uint32_t>(acc)));
+}
+// D[tmem] (+)= A[tmem] . B, issued by one thread (bf16, A K-major in tensor memory)
+__device__ __forceinline__ void mma_bf16_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t id, bool acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d),
+      "r"(a), "l"(b), "r"(id), "r"(static_cast<uint32_t>(acc)));
 }
 // arrive on the mbarrier once all previously issued MMAs of this thread have completed
 __device__ __forceinline__ void commit(uint32_t mbar) {
@@ -139,6 +149,15 @@ __device__ __forceinline__ void ld32x2(uint32_t a0, uint32_t a1, float (&v0)[32]
     v1[i] = __uint_as_float(r[32 + i]);
   }
 }
+
+// 32 lanes x 8 consecutive 32-bit columns from registers (thread t of the warp writes lane
+// base lane + t); complete once wait_st() returns
+__device__ __forceinline__ void st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
+               "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+__device__ __forceinline__ void wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // one lane of a converged warp (the lowest active one)
 __device__ __forceinline__ bool elect_one() {
