@@ -25,14 +25,14 @@ static int launch_scan_tc(const ScanParams& p, cudaStream_t s) {
   return cuda_status(launch_pdl(scan_tc_kernel, dim3(grid), dim3(ScanTcCfg::kThreads), ScanTcCfg::kSmem, s, p));
 }
 
-// d = 256: tcgen05 kernel, one CTA per (sample, head, 128-value half)
+// d = 256: tcgen05 kernel, one CTA per (sample, head, 128-value block)
 static int launch_scan_tc256(const ScanParams& p, cudaStream_t s) {
-  cudaError_t e = ensure_smem(scan_tc256_kernel, ScanTc256Cfg::kSmem);
+  using Cfg = ScanTc256Cfg;
+  cudaError_t e = ensure_smem(scan_tc256_kernel, Cfg::kSmem);
   if (e != cudaSuccess) return cuda_status(e);
-  const unsigned grid = static_cast<unsigned>(p.N) * p.H * 2;
+  const unsigned grid = static_cast<unsigned>(p.N) * p.H * Cfg::kBlocks;
   ProfScope prof(kProfScan, s);
-  return cuda_status(
-      launch_pdl(scan_tc256_kernel, dim3(grid), dim3(ScanTc256Cfg::kThreads), ScanTc256Cfg::kSmem, s, p));
+  return cuda_status(launch_pdl(scan_tc256_kernel, dim3(grid), dim3(Cfg::kThreads), Cfg::kSmem, s, p));
 }
 
 int launch_scan(int D, const ScanParams& p, cudaStream_t s) {
