@@ -96,6 +96,7 @@ int launch_intra(int D, bool erase, const IntraParams& p, int64_t max_chunks, cu
 int launch_scan(int D, const ScanParams& p, cudaStream_t s);
 int launch_recurrent(int D, const RecurrentParams& p, cudaStream_t s);
 // exact: fp32 query and state (no bf16 rounding); maxlen: bound on tokens per block
-int launch_read(const ReadParams& p, int D, bool exact, int64_t maxlen, cudaStream_t s);
+// beside_scan: the read runs beside the commit's scan (short CTAs, so the scan takes its SMs)
+int launch_read(const ReadParams& p, int D, bool exact, int64_t maxlen, cudaStream_t s, bool beside_scan = false);
 
 }  // namespace memt

@@ -246,7 +246,7 @@ int check_read(const memt_gdn2_read_args* a) {
 }
 
 // the read's kernels for arguments check_read accepted
-int read_launch(const memt_gdn2_read_args* a, memt_stream_t stream) {
+int read_launch(const memt_gdn2_read_args* a, memt_stream_t stream, bool beside_scan = false) {
   if (a->total_tokens == 0) return MEMT_OK;
   ReadParams p{};
   p.num_blocks = a->num_blocks;
@@ -261,7 +261,8 @@ int read_launch(const memt_gdn2_read_args* a, memt_stream_t stream) {
   p.slots = a->state_slots;
   p.num_slots = a->num_slots;
   const int64_t maxlen = a->max_block_tokens > 0 ? a->max_block_tokens : a->total_tokens;
-  return launch_read(p, a->key_dim, a->q_dtype == MEMT_F32, maxlen, reinterpret_cast<cudaStream_t>(stream));
+  return launch_read(p, a->key_dim, a->q_dtype == MEMT_F32, maxlen, reinterpret_cast<cudaStream_t>(stream),
+                     beside_scan);
 }
 
 }  // namespace
@@ -369,7 +370,7 @@ int memt_gdn2_update_read(const memt_gdn2_update_args* u, void* workspace, size_
   if (e == cudaSuccess) {
     st = launch_scan(u->key_dim, sp, side);
     e = cudaEventRecord(join, side);  // recorded even after a failed launch, so the join below holds
-    const int st_read = read_launch(r, stream);
+    const int st_read = read_launch(r, stream, true);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(s, join, 0);
     if (st == MEMT_OK) st = st_read;
   }

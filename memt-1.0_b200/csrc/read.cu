@@ -39,9 +39,15 @@ static int launch_tile(const ReadParams& p, int64_t maxlen, cudaStream_t s) {
   return cuda_status(cudaGetLastError());
 }
 
-// d = 128 / 256, bf16 queries, plain read: tcgen05 kernel with TMA query tiles
+// d = 128 / 256, bf16 queries, plain read: tcgen05 kernel with TMA query tiles. A CTA reads
+// runs of 16 tiles of one block, converting the block's snapshot first. By default a block's
+// runs are spread over as many CTAs as it has runs: short CTAs balance over the SMs as they
+// free up, which is also what lets the commit's scan (launched beside the read at higher
+// priority) take its SMs at once. With WAVE (a d = 256 read on its own, whose 128 KB snapshot
+// costs a CTA about as much as a few tiles), the runs are spread over one resident wave
+// instead, at most 8 runs a CTA (long or ragged blocks still spread over the SMs).
 template <int D>
-static int launch_read_tc(const ReadParams& p, int64_t maxlen, cudaStream_t s) {
+static int launch_read_tc(const ReadParams& p, int64_t maxlen, bool wave, cudaStream_t s) {
   using Cfg = ReadTcCfg<D>;
   ReadTcParams P;
   P.p = p;
@@ -54,17 +60,30 @@ static int launch_read_tc(const ReadParams& p, int64_t maxlen, cudaStream_t s) {
   const int64_t per = int64_t(kReadTcTiles) * Cfg::kTok;
   int64_t groups = (maxlen + per - 1) / per;
   if (groups < 1) groups = 1;
-  if (groups > 65535) return MEMT_ERR_UNSUPPORTED;
-  dim3 grid(static_cast<unsigned>(p.num_blocks) * p.H, static_cast<unsigned>(groups));
+  const int64_t blocks = int64_t(p.num_blocks) * p.H;
+  int64_t gy = groups;
+  if (wave) {
+    constexpr int64_t kMaxRuns = 8;
+    int slots = 0;
+    e = resident_slots(read_tc_kernel<D>, Cfg::kThreads, Cfg::kSmem, &slots);
+    if (e != cudaSuccess) return cuda_status(e);
+    gy = slots / blocks;
+    const int64_t gy_min = (groups + kMaxRuns - 1) / kMaxRuns;
+    if (gy < gy_min) gy = gy_min;
+    if (gy > groups) gy = groups;
+    if (gy < 1) gy = 1;
+  }
+  if (gy > 65535) return MEMT_ERR_UNSUPPORTED;
+  dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(gy));
   ProfScope prof(kProfReadTile, s);
   read_tc_kernel<D><<<grid, Cfg::kThreads, Cfg::kSmem, s>>>(P);
   return cuda_status(cudaGetLastError());
 }
 
-int launch_read(const ReadParams& p, int D, bool exact, int64_t maxlen, cudaStream_t s) {
+int launch_read(const ReadParams& p, int D, bool exact, int64_t maxlen, cudaStream_t s, bool beside_scan) {
   if (!exact && !p.fused && maxlen > kGemvMaxBlock) {
-    if (D == 128) return launch_read_tc<128>(p, maxlen, s);
-    if (D == 256) return launch_read_tc<256>(p, maxlen, s);
+    if (D == 128) return launch_read_tc<128>(p, maxlen, false, s);
+    if (D == 256) return launch_read_tc<256>(p, maxlen, !beside_scan, s);
   }
   if (exact || maxlen <= kGemvMaxBlock) {
     switch (D) {
