@@ -164,6 +164,10 @@ CASES = [
     ([100, 37, 64, 200], 2, 128, "head", "head", False, True, 2048),
     ([70, 5], 2, 128, "head", None, False, True, 2048),
     ([90, 40], 2, 64, "head", "channel", False, True, 64),
+    # d = 256 (the tcgen05 scan over two 128-value blocks): ragged, a single-token sample, odd H,
+    # per-head decay through the TMA-fed intra path; per-channel decay with 64-token events
+    ([1, 130, 64, 200], 3, 256, "head", "head", False, True, 2048),
+    ([65, 1, 129], 2, 256, "channel", None, False, False, 64),
 ]
 
 
@@ -262,12 +266,13 @@ def test_reads_from_a_state_pool(cuda):
     assert torch.equal(out[0], ref[0]) and torch.equal(out[2], ref[2])
 
 
-def test_update_in_a_state_pool(cuda):
+@pytest.mark.parametrize("D", [128, 256])
+def test_update_in_a_state_pool(cuda, D):
     """The update reading its initial states from and writing its final states into a state
     pool by slot index (in place, no gather and no index_copy_) equals the gathered update;
     slots not named stay untouched, and the read of the same pool sees the incoming states."""
     bf = torch.bfloat16
-    H, D, S = 4, 128, 9
+    H, S = 4, 9
     x = to_bf16(make_inputs(13, [500, 64, 333], H, D, gate="channel", beta=None, erase=False, write=True))
     gen = torch.Generator(device=cuda).manual_seed(4)
     pool = 0.05 * torch.randn(S, H, D, D, device=cuda, generator=gen)
@@ -287,11 +292,12 @@ def test_update_in_a_state_pool(cuda):
     assert torch.equal(pool[others], before[others])
 
 
-def test_update_partial_chunk_ignores_next_sample(cuda):
+@pytest.mark.parametrize("D", [128, 256])
+def test_update_partial_chunk_ignores_next_sample(cuda, D):
     """The last chunk of a sample is a 64-row tile whose rows past the sample are the next
     sample's tokens (the tile loads do not stop at the sample end). Non-finite values there
     must not reach the sample's result."""
-    x = to_bf16(make_inputs(11, [100, 60], 2, 128, gate="head", beta="head", erase=False, write=True))
+    x = to_bf16(make_inputs(11, [100, 60], 2, D, gate="head", beta="head", erase=False, write=True))
     first = {k_: (v_[:100] if k_ in ("q", "k", "v", "g", "beta", "w") and v_ is not None else v_) for k_, v_ in x.items()}
     first.update(lengths=[100], cu=np.array([0, 100], np.int32), h0=x["h0"][:1])
     for key in ("k", "v", "w", "beta"):
@@ -317,8 +323,9 @@ def test_update_extreme_decay_slow_path(cuda):
     assert O.rel_fro(got, oracle_update(x, 2048, "bf16")) <= TOL_BF16
 
 
-def test_update_in_place(cuda):
-    x = to_bf16(make_inputs(11, [100, 37], 2, 128))
+@pytest.mark.parametrize("D", [128, 256])
+def test_update_in_place(cuda, D):
+    x = to_bf16(make_inputs(11, [100, 37], 2, D))
     state = _t(x["h0"], cuda)
     out = gpu_update(x, cuda, torch.bfloat16, 2048, final_state=state, h0=state)
     torch.cuda.synchronize()
@@ -326,11 +333,24 @@ def test_update_in_place(cuda):
     assert O.rel_fro(state.cpu().numpy(), oracle_update(x, 2048, "bf16")) <= TOL_BF16
 
 
-def test_update_zero_state_and_single_token_samples(cuda):
-    x = to_bf16(make_inputs(12, [1, 1, 1, 2], 2, 64, state=False))
+@pytest.mark.parametrize("D", [64, 256])
+def test_update_zero_state_and_single_token_samples(cuda, D):
+    x = to_bf16(make_inputs(12, [1, 1, 1, 2], 2, D, state=False))
     out = gpu_update(x, cuda, torch.bfloat16, 2048)
     torch.cuda.synchronize()
     assert O.rel_fro(out.cpu().numpy(), oracle_update(x, 2048, "bf16")) <= TOL_BF16
+
+
+@pytest.mark.parametrize("D", [128, 256])
+def test_update_empty_sample_keeps_its_state(cuda, D):
+    """A sample with no tokens (equal offsets) has no chunks: its final state is its initial
+    state, and its neighbours are unaffected."""
+    x = to_bf16(make_inputs(14, [100, 0, 70], 2, D))
+    out = gpu_update(x, cuda, torch.bfloat16, 2048)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    assert np.array_equal(got[1], x["h0"][1].astype(np.float32))
+    assert O.rel_fro(got, oracle_update(x, 2048, "bf16")) <= TOL_BF16
 
 
 def test_update_workspace_status_clean(cuda):
