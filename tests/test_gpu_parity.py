@@ -387,6 +387,35 @@ def test_read_bf16(cuda, lengths, D):
     assert np.mean(got != ref.astype(np.float32)) < 0.02
 
 
+@pytest.mark.parametrize("lengths", [[16384] * 4, [16384, 1000, 7000, 3]])
+def test_read_d256_long_blocks_over_one_wave(cuda, lengths):
+    """A d = 256 read on its own spreads each block's runs of 1024 tokens over one resident wave
+    of CTAs (64 blocks here: two CTAs a block, eight runs each, one snapshot conversion per CTA).
+    Every token of every block is read, ragged and 3-token blocks included: the whole output
+    against an fp32 product on the GPU, and the first and last 64 tokens of each block against
+    the oracle's emulation of the reference's rounding."""
+    H, D = 16, 256
+    gen = torch.Generator(device=cuda).manual_seed(21)
+    L, N = sum(lengths), len(lengths)
+    q = (torch.randn(L, H, D, device=cuda, generator=gen) / D ** 0.5).to(torch.bfloat16)
+    S = 0.05 * torch.randn(N, H, D, D, device=cuda, generator=gen)
+    cu = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32)
+    scale = D ** -0.5
+    out = ops._read(q, S, torch.from_numpy(cu).to(cuda), N, max(lengths), scale, torch.bfloat16)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
+    Sb = S.to(torch.bfloat16).float()
+    for n in range(N):
+        a, b = int(cu[n]), int(cu[n + 1])
+        # fp32 product, rounded to the output's bf16 as the kernel rounds it
+        ref = (torch.einsum("thk,hkv->thv", q[a:b].float(), Sb[n]) * scale).to(torch.bfloat16).float()
+        assert O.rel_fro(out[a:b].float().cpu().numpy(), ref.cpu().numpy()) <= TOL_BF16
+        for lo, hi in ((a, min(a + 64, b)), (max(b - 64, a), b)):
+            qs = q[lo:hi].float().cpu().numpy()
+            ref_o = O.read(qs, S[n:n + 1].cpu().numpy(), np.array([0, hi - lo]), scale, mode="bf16")
+            assert O.rel_fro(out[lo:hi].float().cpu().numpy(), ref_o) <= TOL_BF16
+
+
 @pytest.mark.parametrize("lengths", [[1, 2], [5, 40, 3]])
 def test_read_fp32_exact(cuda, lengths):
     rng = np.random.default_rng(3)
