@@ -96,7 +96,13 @@ int launch_intra(int D, bool erase, const IntraParams& p, int64_t max_chunks, cu
 int launch_scan(int D, const ScanParams& p, cudaStream_t s);
 int launch_recurrent(int D, const RecurrentParams& p, cudaStream_t s);
 // exact: fp32 query and state (no bf16 rounding); maxlen: bound on tokens per block
-// beside_scan: the read runs beside the commit's scan (short CTAs, so the scan takes its SMs)
-int launch_read(const ReadParams& p, int D, bool exact, int64_t maxlen, cudaStream_t s, bool beside_scan = false);
+// Where a read runs. kReadAlone: on its own. kReadBeside: on the caller's stream beside the
+// commit's scan (short CTAs, which the scan's SMs are not held by). kReadAfterScan: on the
+// scan's stream right after it, by programmatic dependent launch, so that its CTAs are placed
+// only once every scan CTA is resident; it never waits for the scan (it reads nothing the scan
+// writes). Only the tcgen05 tile read takes kReadAfterScan (read_uses_tc).
+enum ReadPlacement { kReadAlone = 0, kReadBeside = 1, kReadAfterScan = 2 };
+bool read_uses_tc(const ReadParams& p, int D, bool exact, int64_t maxlen);
+int launch_read(const ReadParams& p, int D, bool exact, int64_t maxlen, cudaStream_t s, int placement = kReadAlone);
 
 }  // namespace memt

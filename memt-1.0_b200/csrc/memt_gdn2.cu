@@ -246,7 +246,9 @@ int check_read(const memt_gdn2_read_args* a) {
 }
 
 // the read's kernels for arguments check_read accepted
-int read_launch(const memt_gdn2_read_args* a, memt_stream_t stream, bool beside_scan = false) {
+// side: the stream of the commit's scan (null for a read on its own): a tcgen05 tile read then
+// runs on it right after the scan, any other read on the caller's stream beside the scan
+int read_launch(const memt_gdn2_read_args* a, memt_stream_t stream, cudaStream_t side = nullptr) {
   if (a->total_tokens == 0) return MEMT_OK;
   ReadParams p{};
   p.num_blocks = a->num_blocks;
@@ -261,8 +263,10 @@ int read_launch(const memt_gdn2_read_args* a, memt_stream_t stream, bool beside_
   p.slots = a->state_slots;
   p.num_slots = a->num_slots;
   const int64_t maxlen = a->max_block_tokens > 0 ? a->max_block_tokens : a->total_tokens;
-  return launch_read(p, a->key_dim, a->q_dtype == MEMT_F32, maxlen, reinterpret_cast<cudaStream_t>(stream),
-                     beside_scan);
+  const bool exact = a->q_dtype == MEMT_F32;
+  if (side == nullptr) return launch_read(p, a->key_dim, exact, maxlen, reinterpret_cast<cudaStream_t>(stream));
+  if (read_uses_tc(p, a->key_dim, exact, maxlen)) return launch_read(p, a->key_dim, exact, maxlen, side, kReadAfterScan);
+  return launch_read(p, a->key_dim, exact, maxlen, reinterpret_cast<cudaStream_t>(stream), kReadBeside);
 }
 
 }  // namespace
@@ -364,13 +368,14 @@ int memt_gdn2_update_read(const memt_gdn2_update_args* u, void* workspace, size_
   ScanParams sp;
   st = update_bf16_front(u, workspace, s, &sp);
   if (st != MEMT_OK) return st;
-  // fork after the intra kernel: the scan on the high-priority stream, the read on the caller's
+  // fork after the intra kernel: the scan on the high-priority stream; the read after it on the
+  // same stream by programmatic launch (tcgen05 tile read) or on the caller's stream
   cudaError_t e = cudaEventRecord(fork, s);
   if (e == cudaSuccess) e = cudaStreamWaitEvent(side, fork, 0);
   if (e == cudaSuccess) {
     st = launch_scan(u->key_dim, sp, side);
+    const int st_read = read_launch(r, stream, side);
     e = cudaEventRecord(join, side);  // recorded even after a failed launch, so the join below holds
-    const int st_read = read_launch(r, stream, true);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(s, join, 0);
     if (st == MEMT_OK) st = st_read;
   }

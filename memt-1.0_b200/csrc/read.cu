@@ -42,12 +42,13 @@ static int launch_tile(const ReadParams& p, int64_t maxlen, cudaStream_t s) {
 // d = 128 / 256, bf16 queries, plain read: tcgen05 kernel with TMA query tiles. A CTA reads
 // runs of 16 tiles of one block, converting the block's snapshot first. By default a block's
 // runs are spread over as many CTAs as it has runs: short CTAs balance over the SMs as they
-// free up, which is also what lets the commit's scan (launched beside the read at higher
-// priority) take its SMs at once. With WAVE (a d = 256 read on its own, whose 128 KB snapshot
-// costs a CTA about as much as a few tiles), the runs are spread over one resident wave
-// instead, at most 8 runs a CTA (long or ragged blocks still spread over the SMs).
+// free up. With WAVE (d = 256, whose 128 KB snapshot costs a CTA about as much as a few tiles),
+// the runs are spread over one resident wave instead, at most 8 runs a CTA (long or ragged
+// blocks still spread over the SMs) — unless the read runs beside the commit's scan on the
+// caller's stream, where long CTAs could hold SMs the scan is waiting for. PDL: launched
+// after the scan on its stream (kReadAfterScan); the kernel never waits on it.
 template <int D>
-static int launch_read_tc(const ReadParams& p, int64_t maxlen, bool wave, cudaStream_t s) {
+static int launch_read_tc(const ReadParams& p, int64_t maxlen, bool wave, bool pdl, cudaStream_t s) {
   using Cfg = ReadTcCfg<D>;
   ReadTcParams P;
   P.p = p;
@@ -76,14 +77,20 @@ static int launch_read_tc(const ReadParams& p, int64_t maxlen, bool wave, cudaSt
   if (gy > 65535) return MEMT_ERR_UNSUPPORTED;
   dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(gy));
   ProfScope prof(kProfReadTile, s);
+  if (pdl) return cuda_status(launch_pdl(read_tc_kernel<D>, grid, dim3(Cfg::kThreads), Cfg::kSmem, s, P));
   read_tc_kernel<D><<<grid, Cfg::kThreads, Cfg::kSmem, s>>>(P);
   return cuda_status(cudaGetLastError());
 }
 
-int launch_read(const ReadParams& p, int D, bool exact, int64_t maxlen, cudaStream_t s, bool beside_scan) {
-  if (!exact && !p.fused && maxlen > kGemvMaxBlock) {
-    if (D == 128) return launch_read_tc<128>(p, maxlen, false, s);
-    if (D == 256) return launch_read_tc<256>(p, maxlen, !beside_scan, s);
+bool read_uses_tc(const ReadParams& p, int D, bool exact, int64_t maxlen) {
+  return !exact && !p.fused && maxlen > kGemvMaxBlock && (D == 128 || D == 256);
+}
+
+int launch_read(const ReadParams& p, int D, bool exact, int64_t maxlen, cudaStream_t s, int placement) {
+  if (read_uses_tc(p, D, exact, maxlen)) {
+    const bool pdl = placement == kReadAfterScan;
+    if (D == 128) return launch_read_tc<128>(p, maxlen, false, pdl, s);
+    return launch_read_tc<256>(p, maxlen, placement != kReadBeside, pdl, s);
   }
   if (exact || maxlen <= kGemvMaxBlock) {
     switch (D) {
