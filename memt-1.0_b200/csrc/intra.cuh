@@ -826,23 +826,25 @@ struct IntraKernel {
       *reinterpret_cast<uint4*>(t + pswz(i / (P / 8), (i % (P / 8)) * 8)) = make_uint4(0, 0, 0, 0);
   }
 
-  // u operand in place: sV = bf16(v * w)   (wy_fast.py:98-100); threads [T0, T0 + NTH); in the
-  // TMA path rows past the chunk become zero
+  // u operand in place: vt = bf16(v * w) (wy_fast.py:98-100), by default of the value tiles sV and
+  // sW; threads [T0, T0 + NTH); in the TMA path rows past the chunk become zero
   template <int T0, int NTH>
-  __device__ void stage_u(const IntraParams& p) {
+  __device__ void stage_u(const IntraParams& p, __nv_bfloat16* vt = nullptr, const __nv_bfloat16* wt = nullptr) {
+    if (vt == nullptr) vt = sV;
+    if (wt == nullptr) wt = sW;
     constexpr int kChunks = kTile * P / 8;
     static_assert(kChunks % NTH == 0, "chunks per thread");
     if (p.write == nullptr) {
       if constexpr (kTma) {  // rows past the chunk hold the next sample's tokens: zero them
-        if (len < kTile) zero_rows<T0, NTH>(sV);
+        if (len < kTile) zero_rows<T0, NTH>(vt);
       }
       return;
     }
     using Wk = Walk<NTH>;
     int row0, col;
     const uint32_t off = walk_start<T0>(row0, col);
-    unsigned char* vb = reinterpret_cast<unsigned char*>(sV) + off;
-    const unsigned char* wb = reinterpret_cast<const unsigned char*>(sW) + off;
+    unsigned char* vb = reinterpret_cast<unsigned char*>(vt) + off;
+    const unsigned char* wb = reinterpret_cast<const unsigned char*>(wt) + off;
 #pragma unroll
     for (int j = 0; j < Wk::kSteps; ++j) {
       uint4 vv = make_uint4(0, 0, 0, 0);
@@ -858,15 +860,17 @@ struct IntraKernel {
     }
   }
 
-  // w operand bf16( bf16(k*b) * 2^G ) in place of k (wy_fast.py:110-116), kg = bf16(k 2^(G_last-G))
-  // to global (wy_fast.py:125-139) and 2^G_last; threads [T0, T0 + NTH)
+  // w operand bf16( bf16(k*b) * 2^G ) in place of k, or into wdst (wy_fast.py:110-116),
+  // kg = bf16(k 2^(G_last-G)) to global (wy_fast.py:125-139) and 2^G_last; threads [T0, T0 + NTH)
   template <int T0, int NTH>
-  __device__ void stage_w_kg(__nv_bfloat16* kt, __nv_bfloat16* gKG, float* gEl, int c0) {
+  __device__ void stage_w_kg(__nv_bfloat16* kt, __nv_bfloat16* gKG, float* gEl, int c0,
+                             __nv_bfloat16* wdst = nullptr) {
     const int last = len - 1;
     using Wk = Walk<NTH>;
     int row0, col;
     const uint32_t off = walk_start<T0>(row0, col);
     unsigned char* kb = reinterpret_cast<unsigned char*>(kt) + off;
+    unsigned char* wb = reinterpret_cast<unsigned char*>(wdst != nullptr ? wdst : kt) + off;
     unsigned char* gb = reinterpret_cast<unsigned char*>(gKG) + (c0 >> 6) * 8192 + off;  // same layout
     const unsigned char* bb = reinterpret_cast<const unsigned char*>(sB) + off;
 #pragma unroll
@@ -914,7 +918,7 @@ struct IntraKernel {
           kw[e] = f32x2_to_bf16x2(mul_f32x2(k2, e2));
         }
       }
-      *reinterpret_cast<uint4*>(kb + j * Wk::kStride) = kv;  // w operand replaces k in place
+      *reinterpret_cast<uint4*>(wb + j * Wk::kStride) = kv;  // w operand (in place of k by default)
       *reinterpret_cast<uint4*>(gb + j * Wk::kStride) = kgv;
     }
     const int j = tid - T0;
@@ -1147,6 +1151,11 @@ struct IntraKernel {
         }
         prepare_key_panel(pn * P);
         scores_panel(acc, kcur);
+        // D = 256: panel 0's w operand (and kg, 2^G_last) now, while its keys and decay table are
+        // resident (it needs neither the scores nor the inverse), into the value tile, which is
+        // free until the u operands; the next panel's load waits for every thread (barrier above)
+        if constexpr (Cfg::kPanels == 2)
+          if (pn == 0) stage_w_kg<0, NT>(kcur, gKG, gEl, 0, sV);
       }
       store_scores(acc);  // nothing reads the score buffer while the scores are formed
       if constexpr (!kOverlap) cp_async_wait<0>();  // every thread's copies of v and w are complete
@@ -1190,43 +1199,43 @@ struct IntraKernel {
         store_tile_async(gU, 0, kcur);
         if (tid == 0) bulk_wait_read();  // before the next unit reloads sW and kcur
       } else {
-        // ---- D = 256: panels one after the other ----
-        if (warp < 4) solve();
+        // ---- D = 256: panel 1's w operand (its keys and decay table are resident) on warps 4-7
+        // while warps 0-3 solve; panel 0's is in the value tile sV since the score loop. One pass
+        // of both WY products then gives w of both panels ----
+        static_assert(Cfg::kPanels == 2, "the panel pair of D = 256");
+        __nv_bfloat16* sA16 = reinterpret_cast<__nv_bfloat16*>(sA);  // free once the solve is done
+        __nv_bfloat16* sE16 = reinterpret_cast<__nv_bfloat16*>(sE);  // free once both w operands are staged
+        if (warp < 4)
+          solve();
+        else
+          stage_w_kg<128, 128>(kcur, gKG, gEl, P);
         __syncthreads();
-        // last panel first: its key tile (beta folded) and decay table are still resident from
-        // the score loop, so only the other panels are reloaded and prepared again
-        for (int pn = Cfg::kPanels - 1; pn >= 0; --pn) {
-          const int c0 = pn * P;
-          if (pn != Cfg::kPanels - 1) {
-            load_key_panel(c0);
-            cp_async_commit();
-            cp_async_wait<0>();
-            prepare_key_panel(c0);
-          }
-          stage_w_kg<0, NT>(kcur, gKG, gEl, c0);
-          __syncthreads();
-          wy_product(kcur, sW);  // the write-gate tile is not loaded in this loop
-          fence_proxy_async_smem();
-          __syncthreads();
-          store_tile_async(gW, c0, sW);
-          if (tid == 0) bulk_wait_read();
-          __syncthreads();
-        }
-        for (int pn = 0; pn < Cfg::kPanels; ++pn) {
-          const int c0 = pn * P;
-          load_value_panel(c0);
-          cp_async_commit();
-          cp_async_wait<0>();
-          __syncthreads();
-          stage_u<0, NT>(p);
-          __syncthreads();
-          wy_product(sV, sW);  // the write gate is folded into the u operand: its tile is free
-          fence_proxy_async_smem();
-          __syncthreads();
-          store_tile_async(gU, c0, sW);
-          if (tid == 0) bulk_wait_read();
-          __syncthreads();  // the next panel's value loads overwrite the tile the store read
-        }
+        wy_products(kcur, sW, sA16);  // w of panel 1 -> sW, of panel 0 (sV) -> the score buffer
+        fence_proxy_async_smem();
+        __syncthreads();
+        store_tile_async(gW, P, sW);
+        store_tile_async(gW, 0, sA16);
+        if (tid == 0) bulk_wait_read();  // before the u pass overwrites sW and the score buffer
+        __syncthreads();
+        // ---- u of both panels: v and the write gate of panel 0 into the value tiles, of panel 1
+        // into the key tile and the decay table; one pass of both products ----
+        load_tile(sV, p.v, 0, p.sv);
+        if (p.write != nullptr) load_tile(sW, p.write, 0, p.sw);
+        load_tile(kcur, p.v, P, p.sv);
+        if (p.write != nullptr) load_tile(sE16, p.write, P, p.sw);
+        cp_async_commit();
+        cp_async_wait<0>();
+        __syncthreads();
+        stage_u<0, NT>(p);              // sV = bf16(v0 * w0)
+        stage_u<0, NT>(p, kcur, sE16);  // kcur = bf16(v1 * w1)
+        __syncthreads();
+        wy_products(kcur, sW, sA16);  // u of panel 1 -> sW, of panel 0 (sV) -> the score buffer
+        fence_proxy_async_smem();
+        __syncthreads();
+        store_tile_async(gU, P, sW);
+        store_tile_async(gU, 0, sA16);
+        if (tid == 0) bulk_wait_read();
+        __syncthreads();  // the next unit's loads overwrite the tiles the stores read
       }
       if (!has_next) {
         if (tid == 0) bulk_wait_all();
