@@ -930,44 +930,7 @@ struct IntraKernel {
     }
   }
 
-  // dst ([64][P], pswz) = A^-1 (lower) . src ([64][P], pswz). Row block r needs k-steps 0..r,
-  // so warp w takes column quarter w % 4 of two row blocks with r + 1 summing to 5: blocks
-  // 3 and 0 (warps 0-3) or 2 and 1 (warps 4-7) -- the same work on every warp.
-  __device__ void wy_product(const __nv_bfloat16* src, __nv_bfloat16* dst) {
-    constexpr int CW = P / 4;     // columns of a quarter
-    constexpr int NTW = CW / 8;   // 8-column tiles of a quarter
-    const int n_base = (warp & 3) * CW;
-    const int g = lane >> 2, t = lane & 3;
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const int r = (warp < 4) ? (half ? 0 : 3) : (half ? 1 : 2);
-      float acc[NTW][4];
-#pragma unroll
-      for (int i = 0; i < NTW; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-      for (int ks = 0; ks <= r; ++ks) {
-        uint32_t a[4], b[NTW / 2][4];
-        ldsm_x4(a, smem_u32(sAi + (16 * r + (lane & 15)) * Cfg::kLdAi + 16 * ks + 8 * (lane >> 4)));
-#pragma unroll
-        for (int np = 0; np < NTW; np += 2)
-          ldsm_x4_t(b[np / 2], smem_u32(src + pswz(16 * ks + (lane & 15), n_base + 8 * np + 8 * (lane >> 4))));
-#pragma unroll
-        for (int np = 0; np < NTW; np += 2) {
-          uint32_t b0[2] = {b[np / 2][0], b[np / 2][1]}, b1[2] = {b[np / 2][2], b[np / 2][3]};
-          mma_bf16_16816(acc[np], a, b0);
-          mma_bf16_16816(acc[np + 1], a, b1);
-        }
-      }
-#pragma unroll
-      for (int nt = 0; nt < NTW; ++nt) {
-        const int col = n_base + 8 * nt + 2 * t;
-        const int i0 = 16 * r + g;
-        *reinterpret_cast<uint32_t*>(dst + pswz(i0, col)) = pack_bf16x2(acc[nt][0], acc[nt][1]);
-        *reinterpret_cast<uint32_t*>(dst + pswz(i0 + 8, col)) = pack_bf16x2(acc[nt][2], acc[nt][3]);
-      }
-    }
-  }
-
-  // Both WY products in one pass (TMA loop): w = A^-1 . (w operand in kt) -> dw and
+  // Both WY products in one pass: w = A^-1 . (w operand in kt) -> dw and
   // u = A^-1 . (u operand in sV) -> du, all [64][P] pswz tiles; the A^-1 fragment of a k-step
   // feeds both. Row block r needs k-steps 0..r: warps 0-3 take row blocks 3 and 0, warps 4-7
   // blocks 2 and 1, each in column quarter warp % 4 -- the same work on every warp. The sources
@@ -1189,15 +1152,15 @@ struct IntraKernel {
 
         }
         __syncthreads();
-        wy_product(kcur, sW);  // w = A^-1 . w operand; the w-gate tile is free
+        // one pass of both products: w = A^-1 . w operand into the w-gate tile (free), u =
+        // A^-1 . bf16(v*w) into the score buffer (free once the solve is done)
+        __nv_bfloat16* sA16 = reinterpret_cast<__nv_bfloat16*>(sA);
+        wy_products(kcur, sW, sA16);
         fence_proxy_async_smem();
         __syncthreads();
         store_tile_async(gW, 0, sW);
-        wy_product(sV, kcur);  // u = A^-1 . bf16(v*w); the w operand is consumed
-        fence_proxy_async_smem();
-        __syncthreads();
-        store_tile_async(gU, 0, kcur);
-        if (tid == 0) bulk_wait_read();  // before the next unit reloads sW and kcur
+        store_tile_async(gU, 0, sA16);
+        if (tid == 0) bulk_wait_read();  // before the next unit reloads sW and stores its scores
       } else {
         // ---- D = 256: panel 1's w operand (its keys and decay table are resident) on warps 4-7
         // while warps 0-3 solve; panel 0's is in the value tile sV since the score loop. One pass
