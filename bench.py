@@ -80,18 +80,40 @@ def update_flops_per_token_head(d, c=64):
 # ---------------------------------------------------------------------------
 
 class ClockSampler:
-    """nvidia-smi samples (200 ms) while the timed region runs."""
+    """SM clocks and clock-event reasons while the timed region runs: NVML read by a thread every
+    2 ms (the timed region can be a few milliseconds), or nvidia-smi at 200 ms when NVML is not
+    importable. Reads only; no setting of the GPU is changed."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
 
     def __init__(self, gpu_id):
         self.gpu_id = gpu_id
         self.proc = None
         self.lines = []
+        self.samples = []  # (sm MHz, max MHz, reason bits) from NVML
+        self.nvml = None
+        self.stop = threading.Event()
+        self.thread = None
 
     def __enter__(self):
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.handle = pynvml.nvmlDeviceGetHandleByUUID(self.gpu_id)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+            self.thread = threading.Thread(target=self._poll, daemon=True)
+            self.thread.start()
+            return self
+        except Exception:
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", self.gpu_id, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -102,11 +124,24 @@ class ClockSampler:
         time.sleep(0.3)
         return self
 
+    def _poll(self):
+        nv = self.nvml
+        while not self.stop.is_set():
+            try:
+                self.samples.append((nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM), self.max_mhz,
+                                     nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)))
+            except Exception:
+                return
+            time.sleep(0.002)
+
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
     def __exit__(self, *exc):
+        if self.thread is not None:
+            self.stop.set()
+            self.thread.join(timeout=5)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -115,21 +150,31 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
-        rows = [[c.strip() for c in ln.split(",")] for ln in self.lines if ln.count(",") >= 8]
         sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in rows:
-            try:
-                sm.append(float(r[1]))
-                mx = float(r[2])
-            except ValueError:
-                continue
-            for name, val in zip(names, r[5:9]):
-                if val.lower().startswith("active"):
-                    reasons.add(name)
+        if self.nvml is not None:
+            for clk, top, bits in self.samples:
+                sm.append(float(clk))
+                mx = float(top)
+                for name, attr in self.REASONS:
+                    if bits & getattr(self.nvml, attr, 0):
+                        reasons.add(name)
+            n = len(self.samples)
+        else:
+            rows = [[c.strip() for c in ln.split(",")] for ln in self.lines if ln.count(",") >= 8]
+            names = [r[0] for r in self.REASONS]
+            for r in rows:
+                try:
+                    sm.append(float(r[1]))
+                    mx = float(r[2])
+                except ValueError:
+                    continue
+                for name, val in zip(names, r[5:9]):
+                    if val.lower().startswith("active"):
+                        reasons.add(name)
+            n = len(rows)
         loaded = [s for s in sm if mx and s > 0.3 * mx] or sm
         return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(rows)}
+                "reasons": sorted(reasons), "samples": n, "source": "nvml" if self.nvml is not None else "nvidia-smi"}
 
 
 def read_traffic(family):
