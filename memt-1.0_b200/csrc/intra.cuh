@@ -400,29 +400,30 @@ struct IntraKernel {
 
   // ---- decay, per-channel layout: cumulative sum and factor tables of one panel ----
   __device__ void channel_tables() {
-    // sE holds the raw decay (cp.async); segmented scan over the 64 tokens per channel
+    // sE holds the raw decay (cp.async); segmented scan over the 64 tokens per channel. A thread's
+    // segment is read into registers first and written once at the end: a running sum stored and
+    // reloaded through sE would serialise every step on a store-to-load dependence
     constexpr int kSeg = NT / P, kSegLen = kTile / kSeg;
     const int c = tid % P, sg = tid / P;
-    {
-      float acc = 0.f;
-#pragma unroll 8
-      for (int i = sg * kSegLen; i < (sg + 1) * kSegLen; ++i) {
-        acc += sE[eidx(i, c)];
-        sE[eidx(i, c)] = acc;
-      }
-      sSeg[sg * P + c] = acc;
+    float x[kSegLen];
+#pragma unroll
+    for (int i = 0; i < kSegLen; ++i) x[i] = sE[eidx(sg * kSegLen + i, c)];
+    float acc = 0.f;
+#pragma unroll
+    for (int i = 0; i < kSegLen; ++i) {
+      acc += x[i];
+      x[i] = acc;
     }
+    sSeg[sg * P + c] = acc;
     __syncthreads();
+    float off = 0.f;
+    for (int s2 = 0; s2 < sg; ++s2) off += sSeg[s2 * P + c];
     bool ok = true;
-    {
-      float off = 0.f;
-      for (int s2 = 0; s2 < sg; ++s2) off += sSeg[s2 * P + c];
-#pragma unroll 8
-      for (int i = sg * kSegLen; i < (sg + 1) * kSegLen; ++i) {
-        const float G = (sE[eidx(i, c)] + off) * kRcpLn2;
-        ok = ok && (G >= -60.f) && (G <= 60.f);
-        sE[eidx(i, c)] = G;
-      }
+#pragma unroll
+    for (int i = 0; i < kSegLen; ++i) {
+      const float G = (x[i] + off) * kRcpLn2;
+      ok = ok && (G >= -60.f) && (G <= 60.f);
+      sE[eidx(sg * kSegLen + i, c)] = G;
     }
     // fast: every exponent of the panel in [-60, 60], so that the factorised diagonal blocks
     // (left factor <= 1, right factor >= 1) cannot overflow; otherwise the diagonal blocks are
