@@ -1168,7 +1168,9 @@ struct IntraKernel {
         // of both WY products then gives w of both panels ----
         static_assert(Cfg::kPanels == 2, "the panel pair of D = 256");
         __nv_bfloat16* sA16 = reinterpret_cast<__nv_bfloat16*>(sA);  // free once the solve is done
-        __nv_bfloat16* sE16 = reinterpret_cast<__nv_bfloat16*>(sE);  // free once both w operands are staged
+        // the decay table (free once both w operands are staged), or with a per-head decay (no
+        // table) the score buffer again: loaded only after the w stores have read it
+        __nv_bfloat16* sE16 = reinterpret_cast<__nv_bfloat16*>(sE);
         if (warp < 4)
           solve();
         else
