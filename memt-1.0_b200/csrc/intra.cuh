@@ -1291,17 +1291,11 @@ struct IntraKernel {
       float* gEl = p.Elast + unit * D;
 
       if (tid == 0) {
-        fence_proxy_async_smem();  // the previous unit's accesses to sV, sW and kspare come first
+        // sV and sW held the previous unit's WY operands, read before its last barrier
+        fence_proxy_async_smem();
         mbar_expect_tx(mb(2), p.write != nullptr ? 2 * kTileBytes : kTileBytes);
         tma_tile(sV, &p.v_map, tok0, h, mb(2));
-        if (has_next) {
-          mbar_expect_tx(mb(kb ^ 1), kTileBytes);
-          tma_tile(kspare, &p.k_map, nd.tok0, hn, mb(kb ^ 1));
-        }
-        if (p.write != nullptr) {
-          bulk_wait_read_but1();  // the previous unit's w has left the write-gate tile
-          tma_tile(sW, &p.w_map, tok0, h, mb(2));
-        }
+        if (p.write != nullptr) tma_tile(sW, &p.w_map, tok0, h, mb(2));
       }
       float ng = 0.f;  // next unit's scalars (threads 128..191), stored in the staging
       uint32_t nb = 0u;
@@ -1325,14 +1319,22 @@ struct IntraKernel {
         fold_beta(p, kcur, 0);
       else if (len < kTile)
         zero_rows<0, NT>(kcur);
-      if (tid == 0) bulk_wait_read();  // the previous unit's u has left the score buffer
+      if (tid == 0) {
+        // the previous unit's u and w have left the score buffer and kspare: the next unit's k
+        bulk_wait_read();
+        if (has_next) {
+          mbar_expect_tx(mb(kb ^ 1), kTileBytes);
+          tma_tile(kspare, &p.k_map, nd.tok0, hn, mb(kb ^ 1));
+        }
+      }
       __syncthreads();
       scores_panel(acc, kcur);
       store_scores(acc);
       __syncthreads();
 
       // warps 0-3: blocked solve; warps 4-7: u operand (v * w in place), the next unit's
-      // scalars, then w operand (in place of k), kg and the next unit's decay factors
+      // scalars, then w operand (into the write-gate tile, read by the u operand), kg and the
+      // next unit's decay factors
       if (warp < 4) {
         solve();
       } else {
@@ -1340,20 +1342,20 @@ struct IntraKernel {
         stage_u<128, 128>(p);
         if (has_next) store_scalars(sPre + (pre ^ 1) * 2 * kTile, 128, ng, nb);
         named_sync(2, 128);
-        stage_w_kg<128, 128>(kcur, gKG, gEl, 0);
+        stage_w_kg<128, 128>(kcur, gKG, gEl, 0, sW);
         if (has_next && warp == 7)
           head_factors(sPre + (pre ^ 1) * 2 * kTile, sFac + (pre ^ 1) * Cfg::kSmall, nd.len);
       }
       vph ^= 1u;
       __syncthreads();
-      // w into the write-gate tile (consumed by the u operand), u into the score buffer (free
-      // once the solve is done); both leave by bulk copies that nothing waits for until their
-      // buffers are loaded again (the write gate at the next unit's top, the scores after its fold)
-      wy_products(kcur, sW, reinterpret_cast<__nv_bfloat16*>(sA));
+      // w into the k tile (read by the scores and the staging), u into the score buffer (free
+      // once the solve is done); both leave by bulk copies that nothing waits for before the
+      // next unit's fold, after which the k tile of the unit after it is loaded into this buffer
+      wy_products(sW, kcur, reinterpret_cast<__nv_bfloat16*>(sA));
       fence_proxy_async_smem();
       __syncthreads();  // every product written, every source tile read
       if (tid == 0) {
-        bulk_s2g(gW, smem_u32(sW), kTileBytes);
+        bulk_s2g(gW, smem_u32(kcur), kTileBytes);
         bulk_commit();
         bulk_s2g(gU, smem_u32(sA), kTileBytes);
         bulk_commit();
