@@ -54,7 +54,7 @@ static int launch_read_tc(const ReadParams& p, int64_t maxlen, bool wave, bool p
   P.p = p;
   const uint64_t row = static_cast<uint64_t>(p.H) * D;
   cudaError_t e = make_tmap_bf16_2d(&P.q_map, p.q, row, static_cast<uint64_t>(p.L), row * 2, 64, Cfg::kTok);
-  if (e == cudaSuccess && p.out_bf16)
+  if (e == cudaSuccess && p.out_bf16 && Cfg::kTmaOut)
     e = make_tmap_bf16_2d(&P.o_map, p.out, row, static_cast<uint64_t>(p.L), row * 2, 64, Cfg::kTok);
   if (e == cudaSuccess) e = ensure_smem(read_tc_kernel<D>, Cfg::kSmem);
   if (e != cudaSuccess) return cuda_status(e);

@@ -12,9 +12,13 @@
 //   * a control warp issues the M = 64, N = D, K = D MMA of each tile into one of two
 //     tensor-memory accumulators (2 x D columns);
 //   * eight worker warps drain the other accumulator (token r in lane 32 (r / 16) + r % 16),
-//     64 columns at a time, scale and round; a bf16 output tile goes back into the ring stage
-//     it came from (the MMA has consumed it) in the TMA box layout and leaves with D/64 TMA
-//     stores, after which the stage takes a later query tile.
+//     64 columns at a time, scale and round. At d = 128 a bf16 output tile goes back into the
+//     ring stage it came from (the MMA has consumed it) in the TMA box layout and leaves with
+//     D/64 TMA stores, after which the stage takes a later query tile. At d = 256 the rows go
+//     straight to global memory and a stage takes a later query tile as soon as its MMA has
+//     completed: with three stages of 32 KB, every stage but the one being multiplied is then
+//     a load in flight (config-4 read 0.290 -> 0.249 ms; the same at d = 128 measured no
+//     faster alone and slower beside the scan).
 // The last tile of a block may straddle into the next block (or past L): its rows are
 // computed from whatever the TMA brought (zeros past L) and stored row by row up to the block
 // end instead. Every wait is bounded.
@@ -31,7 +35,7 @@ constexpr int kReadTcTiles = 16;  // 64-token tiles per CTA
 
 struct ReadTcParams {
   CUtensorMap q_map;  // bf16 [L, H*D], boxes of 64 keys x 64 tokens
-  CUtensorMap o_map;  // bf16 output, same geometry (used when out_bf16)
+  CUtensorMap o_map;  // bf16 output, same geometry (d = 128 with out_bf16)
   ReadParams p;
 };
 
@@ -41,7 +45,8 @@ struct ReadTcCfg {
   static constexpr int kPanels = D / 64;                  // 64-value panels (TMA boxes, B operand panels)
   static constexpr int kWorkerWarps = 8;
   static constexpr int kThreads = (kWorkerWarps + 1) * 32;
-  static constexpr int kStages = D <= 128 ? 4 : 3;        // query / output tile ring
+  static constexpr int kStages = D <= 128 ? 4 : 3;        // query (d = 128: and output) tile ring
+  static constexpr bool kTmaOut = D <= 128;               // bf16 output tiles leave by TMA stores
   // a stage is refilled kRefill iterations after its output store was issued: the control thread
   // then waits only for stores older than kRefill - 1 groups, and the refill runs
   // kStages - kRefill tiles ahead of its MMA
@@ -78,13 +83,14 @@ __global__ void __launch_bounds__(ReadTcCfg<D>::kThreads, ReadTcCfg<D>::kMinBloc
   if (ntiles == 0) return;
   const int64_t slot = state_slot(p, n);
   if (slot < 0) return;
-  const bool tma_out = p.out_bf16 != 0;
+  const bool tma_out = Cfg::kTmaOut && p.out_bf16 != 0;
   auto tile_start = [&](int i) { return bos + strided_tile_index(i, kReadTcTiles) * Cfg::kTok; };
   auto full_tile = [&](int i) { return tile_start(i) + Cfg::kTok <= eos; };
 
-  // barriers: [0, NS) stage holds the query tile (TMA); [QF, QF + NA) accumulator full
+  // barriers: [0, NS) stage holds the query tile (TMA); [AF, AF + NA) accumulator full
   // (commit); [AE, AE + NA) accumulator drained; SR snapshot operand written; [OR, OR + NS)
-  // output tile written to the stage (AE.. and SR.. : one arrival per worker warp)
+  // output tile written to the stage (AE.. and SR.. : one arrival per worker warp) or, without
+  // TMA stores, the stage's MMA has completed (commit)
   constexpr int AF = NS, AE = NS + NA, SR = NS + 2 * NA, OR = SR + 1, NBAR = OR + NS;
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + Cfg::kOffBar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + Cfg::kOffBar + 8 * NBAR);
@@ -94,7 +100,7 @@ __global__ void __launch_bounds__(ReadTcCfg<D>::kThreads, ReadTcCfg<D>::kMinBloc
 
   if (tid == 0) {
     for (int i = 0; i < AE; ++i) mbar_init(B(i), 1);
-    for (int i = AE; i < NBAR; ++i) mbar_init(B(i), Cfg::kWorkerWarps);
+    for (int i = AE; i < NBAR; ++i) mbar_init(B(i), Cfg::kTmaOut || i <= SR ? Cfg::kWorkerWarps : 1);
     mbar_fence_init();
   }
   if (warp == Cfg::kWorkerWarps) tc::alloc(smem_u32(tmem_slot), Cfg::kTmemCols);
@@ -151,15 +157,26 @@ __global__ void __launch_bounds__(ReadTcCfg<D>::kThreads, ReadTcCfg<D>::kMinBloc
           tc::mma_bf16(tmem + D * a, tc::desc_kmajor(q + (ks >> 2) * Cfg::kBytesBox, (ks & 3) * 32),
                        tc::desc_mnmajor(ss, Cfg::kBytesPanelS, ks), kId, ks > 0);
         tc::commit(B(AF + a));
-        if (i >= 1) store_out(i - 1);
-        // refill the stage of tile i - R, whose output store was committed R - 1 groups ago
-        if (i >= R && i - R + NS < ntiles) {
-          asm volatile("cp.async.bulk.wait_group.read %0;\n" ::"n"(R - 1) : "memory");
-          load_q(i - R + NS);
+        if constexpr (Cfg::kTmaOut) {
+          if (i >= 1) store_out(i - 1);
+          // refill the stage of tile i - R, whose output store was committed R - 1 groups ago
+          if (i >= R && i - R + NS < ntiles) {
+            asm volatile("cp.async.bulk.wait_group.read %0;\n" ::"n"(R - 1) : "memory");
+            load_q(i - R + NS);
+          }
+        } else {
+          tc::commit(B(OR + s));
+          // the stage of tile i - 1 takes tile i - 1 + NS once MMA(i - 1) has read it
+          if (i >= 1 && i - 1 + NS < ntiles) {
+            wait(OR + (i - 1) % NS, ((i - 1) / NS) & 1);
+            load_q(i - 1 + NS);
+          }
         }
       }
-      store_out(ntiles - 1);
-      bulk_wait_all();
+      if constexpr (Cfg::kTmaOut) {
+        store_out(ntiles - 1);
+        bulk_wait_all();
+      }
     }
   } else {
     // snapshot -> bf16 MN-major operand [D key rows][NP panels of 64 values]: the worker threads
@@ -242,9 +259,11 @@ __global__ void __launch_bounds__(ReadTcCfg<D>::kThreads, ReadTcCfg<D>::kMinBloc
           }
         }
       }
-      if (staged) fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(B(OR + s));  // output tile i is in the stage (or stored)
+      if constexpr (Cfg::kTmaOut) {
+        if (staged) fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(B(OR + s));  // output tile i is in the stage (or stored)
+      }
     }
   }
   tc::fence_before();
