@@ -416,6 +416,28 @@ def test_read_d256_long_blocks_over_one_wave(cuda, lengths):
             assert O.rel_fro(out[lo:hi].float().cpu().numpy(), ref_o) <= TOL_BF16
 
 
+@pytest.mark.parametrize("D", [128, 256])
+def test_read_tile_kernel_fp32_output(cuda, D):
+    """bf16 queries read into an fp32 output on the tensor-core tile kernel: every row of the
+    ragged blocks (a full-tile block, one ending mid-tile, a 3-token block) equals the fp32
+    product q . bf16(S) times the scale (fp32 accumulation, so only summation order differs)."""
+    lengths = [1024, 645, 3]
+    H = 4
+    gen = torch.Generator(device=cuda).manual_seed(D)
+    L, N = sum(lengths), len(lengths)
+    q = (torch.randn(L, H, D, device=cuda, generator=gen) / D ** 0.5).to(torch.bfloat16)
+    S = 0.05 * torch.randn(N, H, D, D, device=cuda, generator=gen)
+    cu = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32)
+    scale = D ** -0.5
+    out = ops._read(q, S, torch.from_numpy(cu).to(cuda), N, max(lengths), scale, torch.float32)
+    torch.cuda.synchronize()
+    Sb = S.to(torch.bfloat16).float()
+    for n in range(N):
+        a, b = int(cu[n]), int(cu[n + 1])
+        ref = torch.einsum("thk,hkv->thv", q[a:b].float(), Sb[n]) * scale
+        assert O.rel_fro(out[a:b].cpu().numpy(), ref.cpu().numpy()) <= 1e-5, n
+
+
 @pytest.mark.parametrize("lengths", [[1, 2], [5, 40, 3]])
 def test_read_fp32_exact(cuda, lengths):
     rng = np.random.default_rng(3)
