@@ -40,25 +40,26 @@ static int launch_tile(const ReadParams& p, int64_t maxlen, cudaStream_t s) {
 }
 
 // d = 128 / 256, bf16 queries, plain read: tcgen05 kernel with TMA query tiles. A CTA reads
-// runs of 16 tiles of one block, converting the block's snapshot first. By default a block's
-// runs are spread over as many CTAs as it has runs: short CTAs balance over the SMs as they
-// free up. With WAVE (d = 256, whose 128 KB snapshot costs a CTA about as much as a few tiles),
+// runs of RUN tiles of one block (16, or 32 for a d = 128 read on its own), converting the
+// block's snapshot first. By default a block's runs are spread over as many CTAs as it has
+// runs: short CTAs balance over the SMs as they free up. With WAVE (d = 256, whose 128 KB snapshot costs a CTA about as much as a few tiles),
 // the runs are spread over one resident wave instead, at most 8 runs a CTA (long or ragged
 // blocks still spread over the SMs) — unless the read runs beside the commit's scan on the
 // caller's stream, where long CTAs could hold SMs the scan is waiting for. PDL: launched
 // after the scan on its stream (kReadAfterScan); the kernel never waits on it.
-template <int D>
+template <int D, int RUN>
 static int launch_read_tc(const ReadParams& p, int64_t maxlen, bool wave, bool pdl, cudaStream_t s) {
   using Cfg = ReadTcCfg<D>;
+  auto kernel = read_tc_kernel<D, RUN>;
   ReadTcParams P;
   P.p = p;
   const uint64_t row = static_cast<uint64_t>(p.H) * D;
   cudaError_t e = make_tmap_bf16_2d(&P.q_map, p.q, row, static_cast<uint64_t>(p.L), row * 2, 64, Cfg::kTok);
   if (e == cudaSuccess && p.out_bf16 && Cfg::kTmaOut)
     e = make_tmap_bf16_2d(&P.o_map, p.out, row, static_cast<uint64_t>(p.L), row * 2, 64, Cfg::kTok);
-  if (e == cudaSuccess) e = ensure_smem(read_tc_kernel<D>, Cfg::kSmem);
+  if (e == cudaSuccess) e = ensure_smem(kernel, Cfg::kSmem);
   if (e != cudaSuccess) return cuda_status(e);
-  const int64_t per = int64_t(kReadTcTiles) * Cfg::kTok;
+  const int64_t per = int64_t(RUN) * Cfg::kTok;
   int64_t groups = (maxlen + per - 1) / per;
   if (groups < 1) groups = 1;
   const int64_t blocks = int64_t(p.num_blocks) * p.H;
@@ -66,7 +67,7 @@ static int launch_read_tc(const ReadParams& p, int64_t maxlen, bool wave, bool p
   if (wave) {
     constexpr int64_t kMaxRuns = 8;
     int slots = 0;
-    e = resident_slots(read_tc_kernel<D>, Cfg::kThreads, Cfg::kSmem, &slots);
+    e = resident_slots(kernel, Cfg::kThreads, Cfg::kSmem, &slots);
     if (e != cudaSuccess) return cuda_status(e);
     gy = slots / blocks;
     const int64_t gy_min = (groups + kMaxRuns - 1) / kMaxRuns;
@@ -77,8 +78,8 @@ static int launch_read_tc(const ReadParams& p, int64_t maxlen, bool wave, bool p
   if (gy > 65535) return MEMT_ERR_UNSUPPORTED;
   dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(gy));
   ProfScope prof(kProfReadTile, s);
-  if (pdl) return cuda_status(launch_pdl(read_tc_kernel<D>, grid, dim3(Cfg::kThreads), Cfg::kSmem, s, P));
-  read_tc_kernel<D><<<grid, Cfg::kThreads, Cfg::kSmem, s>>>(P);
+  if (pdl) return cuda_status(launch_pdl(kernel, grid, dim3(Cfg::kThreads), Cfg::kSmem, s, P));
+  kernel<<<grid, Cfg::kThreads, Cfg::kSmem, s>>>(P);
   return cuda_status(cudaGetLastError());
 }
 
@@ -89,8 +90,11 @@ bool read_uses_tc(const ReadParams& p, int D, bool exact, int64_t maxlen) {
 int launch_read(const ReadParams& p, int D, bool exact, int64_t maxlen, cudaStream_t s, int placement) {
   if (read_uses_tc(p, D, exact, maxlen)) {
     const bool pdl = placement == kReadAfterScan;
-    if (D == 128) return launch_read_tc<128>(p, maxlen, false, pdl, s);
-    return launch_read_tc<256>(p, maxlen, placement != kReadBeside, pdl, s);
+    if (D == 128) {
+      if (placement == kReadAlone) return launch_read_tc<128, kReadTcTilesAlone>(p, maxlen, false, false, s);
+      return launch_read_tc<128, kReadTcTiles>(p, maxlen, false, pdl, s);
+    }
+    return launch_read_tc<256, kReadTcTiles>(p, maxlen, placement != kReadBeside, pdl, s);
   }
   if (exact || maxlen <= kGemvMaxBlock) {
     switch (D) {

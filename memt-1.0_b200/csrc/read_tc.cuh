@@ -1,7 +1,7 @@
 // Snapshot read o = scale * q . bf16(S) on tcgen05 tensor cores for d = 128 and 256 and blocks of
 // many tokens (the commit read of token_memory_packed, models/qwen/ops/read.py:42-89 and
-// models/deepseek/ops/read.py:6-31): one CTA per (block, head, run of up to kReadTcTiles
-// 128-token tiles).
+// models/deepseek/ops/read.py:6-31): one CTA per (block, head, run of up to RUN 64-token
+// tiles).
 //
 //   * the block's fp32 snapshot is read once, rounded to bf16 (read.py:64) and written as the
 //     MN-major B operand [D key rows][D/64 panels of 64 values] in shared memory (32 KB for
@@ -31,7 +31,11 @@
 
 namespace memt {
 
-constexpr int kReadTcTiles = 16;  // 64-token tiles per CTA
+// 64-token tiles per run: 16 where the read shares the GPU with the commit's scan (short CTAs
+// take the SMs as the scan frees them), 32 for a d = 128 read on its own (half the snapshot
+// conversions: config-1 read 0.145 -> 0.131 ms)
+constexpr int kReadTcTiles = 16;
+constexpr int kReadTcTilesAlone = 32;
 
 struct ReadTcParams {
   CUtensorMap q_map;  // bf16 [L, H*D], boxes of 64 keys x 64 tokens
@@ -64,7 +68,8 @@ struct ReadTcCfg {
   static_assert(kSmem <= 227 * 1024 && kTmemCols <= 512, "one CTA's resources");
 };
 
-template <int D>
+// RUN: 64-token tiles per run, a compile-time constant (the tile index arithmetic divides by it)
+template <int D, int RUN>
 __global__ void __launch_bounds__(ReadTcCfg<D>::kThreads, ReadTcCfg<D>::kMinBlocks)
     read_tc_kernel(const __grid_constant__ ReadTcParams P) {
   using Cfg = ReadTcCfg<D>;
@@ -77,14 +82,14 @@ __global__ void __launch_bounds__(ReadTcCfg<D>::kThreads, ReadTcCfg<D>::kMinBloc
   const int n = blockIdx.x / p.H, h = blockIdx.x % p.H;
   int64_t bos, eos;
   block_range(p, n, bos, eos);
-  // this CTA's tiles: runs y, y + gridDim.y, ... of kReadTcTiles tiles, so that every token is
+  // this CTA's tiles: runs y, y + gridDim.y, ... of RUN tiles, so that every token is
   // read whatever bound on the block length the host sized the grid with
-  const int ntiles = strided_tiles(eos - bos, Cfg::kTok, kReadTcTiles);
+  const int ntiles = strided_tiles(eos - bos, Cfg::kTok, RUN);
   if (ntiles == 0) return;
   const int64_t slot = state_slot(p, n);
   if (slot < 0) return;
   const bool tma_out = Cfg::kTmaOut && p.out_bf16 != 0;
-  auto tile_start = [&](int i) { return bos + strided_tile_index(i, kReadTcTiles) * Cfg::kTok; };
+  auto tile_start = [&](int i) { return bos + strided_tile_index(i, RUN) * Cfg::kTok; };
   auto full_tile = [&](int i) { return tile_start(i) + Cfg::kTok <= eos; };
 
   // barriers: [0, NS) stage holds the query tile (TMA); [AF, AF + NA) accumulator full
