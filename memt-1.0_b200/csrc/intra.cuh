@@ -40,6 +40,8 @@
 //     by pair, exactly as the reference's token-parallel kernel does.
 #pragma once
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "tma.h"
 
@@ -1030,20 +1032,30 @@ struct IntraKernel {
     row_stride = (int64_t)p.H * D;
     __nv_bfloat16* kcur = sK;
 
-    auto load_decay = [&](int c0) {
-      const float* base = p.g + (int64_t)tok0 * row_stride + (int64_t)h * D + c0;
+    // the decay panel of unit (tk0, ln, hd) by threads [T0, T0 + NTH)
+    auto load_decay_for = [&](auto t0_tag, auto nth_tag, int c0, int tk0, int ln, int hd) {
+      constexpr int T0 = decltype(t0_tag)::value, NTH = decltype(nth_tag)::value;
+      const float* base = p.g + (int64_t)tk0 * row_stride + (int64_t)hd * D + c0;
       constexpr int kChunks = kTile * P / 4;
 #pragma unroll
-      for (int i = tid; i < kChunks; i += NT) {
+      for (int i = tid - T0; i < kChunks; i += NTH) {
         const int row = i / (P / 4), col = (i % (P / 4)) * 4;
-        const bool valid = row < len;
+        const bool valid = row < ln;
         cp_async16_zfill(sE + eidx(row, col), valid ? base + (int64_t)row * row_stride + col : p.g, valid);
       }
     };
-    auto load_key_panel = [&](int c0) {
+    auto load_decay = [&](int c0) {
+      load_decay_for(std::integral_constant<int, 0>{}, std::integral_constant<int, NT>{}, c0, tok0, len, h);
+    };
+    // per channel with the solve / staging split, the staging warps load the next unit's decay
+    // table as soon as their staging is done (the table is free then), a whole WY phase before
+    // the unit starts; the key tile follows at the unit's end as before
+    constexpr bool kEarlyDecay = kOverlap && !HEAD;
+    auto load_key_panel = [&](int c0, bool decay) {
       load_tile(kcur, p.k, c0, p.sk);
       if constexpr (ERASE) load_tile(sB, p.erase, c0, row_stride);
-      if constexpr (!HEAD) load_decay(c0);
+      if constexpr (!HEAD)
+        if (decay) load_decay(c0);
     };
     auto load_value_panel = [&](int c0) {
       load_tile(sV, p.v, c0, p.sv);
@@ -1069,7 +1081,7 @@ struct IntraKernel {
     constexpr bool kNextFactors = kOverlap && HEAD;
     bool first = true;
     set_unit(p, unit);
-    load_key_panel(0);
+    load_key_panel(0, true);
     cp_async_commit();
     pre = 0;
     fetch_scalars(p, tok0, len, h, sPre, 0);
@@ -1103,7 +1115,7 @@ struct IntraKernel {
       for (int pn = 0; pn < Cfg::kPanels; ++pn) {
         if (pn > 0) {
           __syncthreads();
-          load_key_panel(pn * P);
+          load_key_panel(pn * P, true);
           cp_async_commit();
           cp_async_wait<0>();
         } else {
@@ -1148,6 +1160,16 @@ struct IntraKernel {
             if (has_next && warp == 7) {
               const ChunkDesc d2 = p.table[static_cast<int>(next / p.H)];
               head_factors(sPre + (pre ^ 1) * 2 * kTile, sFac + (pre ^ 1) * Cfg::kSmall, d2.len);
+            }
+          }
+          if constexpr (kEarlyDecay) {
+            if (has_next) {
+              named_sync(2, 128);  // every staging thread is done with this unit's table
+              const int c2 = static_cast<int>(next / p.H), h2 = static_cast<int>(next % p.H);
+              const ChunkDesc d2 = p.table[c2];
+              load_decay_for(std::integral_constant<int, 128>{}, std::integral_constant<int, 128>{}, 0, d2.tok0,
+                             d2.len, h2);
+              cp_async_commit();
             }
           }
 
@@ -1212,7 +1234,7 @@ struct IntraKernel {
       __syncthreads();  // the last tile stores read shared memory the next unit overwrites
       if constexpr (!kOverlap) fetch_scalars(p, tok0, len, h, sPre + (pre ^ 1) * 2 * kTile, 0);
       pre ^= 1;
-      load_key_panel(0);
+      load_key_panel(0, !kEarlyDecay);
       cp_async_commit();
     }
   }
