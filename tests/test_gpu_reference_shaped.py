@@ -157,6 +157,36 @@ def test_config1_qwen_commit_channel_decay(cuda):
     assert O.rel_fro(_np(read[0, s * 8192:(s + 1) * 8192, h:h + 1]), o_ref) <= TOL_BF16
 
 
+@pytest.mark.parametrize("D", [64, 128])
+def test_channel_decay_with_many_units_per_cta(cuda, D):
+    """Channel-wise decay without erase, ragged sessions and enough (chunk, head) units that
+    every CTA of the persistent intra grid walks several of them (each unit's decay table is
+    loaded while the previous unit finishes). Three (session, head) slices against the oracle,
+    and one session run alone reproduces its pack result bit for bit."""
+    lengths, H = [2000, 1500, 3000, 64, 1, 900], 16
+    L = sum(lengths)
+    x = _latents(cuda, L, H, D, 31 + D)
+    q_hat, k_s, w, g = M.qwen_prologue(x.q, x.k, x.erase_gate, x.write_gate, x.decay, x.bias, x.scale_log)
+    gen = torch.Generator(device=cuda).manual_seed(32)
+    N = len(lengths)
+    h0 = 0.02 * torch.randn(N, H, D, D, device=cuda, generator=gen)
+    args = dict(scale=D ** -0.5, chunk_tokens=2048)
+    _, final = M.token_memory_packed(q_hat, k_s, x.v[None], g, w, h0, h0, erase=None, lengths=lengths, **args)
+    cu = np.concatenate([[0], np.cumsum(lengths)])
+    n = 2
+    sl = slice(int(cu[n]), int(cu[n + 1]))
+    _, one = M.token_memory_packed(q_hat[:, sl], k_s[:, sl], x.v[None, sl], g[:, sl], w[:, sl],
+                                   h0[n:n + 1].contiguous(), h0[n:n + 1].contiguous(), erase=None,
+                                   lengths=[lengths[n]], **args)
+    torch.cuda.synchronize()
+    assert torch.isfinite(final).all()
+    assert torch.equal(final[n], one[0])
+    for s_, h in ((0, 3), (2, 15), (5, 0)):
+        ref = _oracle_state(k_s[0], x.v, g[0], w[0], h0, int(cu[s_]), int(cu[s_ + 1]), s_, h)
+        err = O.rel_fro(_np(final[s_, h:h + 1])[None], ref)
+        assert err <= TOL_BF16, (s_, h, err)
+
+
 def test_config4_flash_full_length(cuda):
     """BASELINE config 4 at its real length: 4 sessions x 16384 tokens, d = 256, the 16 heads
     one of eight tensor-parallel ranks owns (128 heads / TP8), channel-wise decay, write gate,
